@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Benchmark: QPS at recall@10 = 0.95 on the C2 workload (1M x 128 IVF-PQ,
+nlist 4096, PQ 64x8, k=100, exact rerank of the top 1000), nprobe swept over
+{8,16,32,64,128} and QPS interpolated at the recall target.
+
+A step is one search of the whole 10,000-query batch at one nprobe.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fusiongpu|reference]
+
+Under torchrun every rank holds a full replica of the index and searches its
+own copy of the batch (replicas; per-GPU work is fixed, scaling "weak").
+`--impl reference` times the CPU restatement of the reference's search (the
+oracle) on the host cores instead; only rank 0 works.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+RECALL_TARGET = 0.95
+SWEEP = (8, 16, 32, 64, 128)
+CONFIG = dict(workload="C2: 1,000,000 x 128 fp32 integer-valued Gaussian mixture (4096 centres, sigma 10), "
+                       "10,000 queries, L2",
+              nlist=4096, pq_m=64, k=100, rerank_m=1000, p1_lists=12, limit_k=50, threshold_coeff=1.0,
+              mini_batch=128, epsilon=0.1, beta=2, nprobe_sweep=list(SWEEP), recall="recall@10",
+              mode="intended (full rerank_m gather, k+mini_batch rerank window)")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fusiongpu", choices=["fusiongpu", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=400, help="queries in the CPU-baseline sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--quick", action="store_true", help="small workload (development only)")
+    return ap.parse_args()
+
+
+def interp_at_recall(points, target=RECALL_TARGET):
+    """points: [(nprobe, recall, qps)] in nprobe order.  QPS at `target` by
+    linear interpolation in recall between the bracketing sweep points."""
+    pts = sorted(points, key=lambda p: p[0])
+    if pts[0][1] >= target:
+        return pts[0][2], True
+    for a, b in zip(pts, pts[1:]):
+        if a[1] < target <= b[1]:
+            t = (target - a[1]) / (b[1] - a[1])
+            return a[2] + t * (b[2] - a[2]), True
+    best = max(pts, key=lambda p: p[1])
+    return best[2], False
+
+
+def search_params(nprobe, SearchParams):
+    return SearchParams(top_m=nprobe, p1_lists=CONFIG["p1_lists"], limit_k=CONFIG["limit_k"],
+                        threshold_coeff=CONFIG["threshold_coeff"], prune_ratio=100.0,
+                        rerank_m=CONFIG["rerank_m"], final_k=CONFIG["k"], mini_batch=CONFIG["mini_batch"],
+                        epsilon=CONFIG["epsilon"], beta=CONFIG["beta"], ref_compat=False)
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def workload(quick: bool):
+    from fusiongpu_b200 import datasets as ds
+    if quick:
+        return ds.scaled(ds.C2, 200_000, 2_000, n_centres=1024), 1024
+    return ds.C2, CONFIG["nlist"]
+
+
+def setup(device, quick):
+    """Data, GPU-built index and exact ground truth (untimed)."""
+    import torch
+    from fusiongpu_b200 import datasets as ds
+    from fusiongpu_b200.index import IVFPQIndex, knn_exact
+    spec, nlist = workload(quick)
+    t0 = time.time()
+    base, queries = ds.generate(spec)
+    xb = torch.from_numpy(base).to(device)
+    idx = IVFPQIndex.build(xb, nlist, CONFIG["pq_m"], kmeans_iters=20, pq_sample=50000, pq_iters=8, device=device)
+    gt, _ = knn_exact(xb, torch.from_numpy(queries).to(device), 10, device=device)
+    torch.cuda.synchronize(device)
+    return dict(spec=spec, base=base, queries=queries, index=idx, gt=gt.cpu().numpy(), setup_s=time.time() - t0)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return main_reference(args)
+    import torch
+    import torch.distributed as dist
+    from fusiongpu_b200.index import SearchParams, recall_at
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    W = setup(device, args.quick)
+    idx, queries, gt = W["index"], W["queries"], W["gt"]
+    nq = queries.shape[0]
+    qd = torch.from_numpy(queries).to(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > 126 MB L2
+    stream = torch.cuda.current_stream(device)
+    sweep = []
+    launches_per_step = 4 if idx.nlist <= 8192 else 5  # coarse tile + top-k (+stage 2) + scan + rerank
+    clocks = ClockSampler(local)
+    with clocks:
+        for nprobe in SWEEP:
+            p = search_params(nprobe, SearchParams)
+            ids = torch.empty((nq, p.final_k), dtype=torch.int32, device=device)
+            dd = torch.empty((nq, p.final_k), dtype=torch.float32, device=device)
+            for _ in range(args.warmup):
+                idx.search(qd, p, out=(ids, dd))
+            torch.cuda.synchronize(device)
+            rec = recall_at(ids[:, :10].cpu().numpy(), gt[:, :10], 10)
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+            barrier()
+            torch.cuda.synchronize(device)
+            for e0, e1 in ev:
+                flush.zero_()  # L2 flush between steps, outside the timed region
+                e0.record(stream)
+                idx.search(qd, p, out=(ids, dd))
+                e1.record(stream)
+            torch.cuda.synchronize(device)
+            barrier()
+            ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
+            ms = max_over_ranks(ms)
+            sweep.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=world * nq / (ms / 1e3)))
+
+    pts = [(s["nprobe"], s["recall"], s["qps"]) for s in sweep]
+    value, met = interp_at_recall(pts)
+    op = next((s for s in sweep if s["recall"] >= RECALL_TARGET), max(sweep, key=lambda s: s["recall"]))
+
+    # ---- end to end through the public API: pinned host queries in, host results out
+    e2e_pts = []
+    hq = torch.from_numpy(queries).pin_memory()
+    for s in sweep:
+        p = search_params(s["nprobe"], SearchParams)
+        hid = torch.empty((nq, p.final_k), dtype=torch.int32).pin_memory()
+        hdd = torch.empty((nq, p.final_k), dtype=torch.float32).pin_memory()
+        ids = torch.empty((nq, p.final_k), dtype=torch.int32, device=device)
+        dd = torch.empty((nq, p.final_k), dtype=torch.float32, device=device)
+        qdev = torch.empty_like(qd)
+
+        def one():
+            qdev.copy_(hq, non_blocking=True)
+            idx.search(qdev, p, out=(ids, dd))
+            hid.copy_(ids, non_blocking=True)
+            hdd.copy_(dd, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            one()
+        torch.cuda.synchronize(device)
+        barrier()
+        tot = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            one()
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        barrier()
+        ms = max_over_ranks(tot / args.steps)
+        e2e_pts.append((s["nprobe"], s["recall"], world * nq / (ms / 1e3)))
+        s["e2e_ms_per_step"] = ms
+    e2e_value, _ = interp_at_recall(e2e_pts)
+
+    # ---- roofline of the dominant kernel (ADC scan = candidate generation) at the operating point
+    roof = roofline(idx, qd, op["nprobe"], args, device, SearchParams, flush)
+
+    out = {
+        "metric": "QPS at recall@10=0.95 (C2 1M x 128 IVF-PQ)",
+        "value": value,
+        "unit": "queries/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": op["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture standing in for a dataset; index built on the GPU)",
+        "config": dict(CONFIG, parallelism=f"replicas x{world} (full index per GPU, own 10k-query batch)",
+                       l2="flushed (256 MB write) between timed steps",
+                       recall_target_met=met, operating_nprobe=op["nprobe"],
+                       quick=bool(args.quick)),
+        "sweep": sweep,
+        "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
+        "gpu_launches": launches_per_step * args.steps * len(SWEEP),
+        "gpu_launches_per_step": launches_per_step,
+        "roofline": roof,
+        "clocks": clocks.summary(),
+        "setup_s": W["setup_s"],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(W, op["nprobe"], args.cpu_sample)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def roofline(idx, qd, nprobe, args, device, SearchParams, flush):
+    """Algorithmic bytes of the scan kernel per launch (code bytes of every
+    probed list + 4 bytes per emitted candidate) over its CUDA-event time."""
+    import torch
+    from fusiongpu_b200.index import run_gpu_batch_logic
+    p = search_params(nprobe, SearchParams)
+    pid, pd = idx.coarse(qd, nprobe)
+    lens = (idx.offsets[1:] - idx.offsets[:-1]).to(torch.int64)
+    code_bytes = int(lens[pid.long()].sum().item()) * idx.pq_m
+    for _ in range(args.warmup):
+        ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pd, p)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    tot = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pd, p)
+        e1.record(stream)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    ms = tot / args.steps
+    cand_bytes = 4 * int(cc.to(torch.int64).sum().item())
+    alg = code_bytes + cand_bytes
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = alg / (ms / 1e3) / 1e9
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "scan_traffic.json")))
+        if tr.get("nprobe") == nprobe and tr.get("workload") == "C2":
+            traffic = tr["dram_bytes_per_launch"]
+    except Exception:
+        pass
+    return {"kernel": "ivfpq_batch_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+            "traffic": traffic, "algorithmic_bytes": alg, "ms_per_launch": ms, "nprobe": nprobe}
+
+
+def cpu_baseline(W, nprobe, sample):
+    """The oracle (C restatement of the reference search, OpenMP over all
+    host cores) on the first `sample` queries at the operating nprobe."""
+    import oracle
+    from fusiongpu_b200.index import SearchParams
+    p = search_params(nprobe, SearchParams)
+    index = W["index"].to_numpy()
+    q = np.ascontiguousarray(W["queries"][:sample])
+    kw = dict(top_m=p.top_m, p1_lists=p.p1_lists, limit_k=p.limit_k, threshold_coeff=p.threshold_coeff,
+              prune_ratio=p.prune_ratio, rerank_m=p.rerank_m, final_k=p.final_k, mini_batch=p.mini_batch,
+              epsilon=p.epsilon, beta=p.beta, ref_compat=False)
+    cores = os.cpu_count() or 1
+    oracle.search(index, W["base"], q[:8], nthreads=cores, **kw)  # warm caches
+    t0 = time.perf_counter()
+    oracle.search(index, W["base"], q, nthreads=cores, **kw)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"first {sample} of {W['queries'].shape[0]} queries at nprobe={nprobe}, same index",
+            "seconds": dt}
+
+
+def main_reference(args):
+    """CPU arm: the oracle restating the reference's search on the host cores,
+    same workload, metric and sweep; each step is a bounded query sample."""
+    import torch
+    from fusiongpu_b200.index import SearchParams, recall_at
+    import oracle
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    W = setup(device, args.quick)  # index built once (untimed setup) so both arms search the same index
+    index = W["index"].to_numpy()
+    base, queries, gt = W["base"], W["queries"], W["gt"]
+    cores = os.cpu_count() or 1
+    sample = 128
+    pts, sweep = [], []
+    for nprobe in SWEEP:
+        p = search_params(nprobe, SearchParams)
+        kw = dict(top_m=p.top_m, p1_lists=p.p1_lists, limit_k=p.limit_k, threshold_coeff=p.threshold_coeff,
+                  prune_ratio=p.prune_ratio, rerank_m=p.rerank_m, final_k=p.final_k, mini_batch=p.mini_batch,
+                  epsilon=p.epsilon, beta=p.beta, ref_compat=False)
+        rq = np.ascontiguousarray(queries[:1000])
+        ids, _ = oracle.search(index, base, rq, nthreads=cores, **kw)
+        rec = recall_at(ids[:, :10], gt[:1000, :10], 10)
+        for s in range(args.warmup):
+            oracle.search(index, base, np.ascontiguousarray(queries[:sample]), nthreads=cores, **kw)
+        tot = 0.0
+        for s in range(args.steps):
+            qs = np.ascontiguousarray(queries[(s * sample) % 9000:(s * sample) % 9000 + sample])
+            t0 = time.perf_counter()
+            oracle.search(index, base, qs, nthreads=cores, **kw)
+            tot += time.perf_counter() - t0
+        ms = tot / args.steps * 1e3
+        sweep.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=sample / (ms / 1e3)))
+        pts.append((nprobe, rec, sample / (ms / 1e3)))
+    value, met = interp_at_recall(pts)
+    op = next((s for s in sweep if s["recall"] >= RECALL_TARGET), max(sweep, key=lambda s: s["recall"]))
+    out = {
+        "impl": "reference",
+        "metric": "QPS at recall@10=0.95 (C2 1M x 128 IVF-PQ)",
+        "value": value,
+        "unit": "queries/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": op["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture standing in for a dataset)",
+        "config": dict(CONFIG, recall_target_met=met, operating_nprobe=op["nprobe"], quick=bool(args.quick),
+                       parallelism="host CPU (OpenMP)"),
+        "sweep": sweep,
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} queries per step (recall from the first 1000); the reference "
+                                   "ships no CPU search, so its C restatement (oracle/) runs"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,292 @@
+// coarse.cu -- exact squared-L2 tiles and per-row top-k selection.
+//
+// Used by the coarse quantizer (replaces cuVS CAGRA search over centroids,
+// cagra_adapter.cuh:38-68), by k-means assignment (replaces the SGEMM +
+// argmin of kmeans_gpu.cuh:197-229) and by exact k-NN ground truth.
+//
+// Distances are sum_j fmaf(x_j - y_j, x_j - y_j, acc) in dimension order, the
+// same arithmetic the oracle uses, so rankings match it exactly (ties broken
+// by the lower column index).
+#include <algorithm>
+
+#include "fg_common.cuh"
+
+namespace fg {
+
+__host__ __device__ inline int round_up_dev(int x) { return (x + 15) / 16 * 16; }
+
+constexpr int L2_T = 64;       // rows of X and of Y per tile
+constexpr int L2_DC = 32;      // dimensions per shared-memory chunk
+constexpr int L2_LD = L2_T + 4;
+constexpr int L2_NT = 256;
+
+enum { EPI_MATRIX = 0, EPI_ARGMIN = 1 };
+
+// Each CTA owns 64 rows of X; blockIdx.y picks a run of `ytiles` 64-row tiles
+// of Y.  EPI_MATRIX writes D[x][y] (row stride ldd); EPI_ARGMIN keeps the
+// nearest y per x row (grid.y must be 1) and writes amin[x].
+template <int EPI>
+__global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict__ X, long long nx,
+                                                        const float* __restrict__ Y, int ny, int dim,
+                                                        float* __restrict__ D, long long ldd,
+                                                        int32_t* __restrict__ amin, int ytiles) {
+    __shared__ __align__(16) float sX[L2_DC][L2_LD];
+    __shared__ __align__(16) float sY[L2_DC][L2_LD];
+    __shared__ float rd[L2_T][17];
+    __shared__ int ri[L2_T][17];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const long long x0 = (long long)blockIdx.x * L2_T;
+    const int nyt = (ny + L2_T - 1) / L2_T;
+    const int yt0 = blockIdx.y * ytiles;
+    const int yt1 = min(nyt, yt0 + ytiles);
+    float best[4];
+    int bidx[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        best[a] = FLT_MAX;
+        bidx[a] = 0x7fffffff;
+    }
+    for (int yt = yt0; yt < yt1; ++yt) {
+        const int y0 = yt * L2_T;
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+        for (int d0 = 0; d0 < dim; d0 += L2_DC) {
+            // 64 rows x 32 dims of each operand, transposed into shared memory
+            for (int f = tid; f < L2_T * L2_DC; f += L2_NT) {
+                const int r = f / L2_DC, c = f % L2_DC;
+                const int dj = d0 + c;
+                const long long xr = x0 + r;
+                const int yr = y0 + r;
+                sX[c][r] = (xr < nx && dj < dim) ? X[xr * dim + dj] : 0.0f;
+                sY[c][r] = (yr < ny && dj < dim) ? Y[(long long)yr * dim + dj] : 0.0f;
+            }
+            __syncthreads();
+            const int dn = min(L2_DC, dim - d0);
+            for (int j = 0; j < dn; ++j) {
+                const float4 xv = *reinterpret_cast<const float4*>(&sX[j][tx * 4]);
+                const float4 yv = *reinterpret_cast<const float4*>(&sY[j][ty * 4]);
+                const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+                const float yb[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const float df = xa[a] - yb[b];
+                        acc[a][b] = fmaf(df, df, acc[a][b]);
+                    }
+            }
+            __syncthreads();
+        }
+        if (EPI == EPI_MATRIX) {
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const long long xr = x0 + tx * 4 + a;
+                if (xr >= nx) continue;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int yr = y0 + ty * 4 + b;
+                    if (yr < ny) D[xr * ldd + yr] = acc[a][b];
+                }
+            }
+        } else {
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int yr = y0 + ty * 4 + b;
+                    if (yr < ny && acc[a][b] < best[a]) {
+                        best[a] = acc[a][b];
+                        bidx[a] = yr;
+                    }
+                }
+        }
+    }
+    if (EPI == EPI_ARGMIN) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            rd[tx * 4 + a][ty] = best[a];
+            ri[tx * 4 + a][ty] = bidx[a];
+        }
+        __syncthreads();
+        if (tid < L2_T) {
+            float bd = rd[tid][0];
+            int bi = ri[tid][0];
+            for (int t = 1; t < 16; ++t) {
+                const float d = rd[tid][t];
+                const int i = ri[tid][t];
+                if (d < bd || (d == bd && i < bi)) {
+                    bd = d;
+                    bi = i;
+                }
+            }
+            const long long xr = x0 + tid;
+            if (xr < nx) amin[xr] = (bi == 0x7fffffff) ? 0 : bi;
+        }
+    }
+}
+
+constexpr int TK_NT = 512;
+constexpr int TK_SEG = 8192;  // columns per stage-1 segment (32 KB of keys)
+
+// Top-k (ascending by value, ties by column/position) of one segment of one
+// row.  Input value v[row][c0 + i] with row stride ldv; optional payload
+// pay[row][c0 + i] (default: the column index).  Writes kk = min(k, len)
+// sorted (index, value) pairs at out_i/out_v + row*out_ld + seg*k, padding
+// up to k with (-1, FLT_MAX).
+__global__ void __launch_bounds__(TK_NT) topk_segment_kernel(const float* __restrict__ v, long long ldv,
+                                                             int ncols, int seg_len,
+                                                             const int32_t* __restrict__ pay, int k,
+                                                             int32_t* __restrict__ out_i,
+                                                             float* __restrict__ out_v, long long out_ld) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sb[2];
+    __shared__ int warp[TK_NT / 32];
+    const long long row = blockIdx.x;
+    const int seg = blockIdx.y;
+    const int c0 = seg * seg_len;
+    const int len = min(seg_len, ncols - c0);
+    const int kk = min(k, len);
+    const int kpow = next_pow2(kk);
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+    unsigned long long* sortb = reinterpret_cast<unsigned long long*>(smem + round_up_dev(seg_len * 4));
+    const float* vr = v + row * ldv + c0;
+    for (int i = threadIdx.x; i < len; i += TK_NT) keys[i] = f2key(vr[i]);
+    __syncthreads();
+    uint32_t kth;
+    int n_less;
+    block_radix_select<TK_NT>(keys, len, kk, hist, sb, kth, n_less);
+    const int need_eq = kk - n_less;
+    int eq_base = 0, out_base = 0;
+    for (int r0 = 0; r0 < len; r0 += TK_NT) {
+        const int i = r0 + threadIdx.x;
+        const bool in = i < len;
+        const uint32_t key = in ? keys[i] : 0xffffffffu;
+        const int is_eq = (in && key == kth) ? 1 : 0;
+        int eq_tot, s_tot;
+        const int eq_pre = block_exclusive_scan<TK_NT>(is_eq, warp, eq_tot);
+        const bool sel = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
+        eq_base += eq_tot;
+        const int s_pre = block_exclusive_scan<TK_NT>(sel ? 1 : 0, warp, s_tot);
+        if (sel) sortb[out_base + s_pre] = ((unsigned long long)key << 32) | (unsigned)i;
+        out_base += s_tot;
+    }
+    for (int i = kk + threadIdx.x; i < kpow; i += TK_NT) sortb[i] = ~0ull;
+    __syncthreads();
+    block_bitonic_sort<TK_NT>(sortb, kpow);
+    const long long ob = row * out_ld + (long long)seg * k;
+    for (int r = threadIdx.x; r < k; r += TK_NT) {
+        if (r < kk) {
+            const unsigned long long e = sortb[r];
+            const int li = (int)(e & 0xffffffffu);
+            out_i[ob + r] = pay ? pay[row * ldv + c0 + li] : c0 + li;
+            out_v[ob + r] = key2f((uint32_t)(e >> 32));
+        } else {
+            out_i[ob + r] = -1;
+            out_v[ob + r] = FLT_MAX;
+        }
+    }
+}
+
+// Per-row top-k of a [rows][ncols] matrix with row stride ldv.  When ncols
+// exceeds one segment, stage 1 writes the per-segment winners to `stage`
+// ([rows][nseg*k] values + ids) and stage 2 selects from those.
+int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, int32_t* out_i,
+              float* out_v, long long out_ld, float* stage_v, int32_t* stage_i, cudaStream_t s) {
+    if (rows <= 0) return FG_OK;
+    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const int seg_len = nseg == 1 ? ncols : TK_SEG;
+    auto smem_for = [&](int len, int kk) { return round_up_dev(len * 4) + next_pow2(kk) * 8; };
+    if (nseg == 1) {
+        const int sm = smem_for(seg_len, k);
+        FG_CUDA_TRY(cudaFuncSetAttribute(topk_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+        topk_segment_kernel<<<dim3((unsigned)rows, 1), TK_NT, sm, s>>>(v, ldv, ncols, seg_len, nullptr, k,
+                                                                      out_i, out_v, out_ld);
+        return check_launch("topk_segment_kernel");
+    }
+    const long long sld = (long long)nseg * k;
+    int sm = smem_for(seg_len, k);
+    FG_CUDA_TRY(cudaFuncSetAttribute(topk_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     std::max(sm, smem_for((int)sld, k))));
+    topk_segment_kernel<<<dim3((unsigned)rows, nseg), TK_NT, sm, s>>>(v, ldv, ncols, seg_len, nullptr, k,
+                                                                     stage_i, stage_v, sld);
+    int rc = check_launch("topk_segment_kernel(stage 1)");
+    if (rc) return rc;
+    if (sld > TK_SEG * 4) return fail(FG_ERR_UNSUPPORTED, "top-k stage 2 of %lld candidates", sld);
+    sm = smem_for((int)sld, k);
+    topk_segment_kernel<<<dim3((unsigned)rows, 1), TK_NT, sm, s>>>(stage_v, sld, (int)sld, (int)sld, stage_i,
+                                                                   k, out_i, out_v, out_ld);
+    return check_launch("topk_segment_kernel(stage 2)");
+}
+
+size_t rows_topk_stage_bytes(long long rows, int ncols, int k) {
+    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    if (nseg == 1) return 0;
+    return round_up((size_t)rows * nseg * k * 4, 256) * 2;
+}
+
+int l2_matrix(const float* X, long long nx, const float* Y, int ny, int dim, float* D, long long ldd,
+              cudaStream_t s) {
+    if (nx <= 0 || ny <= 0) return FG_OK;
+    const int nyt = (ny + L2_T - 1) / L2_T;
+    dim3 grid((unsigned)((nx + L2_T - 1) / L2_T), nyt);
+    l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
+    return check_launch("l2_tile_kernel(matrix)");
+}
+
+int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int32_t* amin,
+              cudaStream_t s) {
+    if (nx <= 0) return FG_OK;
+    const int nyt = (ny + L2_T - 1) / L2_T;
+    dim3 grid((unsigned)((nx + L2_T - 1) / L2_T), 1);
+    l2_tile_kernel<EPI_ARGMIN><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, nullptr, 0, amin, nyt);
+    return check_launch("l2_tile_kernel(argmin)");
+}
+
+// ---- coarse search and exact k-NN (row chunks through a workspace matrix) ----
+
+static long long chunk_rows(size_t ws_bytes, long long nrows, int ncols, int k) {
+    // matrix [r][ncols] + stage buffers [r][nseg*k] x2
+    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const size_t per_row = (size_t)ncols * 4 + (nseg > 1 ? (size_t)nseg * k * 8 : 0);
+    if (ws_bytes < 1024) return 0;
+    long long r = (long long)((ws_bytes - 1024) / per_row);
+    if (r > nrows) r = nrows;
+    return r;
+}
+
+size_t knn_like_workspace(long long nq, int ncols, int k) {
+    const long long want = std::min<long long>(nq, std::max<long long>(64, (256ll << 20) / ((long long)ncols * 4)));
+    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    size_t b = round_up((size_t)want * ncols * 4, 256);
+    if (nseg > 1) b += round_up((size_t)want * nseg * k * 4, 256) * 2;
+    return b + 1024;
+}
+
+int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
+             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s) {
+    FG_REQUIRE(ny <= 0x7fffffffll, "too many columns");
+    const int ncols = (int)ny;
+    long long rows = chunk_rows(ws_bytes, nq, ncols, k);
+    if (rows < 1) return fail(FG_ERR_WORKSPACE, "workspace of %zu bytes holds no row of %d distances",
+                              ws_bytes, ncols);
+    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    for (long long q0 = 0; q0 < nq; q0 += rows) {
+        const long long r = std::min(rows, nq - q0);
+        Carve cv(ws, ws_bytes);
+        float* D = cv.take<float>((size_t)r * ncols);
+        float* sv = nseg > 1 ? cv.take<float>((size_t)r * nseg * k) : nullptr;
+        int32_t* si = nseg > 1 ? cv.take<int32_t>((size_t)r * nseg * k) : nullptr;
+        if (!cv.ok()) return fail(FG_ERR_WORKSPACE, "workspace too small");
+        int rc = l2_matrix(Q + q0 * dim, r, Y, ncols, dim, D, ncols, s);
+        if (rc) return rc;
+        rc = rows_topk(D, ncols, r, ncols, k, out_i + q0 * k, out_v + q0 * k, k, sv, si, s);
+        if (rc) return rc;
+    }
+    return FG_OK;
+}
+
+}  // namespace fg

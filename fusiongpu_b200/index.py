@@ -1,0 +1,311 @@
+"""Host-side mirror of the reference's IVF-PQ interface over the C ABI.
+
+Device memory and streams come from PyTorch (plumbing only); every kernel is
+the package's own sm_100a code behind ``libfusiongpu_b200.so``.  Function
+names follow the reference so a user of it finds the same entry points:
+
+==============================  ===============================================
+reference (file:line)           here
+==============================  ===============================================
+run_kmeans_gpu                  :func:`run_kmeans_gpu`        kmeans_gpu.cuh:234
+gpu_assign_to_centroids         :func:`gpu_assign_to_centroids` kmeans_gpu.cuh:367
+train_residual_pq_codebooks     :func:`train_residual_pq_codebooks` pq_utils.h:77
+encode_residuals_to_pq_gpu      :func:`encode_residuals_to_pq_gpu` kmeans_gpu.cuh:450
+search_cagra_index              :func:`coarse_search` (exact)  cagra_adapter.cuh:38
+run_gpu_batch_logic             :func:`run_gpu_batch_logic`   gpu_global.cu:679
+run_gpu_rerank                  :func:`run_gpu_rerank`        gpu_global.cu:667
+IVFIndexGPU / load_ivf_index    :class:`IVFPQIndex`           defs.h:49, search_pipeline.cu:481
+build_global main               :meth:`IVFPQIndex.build`      build_global.cu:21
+==============================  ===============================================
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import formats
+
+INVALID_PROBE = 0xFFFFFFFF
+
+
+@dataclasses.dataclass
+class SearchParams:
+    """Search parameters; defaults are the reference's (defs.h:17-41,
+    search_pipeline.cu:562-570)."""
+
+    top_m: int = 20
+    p1_lists: int = 12
+    limit_k: int = 50
+    threshold_coeff: float = 1.0
+    prune_ratio: float = 100.0
+    rerank_m: int = 10000
+    final_k: int = 10
+    mini_batch: int = 128
+    epsilon: float = 0.1
+    beta: int = 2
+    ref_compat: bool = True
+
+    def c(self) -> _lib.SearchParams:
+        return _lib.SearchParams(self.top_m, self.p1_lists, self.limit_k, self.threshold_coeff,
+                                 self.prune_ratio, self.rerank_m, self.final_k, self.mini_batch,
+                                 self.epsilon, self.beta, int(bool(self.ref_compat)))
+
+    def replace(self, **kw) -> "SearchParams":
+        return dataclasses.replace(self, **kw)
+
+
+def _dev(x, dtype, device) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        return x.to(device=device, dtype=dtype).contiguous()
+    return torch.from_numpy(np.ascontiguousarray(x)).to(device=device, dtype=dtype).contiguous()
+
+
+def _p(t: torch.Tensor | None):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def _stream(stream: torch.cuda.Stream | None = None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# ---- build steps ----------------------------------------------------------------
+
+def run_kmeans_gpu(data, k: int, max_iter: int = 20, seed: int = 42, device="cuda") -> torch.Tensor:
+    """Lloyd k-means (strided MT19937 seeding, exact assignment, ordered
+    centroid update).  Returns centroids [k][dim] on the device."""
+    x = _dev(data, torch.float32, device)
+    n, d = x.shape
+    cen = torch.empty((k, d), dtype=torch.float32, device=device)
+    ws = _workspace(_lib.size_query("fg_kmeans_workspace_size", n, d, k), device)
+    _lib.call("fg_kmeans", _p(x), n, d, k, max_iter, seed, _p(cen), _p(ws), ws.numel(), _stream())
+    return cen
+
+
+def gpu_assign_to_centroids(data, centroids, device="cuda") -> torch.Tensor:
+    x = _dev(data, torch.float32, device)
+    c = _dev(centroids, torch.float32, device)
+    out = torch.empty(x.shape[0], dtype=torch.int32, device=device)
+    _lib.call("fg_assign", _p(x), x.shape[0], x.shape[1], _p(c), c.shape[0], _p(out), _stream())
+    return out
+
+
+def sort_by_list(assign: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    n = assign.shape[0]
+    order = torch.empty(n, dtype=torch.int32, device=assign.device)
+    offsets = torch.empty(k + 1, dtype=torch.int32, device=assign.device)
+    ws = _workspace(_lib.size_query("fg_sort_by_list_workspace_size", n, k), assign.device)
+    _lib.call("fg_sort_by_list", _p(assign), n, k, _p(order), _p(offsets), _p(ws), ws.numel(), _stream())
+    return order, offsets
+
+
+def train_residual_pq_codebooks(data, vec_cluster_ids, clusters, pq_m: int, sample_size: int = 50000,
+                                max_iter: int = 8, device="cuda") -> torch.Tensor:
+    x = _dev(data, torch.float32, device)
+    a = _dev(vec_cluster_ids, torch.int32, device)
+    c = _dev(clusters, torch.float32, device)
+    n, d = x.shape
+    cb = torch.empty((pq_m, 256, d // pq_m), dtype=torch.float32, device=device)
+    ws = _workspace(_lib.size_query("fg_pq_train_workspace_size", n, d, pq_m, sample_size), device)
+    _lib.call("fg_pq_train", _p(x), n, d, _p(a), _p(c), pq_m, sample_size, max_iter, _p(cb), _p(ws),
+              ws.numel(), _stream())
+    return cb
+
+
+def encode_residuals_to_pq_gpu(data, cluster_ids, centroids, codebook, device="cuda") -> torch.Tensor:
+    x = _dev(data, torch.float32, device)
+    a = _dev(cluster_ids, torch.int32, device)
+    c = _dev(centroids, torch.float32, device)
+    cb = _dev(codebook, torch.float32, device)
+    pq_m = cb.shape[0]
+    codes = torch.empty((x.shape[0], pq_m), dtype=torch.uint8, device=device)
+    _lib.call("fg_pq_encode", _p(x), x.shape[0], x.shape[1], _p(a), _p(c), _p(cb), pq_m, _p(codes), _stream())
+    return codes
+
+
+# ---- search steps -----------------------------------------------------------------
+
+def coarse_search(queries, centroids, top_m: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact nearest `top_m` centroids (stands in for search_cagra_index).
+    Returns (ids uint32 as int32 tensor, squared distances)."""
+    q = _dev(queries, torch.float32, device)
+    c = _dev(centroids, torch.float32, device)
+    nq, d = q.shape
+    ids = torch.empty((nq, top_m), dtype=torch.int32, device=device)
+    dist = torch.empty((nq, top_m), dtype=torch.float32, device=device)
+    ws = _workspace(_lib.size_query("fg_coarse_workspace_size", c.shape[0], d, nq, top_m), device)
+    _lib.call("fg_coarse_search", _p(c), c.shape[0], d, _p(q), nq, top_m, _p(ids), _p(dist), _p(ws), ws.numel(),
+              _stream())
+    return ids, dist
+
+
+def knn_exact(base, queries, k: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    b = _dev(base, torch.float32, device)
+    q = _dev(queries, torch.float32, device)
+    ids = torch.empty((q.shape[0], k), dtype=torch.int32, device=device)
+    dist = torch.empty((q.shape[0], k), dtype=torch.float32, device=device)
+    ws = _workspace(_lib.size_query("fg_knn_workspace_size", b.shape[0], b.shape[1], q.shape[0], k), device)
+    _lib.call("fg_knn_exact", _p(b), b.shape[0], b.shape[1], _p(q), q.shape[0], k, _p(ids), _p(dist), _p(ws),
+              ws.numel(), _stream())
+    return ids, dist
+
+
+class IVFPQIndex:
+    """A device-resident IVF-PQ index (the reference's IVFIndexGPU plus the raw
+    base vectors SearchPipeline keeps for the rerank)."""
+
+    def __init__(self, centroids, codebook, offsets, ids, codes, base=None, device="cuda"):
+        self.device = torch.device(device)
+        self.centroids = _dev(centroids, torch.float32, device)
+        self.codebook = _dev(codebook, torch.float32, device)
+        self.offsets = _dev(offsets, torch.int32, device)
+        self.ids = _dev(ids, torch.int32, device)
+        self.codes = _dev(codes, torch.uint8, device)
+        self.base = _dev(base, torch.float32, device) if base is not None else None
+        self.nlist, self.dim = self.centroids.shape
+        self.pq_m = self.codes.shape[1]
+        self.total = self.ids.shape[0]
+        lens = self.offsets[1:] - self.offsets[:-1]
+        self.max_list_len = int(lens.max().item()) if self.nlist else 0
+        self._view = _lib.IvfpqView(self.codebook.data_ptr(), self.offsets.data_ptr(), self.codes.data_ptr(),
+                                    self.ids.data_ptr(), self.centroids.data_ptr(), self.nlist, self.dim,
+                                    self.pq_m, self.total, self.max_list_len)
+        self._ws = None
+
+    # -- construction ----------------------------------------------------------
+    @classmethod
+    def from_arrays(cls, index: dict, base=None, device="cuda") -> "IVFPQIndex":
+        return cls(index["centroids"], index["codebook"], index["offsets"], index["ids"], index["codes"], base,
+                   device)
+
+    @classmethod
+    def build(cls, base, nlist: int, pq_m: int, kmeans_iters: int = 20, pq_sample: int = 50000,
+              pq_iters: int = 8, seed: int = 42, keep_base: bool = True, device="cuda") -> "IVFPQIndex":
+        """k-means -> assignment -> residual PQ training -> encoding -> lists
+        (build_global.cu:21-258 without the list rebalancing and the CAGRA
+        graph over centroids, which the exact coarse quantizer replaces)."""
+        x = _dev(base, torch.float32, device)
+        cen = run_kmeans_gpu(x, nlist, kmeans_iters, seed, device)
+        a = gpu_assign_to_centroids(x, cen, device)
+        cb = train_residual_pq_codebooks(x, a, cen, pq_m, pq_sample, pq_iters, device)
+        codes = encode_residuals_to_pq_gpu(x, a, cen, cb, device)
+        order, offsets = sort_by_list(a, nlist)
+        lcodes = torch.empty_like(codes)
+        lids = torch.empty(x.shape[0], dtype=torch.int32, device=x.device)
+        _lib.call("fg_gather_lists", _p(codes), x.shape[0], pq_m, _p(order), _p(lcodes), _p(lids), _stream())
+        idx = cls(cen, cb, offsets, lids, lcodes, x if keep_base else None, device)
+        idx.assignment = a
+        return idx
+
+    @classmethod
+    def load(cls, res_dir: str, pq_m: int, dim: int, base=None, device="cuda") -> "IVFPQIndex":
+        """load_ivf_index_to_gpu (search_pipeline.cu:481-529)."""
+        return cls.from_arrays(formats.load_index(res_dir, pq_m, dim), base, device)
+
+    def save(self, res_dir: str) -> None:
+        formats.save_index(res_dir, self.to_numpy())
+
+    def to_numpy(self) -> dict:
+        return dict(codebook=self.codebook.cpu().numpy(), offsets=self.offsets.cpu().numpy(),
+                    ids=self.ids.cpu().numpy(), codes=self.codes.cpu().numpy(),
+                    centroids=self.centroids.cpu().numpy())
+
+    @property
+    def view(self) -> _lib.IvfpqView:
+        return self._view
+
+    # -- search ------------------------------------------------------------------
+    def workspace_bytes(self, nq: int, params: SearchParams) -> int:
+        return _lib.size_query("fg_search_workspace_size", C.byref(self._view), C.byref(params.c()), nq)
+
+    def workspace(self, nq: int, params: SearchParams) -> torch.Tensor:
+        need = self.workspace_bytes(nq, params)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = _workspace(need, self.device)
+        return self._ws
+
+    def search(self, queries, params: SearchParams | None = None, out=None, stream=None):
+        """Full search: exact coarse -> candidate generation -> rerank.
+        Returns (ids [nq][final_k] int32, dists [nq][final_k] float32)."""
+        params = params or SearchParams()
+        if self.base is None:
+            raise ValueError("search needs the raw base vectors (build with keep_base=True)")
+        q = _dev(queries, torch.float32, self.device)
+        nq = q.shape[0]
+        if out is None:
+            ids = torch.empty((nq, params.final_k), dtype=torch.int32, device=self.device)
+            dist = torch.empty((nq, params.final_k), dtype=torch.float32, device=self.device)
+        else:
+            ids, dist = out
+        ws = self.workspace(nq, params)
+        cp = params.c()
+        _lib.call("fg_search", C.byref(self._view), _p(self.base), self.base.shape[0], _p(q), nq, C.byref(cp),
+                  _p(ids), _p(dist), _p(ws), ws.numel(), _stream(stream))
+        return ids, dist
+
+    def coarse(self, queries, top_m: int):
+        return coarse_search(queries, self.centroids, top_m, self.device)
+
+    def batch_logic(self, queries, probe_ids, probe_dists, params: SearchParams):
+        return run_gpu_batch_logic(self, queries, probe_ids, probe_dists, params)
+
+    def rerank(self, queries, top_ids, top_counts, params: SearchParams):
+        return run_gpu_rerank(queries, top_ids, top_counts, self.base, params, self.device)
+
+
+def run_gpu_batch_logic(index: IVFPQIndex, queries, probe_ids, probe_dists, params: SearchParams):
+    """Candidate generation (gpu_global.cu:679-874).  Returns (top_ids,
+    top_dists [nq][rerank_m], top_counts [nq], candidate_counts [nq])."""
+    dev = index.device
+    q = _dev(queries, torch.float32, dev)
+    pid = _dev(probe_ids, torch.int32, dev)
+    pd = _dev(probe_dists, torch.float32, dev)
+    nq = q.shape[0]
+    rm = params.rerank_m
+    tid = torch.empty((nq, rm), dtype=torch.int32, device=dev)
+    td = torch.empty((nq, rm), dtype=torch.float32, device=dev)
+    tc = torch.empty(nq, dtype=torch.int32, device=dev)
+    cc = torch.empty(nq, dtype=torch.int32, device=dev)
+    cp = params.c()
+    _lib.call("fg_batch_logic", C.byref(index.view), _p(q), nq, _p(pid), _p(pd), C.byref(cp), _p(tid), _p(td),
+              _p(tc), _p(cc), _stream())
+    return tid, td, tc, cc
+
+
+def run_gpu_rerank(queries, top_ids, top_counts, base, params: SearchParams, device="cuda"):
+    """Exact rerank (gpu_global.cu:603-673).  Returns (ids, dists) [nq][final_k]."""
+    q = _dev(queries, torch.float32, device)
+    tid = _dev(top_ids, torch.int32, device)
+    tc = _dev(top_counts, torch.int32, device)
+    b = _dev(base, torch.float32, device)
+    nq = q.shape[0]
+    ids = torch.empty((nq, params.final_k), dtype=torch.int32, device=device)
+    dist = torch.empty((nq, params.final_k), dtype=torch.float32, device=device)
+    cp = params.c()
+    _lib.call("fg_rerank", _p(q), nq, q.shape[1], _p(tid), _p(tc), _p(b), b.shape[0], C.byref(cp), _p(ids),
+              _p(dist), _stream())
+    return ids, dist
+
+
+def recall_at(results: np.ndarray, gt: np.ndarray, k: int) -> float:
+    """compute_recall (search_pipeline.cu:531-557): hits of the first k
+    predicted ids (deduplicated) in the ground-truth rows, over nq*k."""
+    nq = results.shape[0]
+    hits = 0
+    for i in range(nq):
+        g = set(gt[i].tolist())
+        seen = set()
+        for v in results[i, :k].tolist():
+            if v in seen:
+                continue
+            seen.add(v)
+            hits += v in g
+    return hits / (nq * k)

@@ -1,0 +1,171 @@
+/*
+ * fusiongpu.h -- C ABI of the B200 (sm_100a) IVF-PQ search engine.
+ *
+ * Plain C: pointers, sizes and an opaque stream handle (a cudaStream_t passed
+ * as void*; NULL = the legacy default stream).  Every entry point returns an
+ * fg_status; on failure fg_last_error() gives a message (thread-local).
+ * All vector/index buffers are caller-owned DEVICE memory unless the name
+ * says "host".  Scratch memory is caller-owned too: query the *_workspace_size
+ * function and pass a device buffer at least that large (256-byte aligned).
+ * No entry point allocates device memory, and calls on different workspaces
+ * may run concurrently on different streams.
+ *
+ * Each entry point names the reference interface (Hello-day/FusionGPU) it
+ * replaces.
+ */
+#ifndef FUSIONGPU_H
+#define FUSIONGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FG_INVALID_PROBE 0xFFFFFFFFu
+
+typedef enum {
+    FG_OK = 0,
+    FG_ERR_INVALID_ARG = 1,   /* a size, pointer or parameter is out of range         */
+    FG_ERR_CUDA = 2,          /* a CUDA runtime call or kernel launch failed          */
+    FG_ERR_WORKSPACE = 3,     /* workspace missing, misaligned or too small           */
+    FG_ERR_UNSUPPORTED = 4,   /* a shape this build has no kernel for                 */
+    FG_ERR_DEVICE = 5         /* a kernel reported an error status from the device    */
+} fg_status;
+
+/* Read-only device view of an IVF-PQ index.  Same arrays as the reference's
+ * IVFIndexGPU (defs.h:49-56) and ivf_data.bin (build_global.cu:242-252), with
+ * the compile-time DIM / PQ_M of defs.h:9-12 made runtime fields. */
+typedef struct {
+    const float*   pq_codebook;   /* [pq_m][256][dim/pq_m]                       */
+    const int32_t* list_offsets;  /* [nlist + 1], list c = [offsets[c], offsets[c+1]) */
+    const uint8_t* pq_codes;      /* [total][pq_m], row-major, lists contiguous   */
+    const int32_t* vector_ids;    /* [total]                                      */
+    const float*   centroids;     /* [nlist][dim]                                 */
+    int32_t nlist;
+    int32_t dim;
+    int32_t pq_m;
+    int32_t total;
+    int32_t max_list_len;         /* longest list (kernels size shared memory by it) */
+} fg_ivfpq_view;
+
+/* Search parameters.  Names and defaults follow the reference's flags
+ * (search_pipeline.cu:562-588, defs.h:17-41). */
+typedef struct {
+    int32_t top_m;            /* nprobe: probed lists per query (-m)                  */
+    int32_t p1_lists;         /* lists scanned in phase 1 (--p1_lists)                */
+    int32_t limit_k;          /* candidates kept per phase-1 list (--limit_k)         */
+    float   threshold_coeff;  /* phase-2 threshold factor (--threshold_coeff)         */
+    float   prune_ratio;      /* drop probes farther than best * ratio (-p)           */
+    int32_t rerank_m;         /* rerank depth (-r)                                    */
+    int32_t final_k;          /* results per query (-k)                               */
+    int32_t mini_batch;       /* rerank mini-batch (-mb)                              */
+    float   epsilon;          /* rerank change-rate bound (-e)                        */
+    int32_t beta;             /* rerank stable rounds before stopping (--beta)        */
+    int32_t ref_compat;       /* 1: reproduce the reference's 128-lane gather, 128-entry
+                                 rerank window, 1024-vector phase-1 clamp and phase-2
+                                 overflow re-emission; 0: full rerank_m / k+mini_batch */
+} fg_search_params;
+
+const char* fg_version(void);
+const char* fg_last_error(void);
+void fg_search_params_default(fg_search_params* p);
+
+/* ---- coarse quantizer: replaces search_cagra_index (cagra_adapter.cuh:38-68)
+ * Exact top_m nearest centroids per query by squared L2, ascending by
+ * (distance, centroid id).  out_ids/out_dists: [nq][top_m]. */
+int fg_coarse_workspace_size(int32_t nlist, int32_t dim, int32_t nq, int32_t top_m, size_t* bytes);
+int fg_coarse_search(const float* centroids, int32_t nlist, int32_t dim, const float* queries,
+                     int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- candidate generation: replaces run_gpu_batch_logic (gpu_global.cu:679-874)
+ * Prune, per-(query, list) LUT in shared memory, phase-1 ADC scan with
+ * per-list top-limit_k, threshold, phase-2 ADC scan, and the sorted top
+ * rerank_m candidates per query.  probe_ids/probe_dists: [nq][top_m] as
+ * fg_coarse_search writes them (FG_INVALID_PROBE entries are skipped).
+ * top_ids/top_dists: [nq][rerank_m]; top_counts: [nq] = min(#candidates, rerank_m).
+ * Needs no workspace.  The probe list is not modified. */
+int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
+                   const uint32_t* probe_ids, const float* probe_dists,
+                   const fg_search_params* params, int32_t* top_ids, float* top_dists,
+                   int32_t* top_counts, int32_t* candidate_counts, void* stream);
+
+/* ---- exact rerank: replaces run_gpu_rerank (gpu_global.cu:603-673)
+ * Mini-batches of `mini_batch` candidates, exact fp32 squared L2 against the
+ * raw base vectors [nbase][dim], merged into a running top-final_k with the
+ * reference's early stop.  out_ids/out_dists: [nq][final_k]. */
+int fg_rerank(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids,
+              const int32_t* top_counts, const float* base, int64_t nbase,
+              const fg_search_params* params, int32_t* out_ids, float* out_dists, void* stream);
+
+/* ---- full search: coarse + candidate generation + rerank on one stream.
+ * Replaces one SearchPipeline::submit_batch (search_pipeline.cu:311-377)
+ * minus the host copies. */
+int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params,
+                             int32_t nq, size_t* bytes);
+int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries,
+              int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- index build (device pointers; the reference takes host pointers) ----- */
+
+/* Strided k-means seeding: centroid i = data[(i*stride + r_i % stride) % n],
+ * stride = max(1, n/k), r_i = the i-th output of MT19937(seed)
+ * (kmeans_gpu.cuh:259-267).  workspace: at least k*8 bytes. */
+int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_t seed,
+                   float* centroids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Nearest centroid by exact squared L2, lowest index on ties.  Replaces
+ * gpu_assign_to_centroids / gpu_assign_initial_clusters (kmeans_gpu.cuh:329-394). */
+int fg_assign(const float* data, int64_t n, int32_t dim, const float* centroids, int32_t k,
+              int32_t* out_assign, void* stream);
+
+/* Stable counting sort of point ids by assignment: order[] lists the points
+ * of cluster 0, then cluster 1, ... each in increasing id; offsets [k+1]. */
+int fg_sort_by_list_workspace_size(int64_t n, int32_t k, size_t* bytes);
+int fg_sort_by_list(const int32_t* assign, int64_t n, int32_t k, int32_t* order, int32_t* offsets,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Centroid update without float atomics: members summed in point order in
+ * double, one rounding to float; empty clusters keep their centroid.
+ * Replaces accumulate/compute_centroids (kmeans_gpu.cuh:81-116). */
+int fg_kmeans_update(const float* data, int32_t dim, const int32_t* order, const int32_t* offsets,
+                     int32_t k, float* centroids, void* stream);
+
+/* Lloyd k-means: init + iters x (assign, sort, update).  Replaces
+ * run_kmeans_gpu (kmeans_gpu.cuh:234-324). */
+int fg_kmeans_workspace_size(int64_t n, int32_t dim, int32_t k, size_t* bytes);
+int fg_kmeans(const float* data, int64_t n, int32_t dim, int32_t k, int32_t iters, uint32_t seed,
+              float* centroids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Residual PQ codebook training on a strided sample (seed 12345) with a
+ * 256-way k-means per subspace (seed 1234+m).  Replaces
+ * train_residual_pq_codebooks (pq_utils.h:77-138). */
+int fg_pq_train_workspace_size(int64_t n, int32_t dim, int32_t pq_m, int32_t sample, size_t* bytes);
+int fg_pq_train(const float* data, int64_t n, int32_t dim, const int32_t* assign,
+                const float* centroids, int32_t pq_m, int32_t sample, int32_t iters,
+                float* codebook, void* workspace, size_t workspace_bytes, void* stream);
+
+/* code[i][m] = nearest sub-codeword of the residual.  Replaces
+ * encode_residuals_to_pq_gpu (kmeans_gpu.cuh:450-508). */
+int fg_pq_encode(const float* data, int64_t n, int32_t dim, const int32_t* assign,
+                 const float* centroids, const float* codebook, int32_t pq_m, uint8_t* codes,
+                 void* stream);
+
+/* Gather codes into list order: out_codes[r] = codes[order[r]] (rows of pq_m
+ * bytes), out_ids[r] = order[r].  Replaces build_global.cu:226-240. */
+int fg_gather_lists(const uint8_t* codes, int64_t n, int32_t pq_m, const int32_t* order,
+                    uint8_t* out_codes, int32_t* out_ids, void* stream);
+
+/* Exact k nearest base vectors (ground truth), ascending by (distance, id). */
+int fg_knn_workspace_size(int64_t nbase, int32_t dim, int32_t nq, int32_t k, size_t* bytes);
+int fg_knn_exact(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq,
+                 int32_t k, int32_t* out_ids, float* out_dists, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,270 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle, and
+the reference's own kernels (oracle/_ref) against the oracle.
+
+Integer and index outputs must match exactly; distances bit-exactly, since
+both sides compute the same float expressions in the same order."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from tests import refpy
+from tests.conftest import cuda_available
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_available(), reason="needs a CUDA GPU")]
+
+torch = pytest.importorskip("torch")
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def fg():
+    import fusiongpu_b200.index as fgi
+    return fgi
+
+
+def _dataset(kind):
+    from fusiongpu_b200 import datasets as ds
+    if kind == "int128":
+        spec = ds.scaled(ds.C1, 20000, 192, n_centres=64, seed=11)
+        base, q = ds.generate(spec)
+        index, _ = oracle.build_index(base, 128, 32, kmeans_iters=6, pq_sample=8000, pq_iters=6)
+    elif kind == "int128m64":
+        spec = ds.scaled(ds.C2, 20000, 192, n_centres=64, seed=12)
+        base, q = ds.generate(spec)
+        index, _ = oracle.build_index(base, 96, 64, kmeans_iters=6, pq_sample=8000, pq_iters=6)
+    elif kind == "unit96":
+        spec = ds.scaled(ds.C3, 20000, 192, n_centres=64, seed=13)
+        base, q = ds.generate(spec)
+        index, _ = oracle.build_index(base, 128, 48, kmeans_iters=6, pq_sample=8000, pq_iters=6)
+    else:
+        raise ValueError(kind)
+    return index, base, q
+
+
+_CACHE = {}
+
+
+def dataset(kind):
+    if kind not in _CACHE:
+        _CACHE[kind] = _dataset(kind)
+    return _CACHE[kind]
+
+
+PARAMS = {
+    "c1": dict(top_m=16, p1_lists=6, limit_k=50, threshold_coeff=1.0, prune_ratio=100.0, rerank_m=100,
+               final_k=10, mini_batch=128, epsilon=0.1, beta=2),
+    "deep": dict(top_m=24, p1_lists=8, limit_k=60, threshold_coeff=1.2, prune_ratio=100.0, rerank_m=700,
+                 final_k=100, mini_batch=128, epsilon=0.1, beta=2),
+    "overflow": dict(top_m=20, p1_lists=2, limit_k=20, threshold_coeff=4.0, prune_ratio=100.0, rerank_m=400,
+                     final_k=20, mini_batch=64, epsilon=0.05, beta=3),
+    "prune": dict(top_m=32, p1_lists=40, limit_k=10, threshold_coeff=1.0, prune_ratio=1.05, rerank_m=64,
+                  final_k=8, mini_batch=16, epsilon=0.2, beta=1),
+}
+
+
+def _params(fg, name, ref_compat):
+    return fg.SearchParams(**PARAMS[name], ref_compat=ref_compat)
+
+
+@pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
+def test_coarse_matches_oracle(fg, kind):
+    index, base, q = dataset(kind)
+    for top_m in (1, 16, 77):
+        ids, d = fg.coarse_search(q, index["centroids"], top_m)
+        eids, ed = oracle.coarse(index["centroids"], q, top_m)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+        np.testing.assert_array_equal(_np(d), ed)
+
+
+@pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
+@pytest.mark.parametrize("pname", list(PARAMS))
+@pytest.mark.parametrize("ref_compat", [True, False])
+def test_batch_logic_and_rerank_match_oracle(fg, kind, pname, ref_compat):
+    index, base, q = dataset(kind)
+    p = _params(fg, pname, ref_compat)
+    if ref_compat and p.final_k > 128:
+        pytest.skip("ref_compat needs final_k <= 128")
+    eids, ed = oracle.coarse(index["centroids"], q, p.top_m)
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    ti, td, tc, cc = fg.run_gpu_batch_logic(idx, q, eids.view(np.int32), ed, p)
+    pd = dict(PARAMS[pname], ref_compat=ref_compat)
+    oi, od, oc, st = oracle.batch_logic(index, q, eids, ed, **pd)
+    np.testing.assert_array_equal(_np(cc), st["count"])
+    np.testing.assert_array_equal(_np(tc), oc)
+    np.testing.assert_array_equal(_np(td), od)
+    np.testing.assert_array_equal(_np(ti), oi)
+    ri, rd = fg.run_gpu_rerank(q, ti, tc, base, p)
+    xi, xd = oracle.rerank(q, oi, oc, base, **pd)
+    np.testing.assert_array_equal(_np(rd), xd)
+    np.testing.assert_array_equal(_np(ri), xi)
+
+
+@pytest.mark.parametrize("kind", ["int128", "unit96"])
+@pytest.mark.parametrize("ref_compat", [True, False])
+def test_full_search_matches_oracle(fg, kind, ref_compat):
+    index, base, q = dataset(kind)
+    p = _params(fg, "c1", ref_compat)
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    ids, d = idx.search(q, p)
+    ei, ed = oracle.search(index, base, q, **PARAMS["c1"], ref_compat=ref_compat)
+    np.testing.assert_array_equal(_np(ids), ei)
+    np.testing.assert_array_equal(_np(d), ed)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+@pytest.mark.parametrize("ref_compat", [True, False])
+def test_toy_edge_cases(fg, seed, ref_compat):
+    """Empty lists, a 1100-vector list (phase-1 clamp), phase-2 overflow,
+    heavy distance ties (integer codebooks)."""
+    index, base = refpy.toy_index(seed)
+    q = np.random.default_rng(100 + seed).integers(0, 16, size=(12, 16)).astype(np.float32)
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    for pd in [dict(top_m=8, p1_lists=3, limit_k=20, threshold_coeff=1.0, prune_ratio=100.0, rerank_m=200,
+                    final_k=10, mini_batch=128, epsilon=0.1, beta=2),
+               dict(top_m=8, p1_lists=2, limit_k=7, threshold_coeff=50.0, prune_ratio=100.0, rerank_m=300,
+                    final_k=16, mini_batch=40, epsilon=0.1, beta=3),
+               dict(top_m=6, p1_lists=12, limit_k=500, threshold_coeff=1.0, prune_ratio=100.0, rerank_m=50,
+                    final_k=5, mini_batch=16, epsilon=0.0, beta=1)]:
+        pd = dict(pd, ref_compat=ref_compat)
+        p = fg.SearchParams(**pd)
+        eids, ed = oracle.coarse(index["centroids"], q, p.top_m)
+        ti, td, tc, cc = fg.run_gpu_batch_logic(idx, q, eids.view(np.int32), ed, p)
+        oi, od, oc, st = oracle.batch_logic(index, q, eids, ed, **pd)
+        np.testing.assert_array_equal(_np(cc), st["count"])
+        np.testing.assert_array_equal(_np(tc), oc)
+        np.testing.assert_array_equal(_np(td), od)
+        np.testing.assert_array_equal(_np(ti), oi)
+        ri, rd = fg.run_gpu_rerank(q, ti, tc, base, p)
+        xi, xd = oracle.rerank(q, oi, oc, base, **pd)
+        np.testing.assert_array_equal(_np(ri), xi)
+        np.testing.assert_array_equal(_np(rd), xd)
+
+
+def test_knn_matches_oracle(fg):
+    index, base, q = dataset("int128")
+    ids, d = fg.knn_exact(base, q[:64], 10)
+    ei, ed = oracle.knn_exact(base, q[:64], 10)
+    np.testing.assert_array_equal(_np(ids), ei)
+    np.testing.assert_array_equal(_np(d), ed)
+
+
+def test_knn_two_stage_selection(fg):
+    """More than one 8192-column segment: the stage-2 merge must keep the
+    (distance, id) order."""
+    rng = np.random.default_rng(4)
+    base = rng.integers(0, 4, size=(30000, 8)).astype(np.float32)  # many exact ties
+    q = rng.integers(0, 4, size=(16, 8)).astype(np.float32)
+    ids, d = fg.knn_exact(base, q, 50)
+    ei, ed = oracle.knn_exact(base, q, 50)
+    np.testing.assert_array_equal(_np(d), ed)
+    np.testing.assert_array_equal(_np(ids), ei)
+
+
+def test_build_steps_match_oracle(fg):
+    from fusiongpu_b200 import datasets as ds
+    base, _ = ds.generate(ds.scaled(ds.C1, 12000, 4, n_centres=32, seed=21))
+    xb = torch.from_numpy(base).cuda()
+    cen = fg.run_kmeans_gpu(xb, 64, 5)
+    ecen = oracle.kmeans(base, 64, 5)
+    np.testing.assert_array_equal(_np(cen), ecen)
+    a = fg.gpu_assign_to_centroids(xb, cen)
+    ea = oracle.assign(base, ecen)
+    np.testing.assert_array_equal(_np(a), ea)
+    order, offs = fg.sort_by_list(a, 64)
+    np.testing.assert_array_equal(_np(order), np.argsort(ea, kind="stable"))
+    np.testing.assert_array_equal(_np(offs)[1:], np.cumsum(np.bincount(ea, minlength=64)))
+    cb = fg.train_residual_pq_codebooks(xb, a, cen, 32, 6000, 4)
+    ecb = oracle.pq_train(base, ea, ecen, 32, 6000, 4)
+    np.testing.assert_array_equal(_np(cb), ecb)
+    codes = fg.encode_residuals_to_pq_gpu(xb, a, cen, cb)
+    np.testing.assert_array_equal(_np(codes), oracle.pq_encode(base, ea, ecen, ecb))
+    idx = fg.IVFPQIndex.build(xb, 64, 32, kmeans_iters=5, pq_sample=6000, pq_iters=4)
+    eidx, _ = oracle.build_index(base, 64, 32, kmeans_iters=5, pq_sample=6000, pq_iters=4)
+    got = idx.to_numpy()
+    for k in ("centroids", "codebook", "offsets", "ids", "codes"):
+        np.testing.assert_array_equal(got[k], eidx[k])
+
+
+def test_errors_are_reported(fg):
+    from fusiongpu_b200 import _lib
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    with pytest.raises(_lib.FgError) as e:
+        idx.search(q[:4], fg.SearchParams(top_m=0))
+    assert e.value.status == 1
+    with pytest.raises(_lib.FgError) as e:
+        idx.search(q[:4], fg.SearchParams(top_m=10, limit_k=2000, ref_compat=True))
+    assert e.value.status == 1
+    # an empty batch is a no-op
+    ids, d = idx.search(q[:0], fg.SearchParams(top_m=10))
+    assert ids.shape == (0, 10)
+
+
+# ---- the reference's own kernels pin the oracle ---------------------------------
+
+def _ref_batch_and_rerank(index, base, q, pid, pdist, p):
+    dim = index["centroids"].shape[1]
+    pq_m = index["codes"].shape[1]
+    L = oracle.ref_lib("gg", dim, pq_m)
+    if L is None:
+        pytest.skip("oracle/_ref not built")
+    dev = "cuda"
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in index.items()}
+    tq = torch.from_numpy(q).to(dev)
+    tpid = torch.from_numpy(pid.view(np.int32).copy()).to(dev)
+    tpd = torch.from_numpy(pdist).to(dev)
+    nq, rm, k = q.shape[0], p["rerank_m"], p["final_k"]
+    top_i = torch.zeros((nq, rm), dtype=torch.int32, device=dev)  # fresh (zeroed) memory
+    top_d = torch.zeros((nq, rm), dtype=torch.float32, device=dev)
+    top_c = torch.zeros(nq, dtype=torch.int32, device=dev)
+    cnt = torch.zeros(nq, dtype=torch.int32, device=dev)
+    P = lambda x: C.c_void_p(x.data_ptr())
+    torch.cuda.synchronize()
+    rc = L.ref_run_batch_logic(P(t["codebook"]), P(t["offsets"]), P(t["codes"]), P(t["ids"]), P(t["centroids"]),
+                               index["centroids"].shape[0], P(tq), P(tpid), P(tpd), nq, p["top_m"], rm, k,
+                               C.c_float(p["prune_ratio"]), p["p1_lists"], p["limit_k"],
+                               C.c_float(p["threshold_coeff"]), P(top_i), P(top_d), P(top_c), P(cnt))
+    assert rc == 0, f"reference batch logic failed: cuda error {rc}"
+    tb = torch.from_numpy(base).to(dev)
+    fi = torch.zeros((nq, k), dtype=torch.int32, device=dev)
+    fd = torch.zeros((nq, k), dtype=torch.float32, device=dev)
+    rc = L.ref_run_rerank(P(tq), P(top_i), P(top_c), P(tb), P(fi), P(fd), nq, rm, k, base.shape[0],
+                          p["mini_batch"], C.c_float(p["epsilon"]), p["beta"])
+    assert rc == 0, f"reference rerank failed: cuda error {rc}"
+    return [_np(x) for x in (top_i, top_d, top_c, cnt, fi, fd)]
+
+
+@pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
+@pytest.mark.parametrize("pname", ["c1", "deep", "prune"])
+def test_reference_kernels_agree_with_oracle(kind, pname):
+    index, base, q = dataset(kind)
+    p = dict(PARAMS[pname], ref_compat=True)
+    pid, pdist = oracle.coarse(index["centroids"], q, p["top_m"])
+    oi, od, oc, st = oracle.batch_logic(index, q, pid, pdist, **p)
+    # The reference writes each query's candidates into a region sized by the
+    # summed lengths of its probed lists; phase-2 overflow re-emission can
+    # write past it.  Run the reference only where the oracle shows it stays
+    # inside (the oracle's count is the reference's write count).
+    lens = np.diff(index["offsets"])
+    best = pdist[:, :1] * np.float32(p["prune_ratio"])
+    budget = np.where(pdist > best, 0, lens[pid.astype(np.int64)]).sum(1)
+    assert (st["count"] <= budget).all()
+    ri, rd, rc, rn, fi, fd = _ref_batch_and_rerank(index, base, q, pid, pdist, p)
+    np.testing.assert_array_equal(rn, st["count"])
+    np.testing.assert_array_equal(rc, oc)
+    clean = st["p2_overflow"] == 0  # overflow re-emission order depends on atomics
+    assert clean.mean() > 0.5
+    w = min(128, p["rerank_m"])
+    np.testing.assert_array_equal(rd[clean, :w], od[clean, :w])
+    # ids: equal except where equal distances may be ordered differently
+    same = (ri[clean, :w] == oi[clean, :w]) | (rd[clean, :w] == np.roll(rd[clean, :w], 1, axis=1)) | (
+        rd[clean, :w] == np.roll(rd[clean, :w], -1, axis=1))
+    assert same.all()
+    xi, xd = oracle.rerank(q, oi, oc, base, **p)
+    np.testing.assert_array_equal(fd[clean], xd[clean])
+    assert (fi[clean] == xi[clean]).mean() > 0.999
