@@ -28,7 +28,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 RECALL_TARGET = 0.95
-SWEEP = (8, 16, 32, 64, 128)
+# BASELINE's sweep is {8..128}; 1/2/4 extend it downwards so the QPS at the
+# recall target is interpolated between points that bracket it
+SWEEP = (1, 2, 4, 8, 16, 32, 64, 128)
 CONFIG = dict(workload="C2: 1,000,000 x 128 fp32 integer-valued Gaussian mixture (4096 centres, sigma 10), "
                        "10,000 queries, L2",
               nlist=4096, pq_m=64, k=100, rerank_m=1000, p1_lists=12, limit_k=50, threshold_coeff=1.0,
@@ -42,7 +44,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="fusiongpu", choices=["fusiongpu", "reference"])
-    ap.add_argument("--cpu-sample", type=int, default=400, help="queries in the CPU-baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=4000, help="queries in the CPU-baseline sample")
+    ap.add_argument("--nprobe", type=int, default=0, help="time this nprobe only (profiling)")
+    ap.add_argument("--profile", action="store_true",
+                    help="build the index, then run only the scan kernel warmup+1 times (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
     return ap.parse_args()
@@ -167,6 +172,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.profile:
+        return profile_scan(args, device)
     W = setup(device, args.quick)
     idx, queries, gt = W["index"], W["queries"], W["gt"]
     nq = queries.shape[0]
@@ -177,7 +184,7 @@ def main():
     launches_per_step = 4 if idx.nlist <= 8192 else 5  # coarse tile + top-k (+stage 2) + scan + rerank
     clocks = ClockSampler(local)
     with clocks:
-        for nprobe in SWEEP:
+        for nprobe in (SWEEP if not args.nprobe else (args.nprobe,)):
             p = search_params(nprobe, SearchParams)
             ids = torch.empty((nq, p.final_k), dtype=torch.int32, device=device)
             dd = torch.empty((nq, p.final_k), dtype=torch.float32, device=device)
@@ -263,7 +270,7 @@ def main():
         "sweep": sweep,
         "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
-        "gpu_launches": launches_per_step * args.steps * len(SWEEP),
+        "gpu_launches": launches_per_step * args.steps * len(sweep),
         "gpu_launches_per_step": launches_per_step,
         "roofline": roof,
         "clocks": clocks.summary(),
@@ -275,6 +282,26 @@ def main():
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def profile_scan(args, device):
+    """Index build, coarse probes, then warmup+1 launches of the scan kernel
+    alone: the target of `ncu -k regex:ivfpq_batch_kernel -s <warmup> -c 1`."""
+    import torch
+    from fusiongpu_b200 import datasets as ds
+    from fusiongpu_b200.index import IVFPQIndex, SearchParams, run_gpu_batch_logic
+    spec, nlist = workload(args.quick)
+    base, queries = ds.generate(spec)
+    idx = IVFPQIndex.build(torch.from_numpy(base).to(device), nlist, CONFIG["pq_m"], device=device)
+    qd = torch.from_numpy(queries).to(device)
+    nprobe = args.nprobe or 8
+    p = search_params(nprobe, SearchParams)
+    pid, pd = idx.coarse(qd, nprobe)
+    for _ in range(args.warmup + 1):
+        run_gpu_batch_logic(idx, qd, pid, pd, p)
+    torch.cuda.synchronize(device)
+    print(json.dumps({"profile": "scan", "nprobe": nprobe, "nq": int(queries.shape[0]),
+                      "max_list_len": idx.max_list_len}))
 
 
 def roofline(idx, qd, nprobe, args, device, SearchParams, flush):

@@ -35,7 +35,7 @@ struct ScanArgs {
     const uint8_t* codes;
     const int32_t* vids;
     const float* centroids;
-    int nlist, dim;
+    int nlist, dim, pq_m, sub_dim;  // pq_m/sub_dim are read by the generic (M = 0) kernel
     const float* queries;
     const uint32_t* probe_ids;
     const float* probe_dists;
@@ -119,11 +119,25 @@ __device__ __forceinline__ float sub_dist(const float* r, const float* c) {
     }
 }
 
-// ADC distance of one PQ code row: sum of LUT entries in subspace order.
-template <int M>
-__device__ __forceinline__ float adc(const uint8_t* __restrict__ row, const float* __restrict__ lut) {
+__device__ __forceinline__ float sub_dist_rt(const float* r, const float* c, int sd) {
+    if (sd == 4) return sub_dist<4>(r, c);
+    if (sd == 8) return sub_dist<8>(r, c);
     float d = 0.0f;
-    if constexpr (M % 16 == 0) {
+    for (int i = 0; i < sd; ++i) {
+        const float df = r[i] - __ldg(c + i);
+        d = fmaf(df, df, d);
+    }
+    return d;
+}
+
+// ADC distance of one PQ code row: sum of LUT entries in subspace order.
+// M = 0: runtime pq_m (`mrt`), byte loads.
+template <int M>
+__device__ __forceinline__ float adc(const uint8_t* __restrict__ row, const float* __restrict__ lut, int mrt = 0) {
+    float d = 0.0f;
+    if constexpr (M == 0) {
+        for (int m = 0; m < mrt; ++m) d = __fadd_rn(d, lut[m * 256 + __ldg(row + m)]);
+    } else if constexpr (M % 16 == 0) {
         const uint4* r4 = reinterpret_cast<const uint4*>(row);
 #pragma unroll
         for (int w = 0; w < M / 16; ++w) {
@@ -157,9 +171,17 @@ __device__ __forceinline__ void build_lut(const ScanArgs& a, const float* qv, ui
     const float* cv = a.centroids + (size_t)c * a.dim;
     for (int t = threadIdx.x; t < a.dim; t += SCAN_NT) res[t] = qv[t] - cv[t];
     __syncthreads();
-    for (int e = threadIdx.x; e < M * 256; e += SCAN_NT) {
-        const int m = e >> 8;
-        lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
+    if constexpr (M == 0) {
+        const int sd = a.sub_dim;
+        for (int e = threadIdx.x; e < a.pq_m * 256; e += SCAN_NT) {
+            const int m = e >> 8;
+            lut[e] = sub_dist_rt(res + m * sd, a.codebook + (size_t)e * sd, sd);
+        }
+    } else {
+        for (int e = threadIdx.x; e < M * 256; e += SCAN_NT) {
+            const int m = e >> 8;
+            lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
+        }
     }
     __syncthreads();
 }
@@ -221,7 +243,9 @@ template <int M, int SD>
 __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) {
     static_assert(SCAN_NT == 2 * REF_BLOCK, "phase-2 overflow ranks assume 256 threads");
     extern __shared__ __align__(16) unsigned char smem[];
-    const ScanLayout L = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
+    constexpr bool RT = (M == 0);
+    const int MM = RT ? a.pq_m : M;
+    const ScanLayout L = scan_layout(MM, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
     float* lut = reinterpret_cast<float*>(smem + L.lut);
     float* res = reinterpret_cast<float*>(smem + L.res);
     uint32_t* pid = reinterpret_cast<uint32_t*>(smem + L.pid);
@@ -268,7 +292,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
         const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
         build_lut<M, SD>(a, qv, c, res, lut);
         for (int i = tid; i < scan; i += SCAN_NT)
-            lkey[i] = f2key(adc<M>(a.codes + (size_t)(start + i) * M, lut));
+            lkey[i] = f2key(adc<M>(a.codes + (size_t)(start + i) * MM, lut, MM));
         __syncthreads();
         uint32_t kth;
         int n_less;
@@ -319,7 +343,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
             float d = 0.0f;
             bool pass = false;
             if (i < len) {
-                d = adc<M>(a.codes + (size_t)(start + i) * M, lut);
+                d = adc<M>(a.codes + (size_t)(start + i) * MM, lut, MM);
                 pass = d <= thr;
             }
             int p_tot;
@@ -348,7 +372,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
             float d = 0.0f;
             bool pass = false;
             if (i < len) {
-                d = adc<M>(a.codes + (size_t)(start + i) * M, lut);
+                d = adc<M>(a.codes + (size_t)(start + i) * MM, lut, MM);
                 pass = d <= thr;
             }
             ms->passf[tid] = pass ? 1 : 0;
@@ -416,6 +440,7 @@ static ScanKernel pick_scan_kernel(int M, int SD) {
     FG_SCAN_CASE(96, 8)
     FG_SCAN_CASE(128, 1)
 #undef FG_SCAN_CASE
+    if (M <= 256 && SD <= 16) return ivfpq_batch_kernel<0, 0>;  // generic runtime shape
     return nullptr;
 }
 
@@ -440,6 +465,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
                "null index array");
     FG_REQUIRE(aligned(ix->pq_codes, 16) && aligned(ix->pq_codebook, 16) && aligned(queries, 16),
                "codes, codebook and queries must be 16-byte aligned");
+    FG_REQUIRE(ix->nlist >= 1 && ix->total >= 0, "empty index");
     const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
     ScanKernel k = pick_scan_kernel(M, SD);
     if (!k) return fail(FG_ERR_UNSUPPORTED, "no scan kernel for pq_m=%d sub_dim=%d", M, SD);
@@ -452,6 +478,8 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.centroids = ix->centroids;
     a.nlist = ix->nlist;
     a.dim = ix->dim;
+    a.pq_m = M;
+    a.sub_dim = SD;
     a.queries = queries;
     a.probe_ids = probe_ids;
     a.probe_dists = probe_dists;
