@@ -60,6 +60,26 @@ int pq_encode(const float* data, int64_t n, int dim, const int32_t* assign, cons
               const float* codebook, int pq_m, uint8_t* codes, cudaStream_t s);
 int gather_lists(const uint8_t* codes, int64_t n, int pq_m, const int32_t* order, uint8_t* out_codes,
                  int32_t* out_ids, cudaStream_t s);
+bool coarse_tc_supported(int dim);
+size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P);
+int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
+              uint32_t* out_ids, float* out_d, void* ws, size_t ws_bytes, cudaStream_t s, int* n_fallback_host);
+
+// Coarse quantizer dispatch: tensor cores with exact rescoring when the shape
+// fits (3*dim <= 384), else exact CUDA-core tiles.
+static size_t coarse_workspace(long long nq, int nlist, int dim, int P) {
+    size_t b = knn_like_workspace(std::max(nq, 1ll), nlist, P);
+    if (coarse_tc_supported(dim)) b = std::max(b, coarse_tc_workspace(std::max(nq, 1ll), nlist, dim, P));
+    return b;
+}
+
+static int coarse(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
+                  uint32_t* out_ids, float* out_d, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (coarse_tc_supported(dim))
+        return coarse_tc(centroids, nlist, dim, queries, nq, P, out_ids, out_d, ws, ws_bytes, s, nullptr);
+    return knn_like(centroids, nlist, dim, queries, nq, P, reinterpret_cast<int32_t*>(out_ids), out_d, ws,
+                    ws_bytes, s);
+}
 
 static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
@@ -115,7 +135,7 @@ void fg_search_params_default(fg_search_params* p) {
 int fg_coarse_workspace_size(int32_t nlist, int32_t dim, int32_t nq, int32_t top_m, size_t* bytes) {
     FG_REQUIRE(bytes, "null bytes");
     FG_REQUIRE(nlist >= 1 && dim >= 1 && nq >= 0 && top_m >= 1 && top_m <= nlist, "bad coarse shape");
-    *bytes = knn_like_workspace(std::max(nq, 1), nlist, top_m);
+    *bytes = coarse_workspace(std::max(nq, 1), nlist, dim, top_m);
     return FG_OK;
 }
 
@@ -128,8 +148,34 @@ int fg_coarse_search(const float* centroids, int32_t nlist, int32_t dim, const f
     FG_REQUIRE(centroids && queries && out_ids && out_dists, "null buffer");
     int rc = need_ws(ws, ws_bytes, 1024);
     if (rc) return rc;
+    return coarse(centroids, nlist, dim, queries, nq, top_m, out_ids, out_dists, ws, ws_bytes, as_stream(stream));
+}
+
+int fg_coarse_search_simt(const float* centroids, int32_t nlist, int32_t dim, const float* queries, int32_t nq,
+                          int32_t top_m, uint32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes,
+                          void* stream) {
+    FG_REQUIRE(nlist >= 1 && dim >= 1 && nq >= 0, "bad coarse shape");
+    FG_REQUIRE(top_m >= 1 && top_m <= nlist && top_m <= 4096, "top_m %d outside [1, min(nlist, 4096)]", top_m);
+    if (nq == 0) return FG_OK;
+    FG_REQUIRE(centroids && queries && out_ids && out_dists, "null buffer");
+    int rc = need_ws(ws, ws_bytes, 1024);
+    if (rc) return rc;
     return knn_like(centroids, nlist, dim, queries, nq, top_m, reinterpret_cast<int32_t*>(out_ids), out_dists, ws,
                     ws_bytes, as_stream(stream));
+}
+
+int fg_coarse_search_tc(const float* centroids, int32_t nlist, int32_t dim, const float* queries, int32_t nq,
+                        int32_t top_m, uint32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes,
+                        int32_t* n_fallback, void* stream) {
+    FG_REQUIRE(nlist >= 1 && dim >= 1 && nq >= 0, "bad coarse shape");
+    FG_REQUIRE(top_m >= 1 && top_m <= nlist && top_m <= 4096, "top_m %d outside [1, min(nlist, 4096)]", top_m);
+    if (!coarse_tc_supported(dim)) return fail(FG_ERR_UNSUPPORTED, "tensor-core coarse path needs 3*dim <= 384");
+    if (nq == 0) return FG_OK;
+    FG_REQUIRE(centroids && queries && out_ids && out_dists, "null buffer");
+    int rc = need_ws(ws, ws_bytes, coarse_tc_workspace(nq, nlist, dim, top_m));
+    if (rc) return rc;
+    return coarse_tc(centroids, nlist, dim, queries, nq, top_m, out_ids, out_dists, ws, ws_bytes, as_stream(stream),
+                     n_fallback);
 }
 
 int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq, const uint32_t* probe_ids,
@@ -152,7 +198,7 @@ int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params*
     FG_REQUIRE(nq >= 0 && params->top_m >= 1 && params->top_m <= index->nlist && params->rerank_m >= 1,
                "bad search shape");
     *bytes = search_fixed_bytes(std::max(nq, 1), params) +
-             knn_like_workspace(std::max(nq, 1), index->nlist, params->top_m) + 1024;
+             coarse_workspace(std::max(nq, 1), index->nlist, index->dim, params->top_m) + 1024;
     return FG_OK;
 }
 
@@ -176,8 +222,8 @@ int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, cons
     int32_t* tc = cv.take<int32_t>((size_t)nq);
     const size_t used = round_up(cv.used, 256);
     if (!cv.ok() || used >= ws_bytes) return fail(FG_ERR_WORKSPACE, "search workspace too small");
-    rc = knn_like(index->centroids, index->nlist, index->dim, queries, nq, params->top_m,
-                  reinterpret_cast<int32_t*>(pids), pd, static_cast<char*>(ws) + used, ws_bytes - used, s);
+    rc = coarse(index->centroids, index->nlist, index->dim, queries, nq, params->top_m, pids, pd,
+                static_cast<char*>(ws) + used, ws_bytes - used, s);
     if (rc) return rc;
     rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s);
     if (rc) return rc;

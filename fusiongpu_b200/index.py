@@ -133,17 +133,24 @@ def encode_residuals_to_pq_gpu(data, cluster_ids, centroids, codebook, device="c
 
 # ---- search steps -----------------------------------------------------------------
 
-def coarse_search(queries, centroids, top_m: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+def coarse_search(queries, centroids, top_m: int, device="cuda", path: str = "auto"):
     """Exact nearest `top_m` centroids (stands in for search_cagra_index).
-    Returns (ids uint32 as int32 tensor, squared distances)."""
+    Returns (ids uint32 as int32 tensor, squared distances); with path="tc"
+    also the number of queries that needed the exact fallback.
+    path: "auto" (tensor cores when the shape allows), "tc", "simt"."""
     q = _dev(queries, torch.float32, device)
     c = _dev(centroids, torch.float32, device)
     nq, d = q.shape
     ids = torch.empty((nq, top_m), dtype=torch.int32, device=device)
     dist = torch.empty((nq, top_m), dtype=torch.float32, device=device)
     ws = _workspace(_lib.size_query("fg_coarse_workspace_size", c.shape[0], d, nq, top_m), device)
-    _lib.call("fg_coarse_search", _p(c), c.shape[0], d, _p(q), nq, top_m, _p(ids), _p(dist), _p(ws), ws.numel(),
-              _stream())
+    if path == "tc":
+        nfb = C.c_int32(0)
+        _lib.call("fg_coarse_search_tc", _p(c), c.shape[0], d, _p(q), nq, top_m, _p(ids), _p(dist), _p(ws),
+                  ws.numel(), C.byref(nfb), _stream())
+        return ids, dist, int(nfb.value)
+    name = "fg_coarse_search_simt" if path == "simt" else "fg_coarse_search"
+    _lib.call(name, _p(c), c.shape[0], d, _p(q), nq, top_m, _p(ids), _p(dist), _p(ws), ws.numel(), _stream())
     return ids, dist
 
 

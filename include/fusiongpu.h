@@ -80,6 +80,20 @@ int fg_coarse_search(const float* centroids, int32_t nlist, int32_t dim, const f
                      int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same ranking through one fixed path: exact fp32 CUDA-core tiles, or the
+ * tcgen05 tensor-core GEMM (split-bf16 operands staged by TMA) whose top
+ * candidates are rescored exactly and certified against an error bound, with
+ * an exact per-query fallback.  fg_coarse_search picks the tensor-core path
+ * when 3*dim <= 384.  n_fallback (HOST int, may be NULL): when given, the call
+ * waits for the stream and stores how many queries needed the exact fallback.
+ * Both return the same ids and distances. */
+int fg_coarse_search_simt(const float* centroids, int32_t nlist, int32_t dim, const float* queries,
+                          int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
+                          void* workspace, size_t workspace_bytes, void* stream);
+int fg_coarse_search_tc(const float* centroids, int32_t nlist, int32_t dim, const float* queries,
+                        int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
+                        void* workspace, size_t workspace_bytes, int32_t* n_fallback, void* stream);
+
 /* ---- candidate generation: replaces run_gpu_batch_logic (gpu_global.cu:679-874)
  * Prune, per-(query, list) LUT in shared memory, phase-1 ADC scan with
  * per-list top-limit_k, threshold, phase-2 ADC scan, and the sorted top

@@ -81,6 +81,47 @@ def test_coarse_matches_oracle(fg, kind):
         np.testing.assert_array_equal(_np(d), ed)
 
 
+@pytest.mark.parametrize("kind", ["int128", "unit96"])
+@pytest.mark.parametrize("path", ["tc", "simt"])
+def test_coarse_paths_match_oracle(fg, kind, path):
+    index, base, q = dataset(kind)
+    for top_m in (1, 16, 77, 128):
+        r = fg.coarse_search(q, index["centroids"], top_m, path=path)
+        eids, ed = oracle.coarse(index["centroids"], q, top_m)
+        np.testing.assert_array_equal(_np(r[1]), ed)
+        np.testing.assert_array_equal(_np(r[0]).astype(np.uint32), eids)
+        if path == "tc":
+            assert r[2] <= q.shape[0] // 20  # the certificate holds for almost every query
+
+
+def test_coarse_tc_fallback_on_ties(fg):
+    """Every centroid has exactly three ones, so all are at distance 3 from a
+    zero query: the tie spans the cut, the certificate cannot hold, and the
+    exact fallback must reproduce the oracle's (distance, id) ranking."""
+    rng = np.random.default_rng(9)
+    cen = np.zeros((700, 32), np.float32)
+    for i in range(700):
+        cen[i, rng.choice(32, 3, replace=False)] = 1.0
+    q = rng.integers(0, 2, size=(64, 32)).astype(np.float32)
+    q[::2] = 0.0
+    ids, d, nfb = fg.coarse_search(q, cen, 20, path="tc")
+    eids, ed = oracle.coarse(cen, q, 20)
+    np.testing.assert_array_equal(_np(d), ed)
+    np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+    assert nfb >= 32
+
+
+def test_coarse_tc_many_lists_two_stage(fg):
+    """nlist above one select segment (8192): stage-2 merge in the superset select."""
+    rng = np.random.default_rng(10)
+    cen = rng.normal(size=(20000, 64)).astype(np.float32)
+    q = rng.normal(size=(200, 64)).astype(np.float32)
+    ids, d, nfb = fg.coarse_search(q, cen, 64, path="tc")
+    eids, ed = oracle.coarse(cen, q, 64)
+    np.testing.assert_array_equal(_np(d), ed)
+    np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+
+
 @pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
 @pytest.mark.parametrize("pname", list(PARAMS))
 @pytest.mark.parametrize("ref_compat", [True, False])
