@@ -41,6 +41,7 @@ _SIGS = {
     "fg_coarse_search": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P],
     "fg_coarse_search_simt": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P],
     "fg_coarse_search_tc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P, _P],
+    "fg_coarse_search_noalloc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P],
     "fg_batch_logic": [C.POINTER(IvfpqView), _P, _I32, _P, _P, C.POINTER(SearchParams), _P, _P, _P, _P, _P],
     "fg_rerank": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
     "fg_search_workspace_size": [C.POINTER(IvfpqView), C.POINTER(SearchParams), _I32, C.POINTER(_SZ)],

@@ -94,6 +94,21 @@ int fg_coarse_search_tc(const float* centroids, int32_t nlist, int32_t dim, cons
                         int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
                         void* workspace, size_t workspace_bytes, int32_t* n_fallback, void* stream);
 
+/* ---- allocation-free coarse search (no counterpart in the reference)
+ * For callers that cannot give this library device memory when they call it:
+ * code inside CUDA stream capture, plugins whose host runtime owns all device
+ * pools, serving loops that must never reach cudaMalloc.  Same results as
+ * fg_coarse_search_simt, with the scratch in a fixed 16 MiB device array built
+ * into the library (held on every GPU that loads it).  Returns
+ * FG_ERR_INVALID_ARG when one query's scratch row (4*nlist bytes, plus
+ * 8*top_m per 8192 centroids past the first 8192) exceeds it.  The first call
+ * on each device resolves the array's address; make it outside stream
+ * capture.  All calls on a device share the array: calls whose GPU work
+ * overlaps race and must be serialised by the caller. */
+int fg_coarse_search_noalloc(const float* centroids, int32_t nlist, int32_t dim, const float* queries,
+                             int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
+                             void* stream);
+
 /* ---- candidate generation: replaces run_gpu_batch_logic (gpu_global.cu:679-874)
  * Prune, per-(query, list) LUT in shared memory, phase-1 ADC scan with
  * per-list top-limit_k, threshold, phase-2 ADC scan, and the sorted top
