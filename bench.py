@@ -46,8 +46,8 @@ def parse():
     ap.add_argument("--impl", default="fusiongpu", choices=["fusiongpu", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=4000, help="queries in the CPU-baseline sample")
     ap.add_argument("--nprobe", type=int, default=0, help="time this nprobe only (profiling)")
-    ap.add_argument("--profile", action="store_true",
-                    help="build the index, then run only the scan kernel warmup+1 times (for ncu)")
+    ap.add_argument("--profile", default="", choices=["", "scan", "coarse", "rerank", "search"],
+                    help="build the index, then run only this stage warmup+1 times (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
     return ap.parse_args()
@@ -173,7 +173,7 @@ def main():
         return float(t.item())
 
     if args.profile:
-        return profile_scan(args, device)
+        return profile_stage(args, device)
     W = setup(device, args.quick)
     idx, queries, gt = W["index"], W["queries"], W["gt"]
     nq = queries.shape[0]
@@ -284,12 +284,12 @@ def main():
         dist.destroy_process_group()
 
 
-def profile_scan(args, device):
-    """Index build, coarse probes, then warmup+1 launches of the scan kernel
-    alone: the target of `ncu -k regex:ivfpq_batch_kernel -s <warmup> -c 1`."""
+def profile_stage(args, device):
+    """Index build, coarse probes, then warmup+1 launches of one stage alone:
+    the target of `ncu -k regex:<kernel> -s <warmup> -c 1`."""
     import torch
     from fusiongpu_b200 import datasets as ds
-    from fusiongpu_b200.index import IVFPQIndex, SearchParams, run_gpu_batch_logic
+    from fusiongpu_b200.index import IVFPQIndex, SearchParams, run_gpu_batch_logic, run_gpu_rerank
     spec, nlist = workload(args.quick)
     base, queries = ds.generate(spec)
     idx = IVFPQIndex.build(torch.from_numpy(base).to(device), nlist, CONFIG["pq_m"], device=device)
@@ -297,10 +297,19 @@ def profile_scan(args, device):
     nprobe = args.nprobe or 8
     p = search_params(nprobe, SearchParams)
     pid, pd = idx.coarse(qd, nprobe)
-    for _ in range(args.warmup + 1):
-        run_gpu_batch_logic(idx, qd, pid, pd, p)
+    ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pd, p)
     torch.cuda.synchronize(device)
-    print(json.dumps({"profile": "scan", "nprobe": nprobe, "nq": int(queries.shape[0]),
+    for _ in range(args.warmup + 1):
+        if args.profile == "scan":
+            run_gpu_batch_logic(idx, qd, pid, pd, p)
+        elif args.profile == "coarse":
+            idx.coarse(qd, nprobe)
+        elif args.profile == "rerank":
+            run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+        else:
+            idx.search(qd, p)
+    torch.cuda.synchronize(device)
+    print(json.dumps({"profile": args.profile, "nprobe": nprobe, "nq": int(queries.shape[0]),
                       "max_list_len": idx.max_list_len}))
 
 

@@ -60,7 +60,7 @@ int pq_encode(const float* data, int64_t n, int dim, const int32_t* assign, cons
               const float* codebook, int pq_m, uint8_t* codes, cudaStream_t s);
 int gather_lists(const uint8_t* codes, int64_t n, int pq_m, const int32_t* order, uint8_t* out_codes,
                  int32_t* out_ids, cudaStream_t s);
-bool coarse_tc_supported(int dim);
+bool coarse_tc_supported(int dim, int P);
 size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P);
 int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
               uint32_t* out_ids, float* out_d, void* ws, size_t ws_bytes, cudaStream_t s, int* n_fallback_host);
@@ -69,13 +69,13 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
 // fits (3*dim <= 384), else exact CUDA-core tiles.
 static size_t coarse_workspace(long long nq, int nlist, int dim, int P) {
     size_t b = knn_like_workspace(std::max(nq, 1ll), nlist, P);
-    if (coarse_tc_supported(dim)) b = std::max(b, coarse_tc_workspace(std::max(nq, 1ll), nlist, dim, P));
+    if (coarse_tc_supported(dim, P)) b = std::max(b, coarse_tc_workspace(std::max(nq, 1ll), nlist, dim, P));
     return b;
 }
 
 static int coarse(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
                   uint32_t* out_ids, float* out_d, void* ws, size_t ws_bytes, cudaStream_t s) {
-    if (coarse_tc_supported(dim))
+    if (coarse_tc_supported(dim, P))
         return coarse_tc(centroids, nlist, dim, queries, nq, P, out_ids, out_d, ws, ws_bytes, s, nullptr);
     return knn_like(centroids, nlist, dim, queries, nq, P, reinterpret_cast<int32_t*>(out_ids), out_d, ws,
                     ws_bytes, s);
@@ -169,7 +169,8 @@ int fg_coarse_search_tc(const float* centroids, int32_t nlist, int32_t dim, cons
                         int32_t* n_fallback, void* stream) {
     FG_REQUIRE(nlist >= 1 && dim >= 1 && nq >= 0, "bad coarse shape");
     FG_REQUIRE(top_m >= 1 && top_m <= nlist && top_m <= 4096, "top_m %d outside [1, min(nlist, 4096)]", top_m);
-    if (!coarse_tc_supported(dim)) return fail(FG_ERR_UNSUPPORTED, "tensor-core coarse path needs 3*dim <= 384");
+    if (!coarse_tc_supported(dim, top_m))
+        return fail(FG_ERR_UNSUPPORTED, "tensor-core coarse path needs 3*dim <= 384 and top_m <= 256");
     if (nq == 0) return FG_OK;
     FG_REQUIRE(centroids && queries && out_ids && out_dists, "null buffer");
     int rc = need_ws(ws, ws_bytes, coarse_tc_workspace(nq, nlist, dim, top_m));

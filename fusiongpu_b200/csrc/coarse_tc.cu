@@ -5,16 +5,22 @@
 //    A = [q_hi | q_hi | q_lo], B = [c_hi | c_lo | c_hi] (K = 3*dim, zero padded to
 //    a multiple of 64), so one bf16 GEMM A.B^T = q_hi.c_hi + q_hi.c_lo + q_lo.c_hi
 //    approximates q.c to about 2^-16 relative.
-// 2. coarse_gemm_kernel: one 128x128 tile per CTA, operands staged by TMA (128-byte
-//    swizzle, no multicast), tcgen05.mma issued by one thread, accumulator in TMEM,
-//    epilogue writes d~ = |q|^2 + |c|^2 - 2 q.c.
-// 3. the S = max(2P, P+32) smallest d~ per query (two-stage radix select).
-// 4. coarse_rescore_kernel: exact fp32 distances (the oracle's arithmetic) of the S
-//    candidates, sorted by (distance, id).  The top P is certified exact when the
-//    P-th exact distance is below the smallest excluded d~ minus an error bound
-//    E(q) on |d~ - d|; otherwise (or if the GEMM reported a failed wait) the query is
-//    rescored exactly against every centroid.  Rankings therefore equal the exact
-//    ones bit for bit, whatever the tensor-core rounding.
+// 2. coarse_gemm_kernel: persistent, warp-specialised CTA per 128 queries x a run of
+//    64-centroid tiles; A resident in shared memory, B through a 2-stage TMA ring
+//    (128-byte swizzle, no multicast), tcgen05.mma issued by one thread into two
+//    TMEM accumulators; epilogue computes d~ = |q|^2 + |c|^2 - 2 q.c.
+//    Pass 0 writes d~ for a prefix of NS centroids; the S-th smallest of those (S =
+//    max(2P, P+32)) bounds the S-th smallest over all centroids.  Pass 1 covers every
+//    centroid and appends only (d~, id) within that bound to a per-query list, so
+//    no nq x nlist matrix is ever written.
+// 3. coarse_finish_kernel: per query, the S smallest appended d~ are rescored with
+//    exact fp32 distances (the oracle's arithmetic) and sorted by (distance, id).
+//    The top P is certified exact when the P-th exact distance is below the
+//    S-th d~ minus an error bound E(q) on |d~ - d| (every excluded centroid has
+//    d~ >= the S-th); otherwise -- list overflow, a failed wait in the GEMM, or
+//    a certificate that does not hold -- the query is rescored exactly against
+//    every centroid.  Rankings therefore equal the exact ones bit for bit,
+//    whatever the tensor-core rounding.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -24,14 +30,14 @@
 
 namespace fg {
 
-int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, int32_t* out_i, float* out_v,
-              long long out_ld, float* stage_v, int32_t* stage_i, cudaStream_t s);
-size_t rows_topk_stage_bytes(long long rows, int ncols, int k);
 
-constexpr int TC_TILE = 128;    // M = N = 128 per CTA
+constexpr int TC_M = 128;       // queries per CTA (UMMA M, TMEM lanes)
+constexpr int TC_N = 64;        // centroids per tile (UMMA N)
+constexpr int TC_TILE = 128;    // row padding of both operands
 constexpr int TC_KB = 64;       // bf16 elements per K block (one 128-byte swizzle row)
-constexpr int TC_MAX_KB = 6;    // all K blocks resident: 2 * 6 * 16 KB = 192 KB
-constexpr int TC_NT = 128;
+constexpr int TC_MAX_KB = 6;    // A resident + 2 B stages: 6*16 KB + 2*6*8 KB = 192 KB
+constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, each half of a tile's columns
+constexpr int TC_NT = 64 + TC_EPI_WARPS * 32;
 constexpr int RS_NT = 256;
 
 __host__ __device__ inline int tc_kpad(int dim) { return (3 * dim + TC_KB - 1) / TC_KB * TC_KB; }
@@ -64,83 +70,191 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, long long n, int 
     }
 }
 
+// Warp roles of the persistent GEMM CTA (320 threads):
+//   warp 0, lane 0: TMA producer (A once, then B tiles through a 2-stage ring)
+//   warp 1, lane 0: MMA issuer (and warp 1 owns the TMEM allocation)
+//   warps 2..9:     epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (its 32
+//                   queries) and columns 32*((w-2)/4) .. +31 of each tile
+// TMEM holds two 128 x 64 fp32 accumulators, so the epilogue of tile i runs
+// while the MMAs of tile i+1 fill the other one.
+struct GemmArgs {
+    int kt;              // 64-wide K blocks
+    long long q0;        // first query row of this launch (row of the A tensor map)
+    int nq;              // query rows of this launch
+    int ncols;           // centroid columns [0, ncols)
+    int tiles_per_cta;   // 64-column tiles per CTA (blockIdx.y picks the run)
+    const float* qn;     // |q|^2, indexed by q0 + row
+    const float* cn;     // |c|^2
+    uint32_t* out;       // GEMM_MATRIX: order key of d~ at out[row * ldo + col]
+    long long ldo;
+    const float* tq;     // GEMM_FILTER: per-query bound
+    int cap;             // GEMM_FILTER: capacity of each (query, CTA column run) segment
+    int* cnt;            // GEMM_FILTER: [nq][gridDim.y * 2] appended counts (may exceed cap)
+    uint32_t* list_k;    // [nq][gridDim.y * 2][cap] keys of d~ (one segment per column half)
+    int32_t* list_i;     // [nq][gridDim.y * 2][cap] centroid ids
+    int* err;
+};
+
+enum { GEMM_MATRIX = 0, GEMM_FILTER = 1 };
+
+template <int MODE>
 __global__ void __launch_bounds__(TC_NT, 1)
-    coarse_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, int kt,
-                       long long q0, int nq_chunk, int nlist, const float* __restrict__ qn,
-                       const float* __restrict__ cn, float* __restrict__ out, long long ldo, int* err) {
+    coarse_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                       const GemmArgs g) {
     extern __shared__ __align__(1024) unsigned char dsmem[];
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(8) uint64_t a_full, b_full[2], b_empty[2], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int s_fail;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // 1024-byte aligned operand area: A blocks then B blocks, 16 KB each
+    const int ntiles = (g.ncols + TC_N - 1) / TC_N;
+    const int tile0 = blockIdx.y * g.tiles_per_cta;
+    const int nt = min(ntiles, tile0 + g.tiles_per_cta) - tile0;
+    if (nt <= 0) return;  // uniform for the whole CTA
+    constexpr int A_KB = TC_M * TC_KB * 2;  // 16 KB per K block
+    constexpr int B_KB = TC_N * TC_KB * 2;  // 8 KB per K block
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
     unsigned char* sa = base;
-    unsigned char* sb = base + kt * (TC_TILE * TC_KB * 2);
-    const int m0 = blockIdx.x * TC_TILE;  // row inside the chunk
-    const int n0 = blockIdx.y * TC_TILE;
+    unsigned char* sb = base + g.kt * A_KB;
+    const int stage_bytes = g.kt * B_KB;
+    const int m0 = blockIdx.x * TC_M;
 
     if (tid == 0) {
         s_fail = 0;
-        tc::mbar_init(&bars[0], 1);
-        tc::mbar_init(&bars[1], 1);
+        tc::mbar_init(&a_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&b_full[i], 1);
+            tc::mbar_init(&b_empty[i], 1);
+            tc::mbar_init(&acc_full[i], 1);
+            tc::mbar_init(&acc_empty[i], TC_EPI_WARPS * 32);
+        }
         tc::fence_mbar_init();
     }
-    if (warp == 0) {
-        tc::tmem_alloc(&tmem_slot, TC_TILE);
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_slot, 2 * TC_N);
         tc::tmem_relinquish();
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t taddr = tmem_slot;
+    volatile int* fail = &s_fail;
 
-    if (tid == 0) {
-        tc::mbar_arrive_expect_tx(&bars[0], (uint32_t)(2 * kt * TC_TILE * TC_KB * 2));
-        for (int k = 0; k < kt; ++k) {
-            tc::tma_load_2d(sa + k * (TC_TILE * TC_KB * 2), &ta, &bars[0], k * TC_KB, (int)(q0 + m0));
-            tc::tma_load_2d(sb + k * (TC_TILE * TC_KB * 2), &tb, &bars[0], k * TC_KB, n0);
-        }
-        if (tc::mbar_wait(&bars[0], 0)) {
-            constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_TILE, TC_TILE);
-            for (int k = 0; k < kt; ++k) {
-                const uint64_t da = tc::desc_kmajor_sw128(sa + k * (TC_TILE * TC_KB * 2));
-                const uint64_t db = tc::desc_kmajor_sw128(sb + k * (TC_TILE * TC_KB * 2));
-#pragma unroll
-                for (int kk = 0; kk < TC_KB / 16; ++kk)  // K = 16 per MMA: +32 bytes in the swizzle row
-                    tc::umma_bf16(taddr, da + 2 * kk, db + 2 * kk, idesc, (k | kk) != 0);
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            tc::mbar_arrive_expect_tx(&a_full, (uint32_t)(g.kt * A_KB));
+            for (int k = 0; k < g.kt; ++k)
+                tc::tma_load_2d(sa + k * A_KB, &ta, &a_full, k * TC_KB, (int)(g.q0 + m0));
+            for (int i = 0; i < nt; ++i) {
+                const int s = i & 1;
+                if (!tc::mbar_wait_or_fail(&b_empty[s], ((i >> 1) & 1) ^ 1, fail)) break;
+                tc::mbar_arrive_expect_tx(&b_full[s], (uint32_t)stage_bytes);
+                const int col0 = (tile0 + i) * TC_N;
+                for (int k = 0; k < g.kt; ++k)
+                    tc::tma_load_2d(sb + s * stage_bytes + k * B_KB, &tb, &b_full[s], k * TC_KB, col0);
             }
-            tc::umma_commit(&bars[1]);
-        } else {
-            s_fail = 1;
         }
-    }
-    __syncthreads();
-    // block-uniform: the TMEM loads below are .sync.aligned
-    const bool ok = __syncthreads_and(!s_fail && tc::mbar_wait(&bars[1], 0));
-    tc::fence_after_sync();
-    if (ok) {
-        const int row = m0 + warp * 32 + lane;
-        const float qnr = row < nq_chunk ? qn[q0 + row] : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < TC_TILE / 32; ++c) {
+    } else if (warp == 1) {
+        if (lane == 0 && tc::mbar_wait_or_fail(&a_full, 0, fail)) {  // ---- MMA issuer
+            constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_M, TC_N);
+            for (int i = 0; i < nt; ++i) {
+                const int s = i & 1, acc = i & 1, ph = (i >> 1) & 1;
+                if (!tc::mbar_wait_or_fail(&b_full[s], ph, fail)) break;
+                if (!tc::mbar_wait_or_fail(&acc_empty[acc], ph ^ 1, fail)) break;
+                tc::fence_after_sync();
+                for (int k = 0; k < g.kt; ++k) {
+                    const uint64_t da = tc::desc_kmajor_sw128(sa + k * A_KB);
+                    const uint64_t db = tc::desc_kmajor_sw128(sb + s * stage_bytes + k * B_KB);
+#pragma unroll
+                    for (int kk = 0; kk < TC_KB / 16; ++kk)
+                        tc::umma_bf16(taddr + (uint32_t)(acc * TC_N), da + 2 * kk, db + 2 * kk, idesc,
+                                      (k | kk) != 0);
+                }
+                tc::umma_commit(&b_empty[s]);    // the B stage may be refilled once these MMAs finish
+                tc::umma_commit(&acc_full[acc]);  // and the accumulator is ready for the epilogue
+            }
+        }
+    } else {  // ---- epilogue warps 2..9
+        const int q4 = warp & 3;
+        const int half = (warp - 2) >> 2;  // which 32 columns of each tile
+        const int row = m0 + q4 * 32 + lane;
+        const bool valid = row < g.nq;
+        const long long qg = g.q0 + row;
+        const float qnr = valid ? g.qn[qg] : 0.0f;
+        const float bound = (MODE == GEMM_FILTER && valid) ? g.tq[qg] : 0.0f;
+        // each (query, column half) belongs to exactly one thread: its segment needs no atomics
+        const long long seg = ((qg * gridDim.y + blockIdx.y) * 2 + half) * (long long)g.cap;
+        int n = 0;
+        for (int i = 0; i < nt; ++i) {
+            const int acc = i & 1, ph = (i >> 1) & 1;
+            if (!__all_sync(0xffffffffu, tc::mbar_wait_or_fail(&acc_full[acc], ph, fail))) break;
+            tc::fence_after_sync();
             float v[32];
-            tc::tmem_ld_32x32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
-            if (row < nq_chunk) {
-                float* o = out + (long long)row * ldo + n0 + c * 32;
+            tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + half * 32), v);
+            tc::fence_before_sync();
+            tc::mbar_arrive(&acc_empty[acc]);
+            if (!valid) continue;
+            const int col0 = (tile0 + i) * TC_N + half * 32;
+            // all column norms of the chunk first, so no load waits behind a store
+            float c[32];
+            if (col0 + 32 <= g.ncols) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(g.cn + col0 + j));
+                    c[j] = c4.x;
+                    c[j + 1] = c4.y;
+                    c[j + 2] = c4.z;
+                    c[j + 3] = c4.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) c[j] = (col0 + j < g.ncols) ? __ldg(g.cn + col0 + j) : 0.0f;
+            }
+            const int ncol = min(32, g.ncols - col0);
+            if (MODE == GEMM_MATRIX) {
+                uint32_t* o = g.out + (long long)row * g.ldo + col0;
+                if (ncol == 32 && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        uint4 k4;
+                        k4.x = f2key(qnr + c[j] - 2.0f * v[j]);
+                        k4.y = f2key(qnr + c[j + 1] - 2.0f * v[j + 1]);
+                        k4.z = f2key(qnr + c[j + 2] - 2.0f * v[j + 2]);
+                        k4.w = f2key(qnr + c[j + 3] - 2.0f * v[j + 3]);
+                        *reinterpret_cast<uint4*>(o + j) = k4;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
+                }
+            } else {
+                unsigned pass = 0;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int col = n0 + c * 32 + j;
-                    if (col < nlist) o[j] = qnr + cn[col] - 2.0f * v[j];
+                    v[j] = qnr + c[j] - 2.0f * v[j];
+                    pass |= (j < ncol && v[j] <= bound) ? (1u << j) : 0u;
+                }
+                if (pass) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (pass & (1u << j)) {
+                            if (n < g.cap) {
+                                g.list_k[seg + n] = f2key(v[j]);
+                                g.list_i[seg + n] = col0 + j;
+                            }
+                            ++n;
+                        }
+                    }
                 }
             }
         }
+        if (MODE == GEMM_FILTER && valid) g.cnt[(qg * gridDim.y + blockIdx.y) * 2 + half] = n;
     }
-    if (!ok && tid == 0) atomicExch(err, 1);
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(taddr, TC_TILE);
+    if (warp == 1) tc::tmem_dealloc(taddr, 2 * TC_N);
+    if (tid == 0 && s_fail) atomicExch(g.err, 1);
 }
 
 __device__ __forceinline__ float l2_seq_dev(const float* __restrict__ a_smem, const float* __restrict__ b, int dim) {
@@ -168,80 +282,115 @@ __device__ __forceinline__ float l2_seq_dev(const float* __restrict__ a_smem, co
     return d;
 }
 
-// One CTA per query of the chunk: exact rescoring of the S candidates and the
-// certificate; exact fallback over all centroids when it fails.
-__global__ void __launch_bounds__(RS_NT) coarse_rescore_kernel(
-    const float* __restrict__ centroids, int nlist, int dim, const float* __restrict__ queries, long long q0,
-    const int32_t* __restrict__ cand_i, const float* __restrict__ cand_d, int S, int P,
-    const float* __restrict__ qn, const unsigned* __restrict__ max_cn_bits, const int* __restrict__ err,
-    uint32_t* __restrict__ row_keys, long long ldk, uint32_t* __restrict__ out_ids, float* __restrict__ out_d,
-    int* __restrict__ n_fallback) {
+constexpr int FIN_WARPS = 4;      // queries per finish CTA (one warp each)
+constexpr int FIN_TOT = 2048;     // appended candidates a warp gathers per query
+constexpr int TC_MAX_S = 512;     // superset bound of the tensor-core path
+
+// Warp per query: the bound for pass 1 is the S-th smallest key of the query's
+// prefix row (exact order statistic of a subset, so an upper bound on the
+// S-th smallest over all centroids).
+__global__ void __launch_bounds__(256) coarse_bound_kernel(const uint32_t* __restrict__ M0, int NS, long long ldm,
+                                                           int nq, int S, float* __restrict__ tq) {
+    __shared__ uint32_t hist[8][256];
+    const int w = threadIdx.x >> 5;
+    const int q = blockIdx.x * 8 + w;
+    if (q >= nq) return;
+    uint32_t kth;
+    int n_less;
+    warp_radix_select(M0 + (size_t)q * ldm, NS, S, hist[w], kth, n_less);
+    if ((threadIdx.x & 31) == 0) tq[q] = key2f(kth);
+}
+
+struct FinishSmem {
+    int dim4, spow;
+    __host__ __device__ int per_warp_bytes() const {
+        return dim4 * 4 + 256 * 4 + FIN_TOT * 8 + spow * 8 * 2;
+    }
+};
+
+// Warp per query: gather the appended (key, id) of every column run, keep the
+// S smallest keys, rescore them exactly, sort by (distance, id), certify;
+// otherwise rescore all centroids exactly through the warp's scratch row.
+__global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
+    const float* __restrict__ centroids, int nlist, int dim, const float* __restrict__ queries, int nq,
+    const int* __restrict__ cnt, int gy, const uint32_t* __restrict__ list_k, const int32_t* __restrict__ list_i,
+    int cap, int S, int P, const float* __restrict__ qn, const unsigned* __restrict__ max_cn_bits,
+    const int* __restrict__ err, uint32_t* __restrict__ fb, uint32_t* __restrict__ out_ids,
+    float* __restrict__ out_d, int* __restrict__ n_fallback) {
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ uint32_t hist[256];
-    __shared__ uint32_t sb[2];
-    __shared__ int warp[RS_NT / 32];
-    const int row = blockIdx.x;
-    const long long q = q0 + row;
-    const int tid = threadIdx.x;
-    const int dim4 = (dim + 3) / 4 * 4;
-    float* sq = reinterpret_cast<float*>(smem);
-    unsigned long long* sk = reinterpret_cast<unsigned long long*>(smem + dim4 * 4 + (dim4 * 4 % 8));
-    for (int t = tid; t < dim; t += RS_NT) sq[t] = queries[q * dim + t];
-    __syncthreads();
-    const int spow = next_pow2(S > P ? S : P);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * FIN_WARPS + w;
+    if (q >= nq) return;
+    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(S > P ? S : P)};
+    unsigned char* mine = smem + (size_t)w * L.per_warp_bytes();
+    float* sq = reinterpret_cast<float*>(mine);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(mine + L.dim4 * 4);
+    uint32_t* wk = hist + 256;
+    int32_t* wi = reinterpret_cast<int32_t*>(wk + FIN_TOT);
+    unsigned long long* sx = reinterpret_cast<unsigned long long*>(wi + FIN_TOT);
+    unsigned long long* ex = sx + L.spow;
+    for (int t = lane; t < dim; t += 32) sq[t] = queries[(size_t)q * dim + t];
+
+    // gather the column runs' segments
+    int total = 0;
+    bool over = false;
+    for (int y = 0; y < gy; ++y) {
+        const int c = cnt[(size_t)q * gy + y];
+        over |= c > cap;
+        const int take = min(c, cap);
+        if (total + take > FIN_TOT) {
+            over = true;
+            break;
+        }
+        const size_t seg = ((size_t)q * gy + y) * cap;
+        for (int i = lane; i < take; i += 32) {
+            wk[total + i] = list_k[seg + i];
+            wi[total + i] = list_i[seg + i];
+        }
+        total += take;
+    }
+    __syncwarp();
     bool certified = false;
-    if (*err == 0) {
-        for (int i = tid; i < spow; i += RS_NT) {
+    if (*err == 0 && !over && total >= S) {
+        uint32_t kth;
+        int n_less;
+        warp_radix_select(wk, total, S, hist, kth, n_less);
+        warp_collect_smallest(wk, total, S, kth, n_less, sx, [&](int i) { return wi[i]; });
+        for (int i = lane; i < L.spow; i += 32) {
             unsigned long long key = ~0ull;
             if (i < S) {
-                const int cid = cand_i[(long long)row * S + i];
-                if (cid >= 0 && cid < nlist)
-                    key = ((unsigned long long)f2key(l2_seq_dev(sq, centroids + (size_t)cid * dim, dim)) << 32) |
-                          (unsigned)cid;
+                const uint32_t cid = (uint32_t)(sx[i] & 0xffffffffu);
+                key = ((unsigned long long)f2key(l2_seq_dev(sq, centroids + (size_t)cid * dim, dim)) << 32) | cid;
             }
-            sk[i] = key;
+            ex[i] = key;
         }
-        __syncthreads();
-        block_bitonic_sort<RS_NT>(sk, spow);
-        const float dp = key2f((uint32_t)(sk[P - 1] >> 32));
-        const float T = cand_d[(long long)row * S + S - 1];
+        __syncwarp();
+        warp_bitonic_sort(ex, L.spow);
+        const float dp = key2f((uint32_t)(ex[P - 1] >> 32));
+        const float T = key2f(kth);
         const float qq = qn[q];
         const float cc = __uint_as_float(*max_cn_bits);
         const float E = 0x1p-12f * sqrtf(qq) * sqrtf(cc) + 0x1p-16f * (qq + cc);
         certified = (S >= nlist) || (dp < T - E);
     }
     if (!certified) {
-        uint32_t* rk = row_keys + (long long)row * ldk;
-        for (int c = tid; c < nlist; c += RS_NT) rk[c] = f2key(l2_seq_dev(sq, centroids + (size_t)c * dim, dim));
-        __syncthreads();
+        uint32_t* rk = fb + ((size_t)blockIdx.x * FIN_WARPS + w) * nlist;
+        for (int c = lane; c < nlist; c += 32) rk[c] = f2key(l2_seq_dev(sq, centroids + (size_t)c * dim, dim));
+        __syncwarp();
         uint32_t kth;
         int n_less;
-        block_radix_select<RS_NT>(rk, nlist, P, hist, sb, kth, n_less);
-        const int need_eq = P - n_less;
-        int eq_base = 0, out_base = 0;
-        for (int r0 = 0; r0 < nlist; r0 += RS_NT) {
-            const int c = r0 + tid;
-            const bool in = c < nlist;
-            const uint32_t key = in ? rk[c] : 0xffffffffu;
-            const int is_eq = (in && key == kth) ? 1 : 0;
-            int eq_tot, s_tot;
-            const int eq_pre = block_exclusive_scan<RS_NT>(is_eq, warp, eq_tot);
-            const bool sel = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
-            eq_base += eq_tot;
-            const int s_pre = block_exclusive_scan<RS_NT>(sel ? 1 : 0, warp, s_tot);
-            if (sel) sk[out_base + s_pre] = ((unsigned long long)key << 32) | (unsigned)c;
-            out_base += s_tot;
-        }
+        warp_radix_select(rk, nlist, P, hist, kth, n_less);
+        warp_collect_smallest(rk, nlist, P, kth, n_less, ex, [](int i) { return i; });
         const int ppow = next_pow2(P);
-        for (int i = P + tid; i < ppow; i += RS_NT) sk[i] = ~0ull;
-        __syncthreads();
-        block_bitonic_sort<RS_NT>(sk, ppow);
-        if (tid == 0) atomicAdd(n_fallback, 1);
+        for (int i = P + lane; i < ppow; i += 32) ex[i] = ~0ull;
+        __syncwarp();
+        warp_bitonic_sort(ex, ppow);
+        if (lane == 0) atomicAdd(n_fallback, 1);
     }
-    for (int j = tid; j < P; j += RS_NT) {
-        const unsigned long long e = sk[j];
-        out_ids[q * P + j] = (uint32_t)(e & 0xffffffffu);
-        out_d[q * P + j] = key2f((uint32_t)(e >> 32));
+    for (int j = lane; j < P; j += 32) {
+        const unsigned long long e = ex[j];
+        out_ids[(size_t)q * P + j] = (uint32_t)(e & 0xffffffffu);
+        out_d[(size_t)q * P + j] = key2f((uint32_t)(e >> 32));
     }
 }
 
@@ -263,13 +412,13 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-static int make_map(CUtensorMap* m, const void* base, long long rows, int kpad) {
+static int make_map(CUtensorMap* m, const void* base, long long rows, int kpad, int box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(FG_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
     if (!aligned(base, 16)) return fail(FG_ERR_INVALID_ARG, "TMA operand not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)kpad, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)kpad * 2};
-    cuuint32_t box[2] = {TC_KB, TC_TILE};
+    cuuint32_t box[2] = {TC_KB, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -278,53 +427,82 @@ static int make_map(CUtensorMap* m, const void* base, long long rows, int kpad) 
     return FG_OK;
 }
 
-bool coarse_tc_supported(int dim) { return tc_kpad(dim) / TC_KB <= TC_MAX_KB; }
-
-static int superset(int P, int nlist) { return std::min(nlist, std::max(2 * P, P + 32)); }
-
-static long long tc_chunk_rows(long long nq, int nlist) {
-    long long r = std::max<long long>(128, (256ll << 20) / ((long long)nlist * 4));
-    r = r / 128 * 128;
-    return std::min(nq, r);
+bool coarse_tc_supported(int dim, int P) {
+    const int S = std::max(2 * P, P + 32);
+    return tc_kpad(dim) / TC_KB <= TC_MAX_KB && S <= TC_MAX_S;
 }
+
+namespace {
+struct CoarsePlan {
+    int S;       // exactly rescored superset
+    int NS;      // prefix of centroids whose S-th smallest d~ bounds the S-th over all
+    int cap;     // capacity of one (query, column run) segment
+    int gy1;     // column runs of pass 1
+    int tpc1;    // 64-column tiles per run
+    int fin_cta;
+};
+
+// column runs so that the grid covers the SMs at least once
+void col_split(int mtiles, int ntiles, int& gy, int& tpc) {
+    const int want = std::max(1, std::min(ntiles, (148 + mtiles - 1) / mtiles));
+    tpc = (ntiles + want - 1) / want;
+    gy = (ntiles + tpc - 1) / tpc;
+}
+
+CoarsePlan coarse_plan(long long nq, int nlist, int P) {
+    CoarsePlan c;
+    c.S = std::min(nlist, std::max(2 * P, P + 32));
+    int ns = std::max({1024, 8 * c.S, nlist / 8});
+    ns = (ns + TC_N - 1) / TC_N * TC_N;
+    c.NS = std::min(nlist, std::min(ns, 8192));
+    const long long expect = (long long)c.S * nlist / c.NS;
+    const int mtiles = (int)((std::max(nq, 1ll) + TC_M - 1) / TC_M);
+    col_split(mtiles, (nlist + TC_N - 1) / TC_N, c.gy1, c.tpc1);
+    c.cap = (int)std::min<long long>(FIN_TOT, std::max<long long>(4 * expect, c.S + 256));
+    c.cap = std::min(c.cap, c.tpc1 * TC_N / 2);
+    c.fin_cta = (int)((std::max(nq, 1ll) + FIN_WARPS - 1) / FIN_WARPS);
+    return c;
+}
+}  // namespace
 
 size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P) {
     const int kpad = tc_kpad(dim);
-    const int S = superset(P, nlist);
-    const long long rows = tc_chunk_rows(std::max(nq, 1ll), nlist);
+    const CoarsePlan c = coarse_plan(nq, nlist, P);
     size_t b = 0;
-    b += round_up((size_t)round_up(nq, TC_TILE) * kpad * 2, 256) + round_up((size_t)round_up(nlist, TC_TILE) * kpad * 2, 256);
-    b += round_up((size_t)nq * 4, 256) + round_up((size_t)nlist * 4, 256) + 256 * 3;
-    b += round_up((size_t)rows * nlist * 4, 256);
-    b += round_up((size_t)rows * S * 4, 256) * 2;
-    b += rows_topk_stage_bytes(rows, nlist, S);
-    return b + 2048;
+    b += round_up(round_up((size_t)nq, TC_TILE) * kpad * 2, 256) + round_up(round_up((size_t)nlist, TC_TILE) * kpad * 2, 256);
+    b += round_up((size_t)nq * 4, 256) * 2 + round_up((size_t)nlist * 4, 256) + 256 * 3;
+    b += round_up((size_t)nq * round_up(c.NS, 4) * 4, 256);     // prefix keys
+    b += round_up((size_t)nq * c.gy1 * 2 * 4, 256);             // segment counts
+    b += round_up((size_t)nq * c.gy1 * 2 * c.cap * 4, 256) * 2; // segments
+    b += round_up((size_t)c.fin_cta * FIN_WARPS * nlist * 4, 256);  // fallback rows
+    return b + 4096;
 }
 
 int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
               uint32_t* out_ids, float* out_d, void* ws, size_t ws_bytes, cudaStream_t s, int* n_fallback_host) {
     const int kpad = tc_kpad(dim);
     const int kt = kpad / TC_KB;
-    if (kt > TC_MAX_KB) return fail(FG_ERR_UNSUPPORTED, "tensor-core coarse path needs 3*dim <= 384");
-    const int S = superset(P, nlist);
-    const long long rows = tc_chunk_rows(nq, nlist);
-    // operands padded to whole 128-row tiles (zero rows), so no TMA box exceeds its tensor
+    if (!coarse_tc_supported(dim, P))
+        return fail(FG_ERR_UNSUPPORTED, "tensor-core coarse path needs 3*dim <= 384 and top_m <= 256");
+    if (nq > 0x7fffffffll) return fail(FG_ERR_INVALID_ARG, "too many queries");
+    const CoarsePlan c = coarse_plan(nq, nlist, P);
     const long long nq_pad = (long long)round_up((size_t)nq, TC_TILE);
     const long long nl_pad = (long long)round_up((size_t)nlist, TC_TILE);
     Carve cv(ws, ws_bytes);
     __nv_bfloat16* A = cv.take<__nv_bfloat16>((size_t)nq_pad * kpad);
     __nv_bfloat16* B = cv.take<__nv_bfloat16>((size_t)nl_pad * kpad);
     float* qn = cv.take<float>((size_t)nq);
+    float* tq = cv.take<float>((size_t)nq);
     float* cn = cv.take<float>((size_t)nlist);
     unsigned* maxc = cv.take<unsigned>(4);
     int* err = cv.take<int>(4);
     int* nfb = cv.take<int>(4);
-    float* M = cv.take<float>((size_t)rows * nlist);
-    int32_t* ci = cv.take<int32_t>((size_t)rows * S);
-    float* cd = cv.take<float>((size_t)rows * S);
-    const size_t stage = rows_topk_stage_bytes(rows, nlist, S);
-    float* sv = stage ? cv.take<float>(stage / 8) : nullptr;
-    int32_t* si = stage ? cv.take<int32_t>(stage / 8) : nullptr;
+    const long long ldm = (long long)round_up((size_t)c.NS, 4);
+    uint32_t* M0 = cv.take<uint32_t>((size_t)nq * ldm);
+    int* cnt = cv.take<int>((size_t)nq * c.gy1 * 2);
+    uint32_t* lk = cv.take<uint32_t>((size_t)nq * c.gy1 * 2 * c.cap);
+    int32_t* li = cv.take<int32_t>((size_t)nq * c.gy1 * 2 * c.cap);
+    uint32_t* fb = cv.take<uint32_t>((size_t)c.fin_cta * FIN_WARPS * nlist);
     if (!cv.ok()) return fail(FG_ERR_WORKSPACE, "coarse workspace too small (%zu < %zu)", ws_bytes,
                               coarse_tc_workspace(nq, nlist, dim, P));
     FG_CUDA_TRY(cudaMemsetAsync(maxc, 0, 4, s));
@@ -339,24 +517,54 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     split_bf16_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(queries, nq, dim, kpad, 0, A, qn, nullptr);
     if ((rc = check_launch("split_bf16_kernel(queries)"))) return rc;
     CUtensorMap ta, tb;
-    if ((rc = make_map(&ta, A, nq_pad, kpad))) return rc;
-    if ((rc = make_map(&tb, B, nl_pad, kpad))) return rc;
-    const int smem = 1024 + 2 * kt * TC_TILE * TC_KB * 2;
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int spow = next_pow2(std::max(S, P));
-    const int rs_smem = ((dim + 3) / 4 * 4) * 4 + 8 + spow * 8;
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rs_smem));
-    for (long long q0 = 0; q0 < nq; q0 += rows) {
-        const int r = (int)std::min(rows, nq - q0);
-        dim3 grid((unsigned)((r + TC_TILE - 1) / TC_TILE), (unsigned)((nlist + TC_TILE - 1) / TC_TILE));
-        coarse_gemm_kernel<<<grid, TC_NT, smem, s>>>(ta, tb, kt, q0, r, nlist, qn, cn, M, nlist, err);
-        if ((rc = check_launch("coarse_gemm_kernel"))) return rc;
-        if ((rc = rows_topk(M, nlist, r, nlist, S, ci, cd, S, sv, si, s))) return rc;
-        coarse_rescore_kernel<<<r, RS_NT, rs_smem, s>>>(centroids, nlist, dim, queries, q0, ci, cd, S, P, qn, maxc,
-                                                        err, reinterpret_cast<uint32_t*>(M), nlist, out_ids, out_d,
-                                                        nfb);
-        if ((rc = check_launch("coarse_rescore_kernel"))) return rc;
-    }
+    if ((rc = make_map(&ta, A, nq_pad, kpad, TC_M))) return rc;
+    if ((rc = make_map(&tb, B, nl_pad, kpad, TC_N))) return rc;
+    const int smem = 1024 + kt * TC_M * TC_KB * 2 + 2 * kt * TC_N * TC_KB * 2;
+    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_MATRIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+    const int mtiles = (int)((nq + TC_M - 1) / TC_M);
+
+    // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
+    GemmArgs g{};
+    g.kt = kt;
+    g.q0 = 0;
+    g.nq = (int)nq;
+    g.qn = qn;
+    g.cn = cn;
+    g.err = err;
+    g.ncols = c.NS;
+    int gy0, tpc0;
+    col_split(mtiles, (c.NS + TC_N - 1) / TC_N, gy0, tpc0);
+    g.tiles_per_cta = tpc0;
+    g.out = M0;
+    g.ldo = ldm;
+    coarse_gemm_kernel<GEMM_MATRIX><<<dim3(mtiles, gy0), TC_NT, smem, s>>>(ta, tb, g);
+    if ((rc = check_launch("coarse_gemm_kernel(prefix)"))) return rc;
+    coarse_bound_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(M0, c.NS, ldm, (int)nq, c.S, tq);
+    if ((rc = check_launch("coarse_bound_kernel"))) return rc;
+
+    // pass 1: every centroid; each query row appends those within its bound
+    g.ncols = nlist;
+    g.tiles_per_cta = c.tpc1;
+    g.out = nullptr;
+    g.tq = tq;
+    g.cap = c.cap;
+    g.cnt = cnt;
+    g.list_k = lk;
+    g.list_i = li;
+    coarse_gemm_kernel<GEMM_FILTER><<<dim3(mtiles, c.gy1), TC_NT, smem, s>>>(ta, tb, g);
+    if ((rc = check_launch("coarse_gemm_kernel(filter)"))) return rc;
+
+    // pass 2: select, rescore exactly, certify (or fall back)
+    const FinishSmem FL{(dim + 3) / 4 * 4, next_pow2(std::max(c.S, P))};
+    const int fin_smem = FIN_WARPS * FL.per_warp_bytes();
+    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem));
+    coarse_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fin_smem, s>>>(centroids, nlist, dim, queries, (int)nq, cnt,
+                                                                     c.gy1 * 2, lk, li, c.cap, c.S, P, qn, maxc, err, fb,
+                                                                     out_ids, out_d, nfb);
+    if ((rc = check_launch("coarse_finish_kernel"))) return rc;
     if (n_fallback_host) {
         FG_CUDA_TRY(cudaMemcpyAsync(n_fallback_host, nfb, sizeof(int), cudaMemcpyDeviceToHost, s));
         FG_CUDA_TRY(cudaStreamSynchronize(s));

@@ -164,6 +164,113 @@ __device__ void block_bitonic_sort(unsigned long long* s, int n_pow2) {
     }
 }
 
+// ---- warp-level selection (no block barriers) -----------------------------------
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// k-th smallest (1-based, 1 <= k <= n) of n uint32 keys, by one warp.
+// `hist`: 256 uint32 of shared memory owned by this warp.
+__device__ inline void warp_radix_select(const uint32_t* keys, int n, int k, uint32_t* hist, uint32_t& kth,
+                                         int& n_less) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, mask = 0, kk = (uint32_t)k, less = 0;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = lane; i < 256; i += 32) hist[i] = 0;
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            const uint32_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        uint32_t c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            c[j] = hist[lane * 8 + j];
+            sum += c[j];
+        }
+        uint32_t incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - sum;
+        const bool mine = excl < kk && kk <= incl;
+        uint32_t b = 0, below = 0;
+        if (mine) {
+            uint32_t run = excl;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (run + c[j] >= kk) {
+                    b = (uint32_t)(lane * 8 + j);
+                    below = run;
+                    break;
+                }
+                run += c[j];
+            }
+        }
+        const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        b = __shfl_sync(0xffffffffu, b, src);
+        below = __shfl_sync(0xffffffffu, below, src);
+        prefix |= b << shift;
+        mask |= 255u << shift;
+        kk -= below;
+        less += below;
+        __syncwarp();
+    }
+    kth = prefix;
+    n_less = (int)less;
+}
+
+// The k smallest keys (ties: lower index first), written in index order as
+// (key << 32 | payload(i)) to dst[0..k).  kth/n_less from warp_radix_select.
+template <class Payload>
+__device__ inline void warp_collect_smallest(const uint32_t* keys, int n, int k, uint32_t kth, int n_less,
+                                             unsigned long long* dst, Payload payload) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = lanemask_lt();
+    const int need_eq = k - n_less;
+    int eq_base = 0, out = 0;
+    for (int c0 = 0; c0 < n; c0 += 32) {
+        const int i = c0 + lane;
+        const bool in = i < n;
+        const uint32_t key = in ? keys[i] : 0xffffffffu;
+        const bool eq = in && key == kth;
+        const unsigned eqb = __ballot_sync(0xffffffffu, eq);
+        const bool sel = in && (key < kth || (eq && eq_base + __popc(eqb & lt) < need_eq));
+        const unsigned sb = __ballot_sync(0xffffffffu, sel);
+        if (sel) dst[out + __popc(sb & lt)] = ((unsigned long long)key << 32) | (uint32_t)payload(i);
+        eq_base += __popc(eqb);
+        out += __popc(sb);
+    }
+    __syncwarp();
+}
+
+// Ascending bitonic sort of n_pow2 uint64 keys in shared memory by one warp.
+__device__ inline void warp_bitonic_sort(unsigned long long* s, int n_pow2) {
+    const int lane = threadIdx.x & 31;
+    for (int k = 2; k <= n_pow2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n_pow2; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = s[i], b = s[ixj];
+                    if ((a > b) == ((i & k) == 0)) {
+                        s[i] = b;
+                        s[ixj] = a;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
 __host__ __device__ inline int next_pow2(int x) {
     int p = 1;
     while (p < x) p <<= 1;

@@ -31,6 +31,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Bounded wait for the phase with the given parity; true once it completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = kWaitLimit) {
     const uint32_t a = smem_u32(bar);
@@ -127,6 +131,26 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(const void* smem) {
     d |= (uint64_t)1 << 46;               // descriptor version (sm_100)
     d |= (uint64_t)2 << 61;               // SWIZZLE_128B
     return d;
+}
+
+// Bounded wait that gives up early once another role of the CTA has failed
+// (`fail` is a shared flag); sets the flag when it runs out itself.
+__device__ __forceinline__ bool mbar_wait_or_fail(uint64_t* bar, uint32_t parity, volatile int* fail) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 1023u) == 1023u && *fail) return false;
+    }
+    *fail = 1;
+    return false;
 }
 
 // Instruction descriptor, kind::f16: bf16 x bf16 -> f32, both K-major.

@@ -111,6 +111,18 @@ def test_coarse_tc_fallback_on_ties(fg):
     assert nfb >= 32
 
 
+def test_coarse_tc_odd_shapes(fg):
+    """nlist and nq not multiples of the tiles, dim not a multiple of 64/3."""
+    rng = np.random.default_rng(11)
+    cen = rng.normal(size=(1001, 40)).astype(np.float32)
+    q = rng.normal(size=(333, 40)).astype(np.float32)
+    for top_m in (1, 7, 64):
+        ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
+        eids, ed = oracle.coarse(cen, q, top_m)
+        np.testing.assert_array_equal(_np(d), ed)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+
+
 def test_coarse_tc_many_lists_two_stage(fg):
     """nlist above one select segment (8192): stage-2 merge in the superset select."""
     rng = np.random.default_rng(10)
