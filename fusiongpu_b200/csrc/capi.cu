@@ -36,7 +36,7 @@ int check_launch(const char* what) {
 
 // implemented in the kernel files
 int batch_logic(const fg_ivfpq_view*, const float*, int, const uint32_t*, const float*, const fg_search_params*,
-                int32_t*, float*, int32_t*, int32_t*, cudaStream_t);
+                int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad);
 int rerank(const float*, int, int, const int32_t*, const int32_t*, const float*, long long, const fg_search_params*,
            int32_t*, float*, cudaStream_t);
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
@@ -183,7 +183,7 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                    const float* probe_dists, const fg_search_params* params, int32_t* top_ids, float* top_dists,
                    int32_t* top_counts, int32_t* candidate_counts, void* stream) {
     return batch_logic(index, queries, nq, probe_ids, probe_dists, params, top_ids, top_dists, top_counts,
-                       candidate_counts, as_stream(stream));
+                       candidate_counts, as_stream(stream), true);
 }
 
 int fg_rerank(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids, const int32_t* top_counts,
@@ -226,7 +226,8 @@ int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, cons
     rc = coarse(index->centroids, index->nlist, index->dim, queries, nq, params->top_m, pids, pd,
                 static_cast<char*>(ws) + used, ws_bytes - used, s);
     if (rc) return rc;
-    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s);
+    // the rerank reads only the first top_counts[q] entries: skip the padding
+    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false);
     if (rc) return rc;
     return rerank(queries, nq, index->dim, tid, tc, base, nbase, params, out_ids, out_dists, s);
 }

@@ -33,17 +33,63 @@ struct RerankArgs {
     float* out_dists;
 };
 
+// Exact squared L2 in dimension order (fmaf, as nvcc contracts the reference's
+// `local_d += diff*diff`), eight 16-byte loads in flight.
+__device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const float* __restrict__ v, int dim) {
+    float d = 0.0f;
+    if ((dim & 3) == 0) {
+        const float4* v4 = reinterpret_cast<const float4*>(v);
+        const int n4 = dim >> 2;
+        int t = 0;
+        for (; t + 8 <= n4; t += 8) {
+            float4 x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = __ldg(v4 + t + u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float4 q = *reinterpret_cast<const float4*>(sq + 4 * (t + u));
+                float df = q.x - x[u].x;
+                d = fmaf(df, df, d);
+                df = q.y - x[u].y;
+                d = fmaf(df, df, d);
+                df = q.z - x[u].z;
+                d = fmaf(df, df, d);
+                df = q.w - x[u].w;
+                d = fmaf(df, df, d);
+            }
+        }
+        for (; t < n4; ++t) {
+            const float4 x = __ldg(v4 + t);
+            const float4 q = *reinterpret_cast<const float4*>(sq + 4 * t);
+            float df = q.x - x.x;
+            d = fmaf(df, df, d);
+            df = q.y - x.y;
+            d = fmaf(df, df, d);
+            df = q.z - x.z;
+            d = fmaf(df, df, d);
+            df = q.w - x.w;
+            d = fmaf(df, df, d);
+        }
+    } else {
+        for (int t = 0; t < dim; ++t) {
+            const float df = sq[t] - __ldg(v + t);
+            d = fmaf(df, df, d);
+        }
+    }
+    return d;
+}
+
 __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp[RR_NT / 32];
     __shared__ int s_stab;
     float* s_q = reinterpret_cast<float*>(smem);
     const int dim4 = (a.dim + 3) / 4 * 4;
-    float* fd = s_q + dim4;          // running top-k distances
+    float* fd = s_q + dim4;          // running top-k distances (ascending)
     int32_t* fid = reinterpret_cast<int32_t*>(fd + a.k);
-    float* wd = reinterpret_cast<float*>(fid + a.k);  // window [nw]
-    int32_t* wi = reinterpret_cast<int32_t*>(wd + a.nw);
-    float* nd = reinterpret_cast<float*>(wi + a.nw);  // new top-k [k]
+    float* wd = reinterpret_cast<float*>(fid + a.k);  // this mini-batch's candidates
+    int32_t* wi = reinterpret_cast<int32_t*>(wd + a.mb);
+    float* nd = reinterpret_cast<float*>(wi + a.mb);  // merged top-k
     int32_t* ni = reinterpret_cast<int32_t*>(nd + a.k);
 
     const int q = blockIdx.x, tid = threadIdx.x, k = a.k;
@@ -56,63 +102,47 @@ __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
     if (tid == 0) s_stab = 0;
     __syncthreads();
     const int total = a.top_counts[q];
-    const bool vec4 = (a.dim % 4) == 0;
 
     for (int off = 0; off < a.rm; off += a.mb) {
         if (off >= total) break;
         const int eff = min(a.mb, total - off);
-        for (int w = tid; w < a.nw; w += RR_NT) {
-            if (w < k) {
-                wd[w] = fd[w];
-                wi[w] = fid[w];
-            } else {
-                const int i = w - k;
-                int32_t vid = -1;
-                float dist = FLT_MAX;
-                if (i < eff) {
-                    vid = a.top_ids[(size_t)q * a.rm + off + i];
-                    if (vid >= 0 && (long long)vid < a.nbase) {
-                        const float* v = a.base + (size_t)vid * a.dim;
-                        float d = 0.0f;
-                        if (vec4) {
-                            const float4* v4 = reinterpret_cast<const float4*>(v);
-                            for (int t = 0; t < a.dim / 4; ++t) {
-                                const float4 x = __ldg(v4 + t);
-                                const float4 qq = *reinterpret_cast<const float4*>(s_q + 4 * t);
-                                float df = qq.x - x.x;
-                                d = fmaf(df, df, d);
-                                df = qq.y - x.y;
-                                d = fmaf(df, df, d);
-                                df = qq.z - x.z;
-                                d = fmaf(df, df, d);
-                                df = qq.w - x.w;
-                                d = fmaf(df, df, d);
-                            }
-                        } else {
-                            for (int t = 0; t < a.dim; ++t) {
-                                const float df = s_q[t] - __ldg(v + t);
-                                d = fmaf(df, df, d);
-                            }
-                        }
-                        dist = d;
-                    }
-                }
-                wd[w] = dist;
-                wi[w] = vid;
-            }
+        // The window is [top-k ; mini-batch].  Its tail past eff is (FLT_MAX, -1)
+        // padding, which sorts after k earlier entries and can never enter the
+        // top-k, so only m = min(eff, nw - k) new entries take part.
+        const int m = min(eff, a.nw - k);
+        for (int i = tid; i < m; i += RR_NT) {
+            const int32_t vid = a.top_ids[(size_t)q * a.rm + off + i];
+            float dist = FLT_MAX;
+            if (vid >= 0 && (long long)vid < a.nbase) dist = exact_l2(s_q, a.base + (size_t)vid * a.dim, a.dim);
+            wd[i] = dist;
+            wi[i] = vid;
         }
         __syncthreads();
-        // stable rank by distance within the window; the first k survive
-        for (int w = tid; w < a.nw; w += RR_NT) {
-            const float d = wd[w];
-            int r = 0;
-            for (int u = 0; u < a.nw; ++u) {
+        // stable ranks: old entries come before new ones on equal distance
+        for (int j = tid; j < k; j += RR_NT) {  // old entry j (the top-k is sorted)
+            const float d = fd[j];
+            int r = j;
+            for (int u = 0; u < m; ++u) r += wd[u] < d;
+            if (r < k) {
+                nd[r] = d;
+                ni[r] = fid[j];
+            }
+        }
+        for (int i = tid; i < m; i += RR_NT) {  // new entry i
+            const float d = wd[i];
+            int lo = 0, hi = k;  // old entries with distance <= d
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (fd[mid] <= d) lo = mid + 1; else hi = mid;
+            }
+            int r = lo;
+            for (int u = 0; u < m; ++u) {
                 const float du = wd[u];
-                r += (du < d) || (du == d && u < w);
+                r += (du < d) || (du == d && u < i);
             }
             if (r < k) {
                 nd[r] = d;
-                ni[r] = wi[w];
+                ni[r] = wi[i];
             }
         }
         __syncthreads();
@@ -176,7 +206,7 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
     a.beta = p->beta;
     a.out_ids = out_ids;
     a.out_dists = out_dists;
-    const size_t smem = (size_t)((dim + 3) / 4 * 4) * 4 + (size_t)a.k * 16 + (size_t)a.nw * 8;
+    const size_t smem = (size_t)((dim + 3) / 4 * 4) * 4 + (size_t)a.k * 16 + (size_t)a.mb * 8;
     int dev = 0, smem_max = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));

@@ -25,7 +25,7 @@
 
 namespace fg {
 
-constexpr int SCAN_NT = 256;
+constexpr int SCAN_NT = 512;
 constexpr int REF_BLOCK = 128;      // blockDim of the reference's scan/gather kernels
 constexpr int REF_P1_CLAMP = 1024;  // 128 threads x 8 items (gpu_global.cu:343-346)
 
@@ -42,6 +42,7 @@ struct ScanArgs {
     int top_m, p1, limit_k;
     float coeff, prune_ratio;
     int rerank_m, rsel, ref_compat, lmax, cap, sort_n;
+    int write_pad;  // write (-1, FLT_MAX) / ref_compat zeros past each query's count
     int32_t* top_ids;
     float* top_dists;
     int32_t* top_counts;
@@ -108,6 +109,11 @@ __device__ __forceinline__ float sub_dist(const float* r, const float* c) {
         const float a4 = r1.x - c1.x, a5 = r1.y - c1.y, a6 = r1.z - c1.z, a7 = r1.w - c1.w;
         const float d = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, __fmul_rn(a3, a3))));
         return fmaf(a4, a4, fmaf(a5, a5, fmaf(a6, a6, fmaf(a7, a7, d))));
+    } else if constexpr (SD == 2) {
+        const float2 rv = *reinterpret_cast<const float2*>(r);
+        const float2 cv = __ldg(reinterpret_cast<const float2*>(c));
+        const float d0 = rv.x - cv.x, d1 = rv.y - cv.y;
+        return fmaf(d1, d1, fmaf(d0, d0, 0.0f));
     } else {
         float d = 0.0f;
 #pragma unroll
@@ -241,7 +247,7 @@ __device__ __forceinline__ void append(const ScanArgs& a, bool emit, uint32_t ke
 
 template <int M, int SD>
 __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) {
-    static_assert(SCAN_NT == 2 * REF_BLOCK, "phase-2 overflow ranks assume 256 threads");
+    static_assert(SCAN_NT % REF_BLOCK == 0, "phase-2 overflow ranks need whole 128-thread groups");
     extern __shared__ __align__(16) unsigned char smem[];
     constexpr bool RT = (M == 0);
     const int MM = RT ? a.pq_m : M;
@@ -377,8 +383,10 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
             }
             ms->passf[tid] = pass ? 1 : 0;
             __syncthreads();
-            const int rank = (tid < REF_BLOCK) ? ms->carry[tid]
-                                               : ms->carry[tid - REF_BLOCK] + ms->passf[tid - REF_BLOCK];
+            // rank among the passing vectors of the same reference thread (i mod 128)
+            const int t = tid % REF_BLOCK;
+            int rank = ms->carry[t];
+            for (int u = t; u < tid; u += REF_BLOCK) rank += ms->passf[u];
             const bool re = pass && rank < quota;
             int r_tot;
             (void)block_exclusive_scan<SCAN_NT>(re ? 1 : 0, ms->warp, r_tot);
@@ -386,7 +394,11 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
             const uint32_t key = f2key(d);
             const bool emit = re && key < ms->prune_key;
             append(a, emit, key, emit ? __ldg(a.vids + start + i) : 0, ckey, cid, ms);
-            if (tid < REF_BLOCK) ms->carry[tid] += ms->passf[tid] + ms->passf[tid + REF_BLOCK];
+            if (tid < REF_BLOCK) {
+                int add = 0;
+                for (int u = tid; u < SCAN_NT; u += REF_BLOCK) add += ms->passf[u];
+                ms->carry[tid] += add;
+            }
             __syncthreads();
         }
     }
@@ -403,7 +415,8 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
     const int count = ms->count;
     const int rm = a.rerank_m;
     const int ak = count < rm ? count : rm;
-    for (int p = tid; p < rm; p += SCAN_NT) {
+    const int pend = a.write_pad ? rm : (ak < rm ? ak : rm);
+    for (int p = tid; p < pend; p += SCAN_NT) {
         const size_t o = (size_t)q * rm + p;
         if (a.ref_compat && p >= REF_BLOCK) {
             // never written by the reference's 128-thread gather; modelled as
@@ -446,7 +459,8 @@ static ScanKernel pick_scan_kernel(int M, int SD) {
 
 int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uint32_t* probe_ids,
                 const float* probe_dists, const fg_search_params* p, int32_t* top_ids,
-                float* top_dists, int32_t* top_counts, int32_t* cand_counts, cudaStream_t stream) {
+                float* top_dists, int32_t* top_counts, int32_t* cand_counts, cudaStream_t stream,
+                bool write_pad) {
     FG_REQUIRE(ix && p, "null index or params");
     FG_REQUIRE(nq >= 0, "nq < 0");
     FG_REQUIRE(ix->dim > 0 && ix->pq_m > 0 && ix->dim % ix->pq_m == 0, "dim %d not divisible by pq_m %d",
@@ -499,6 +513,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.top_dists = top_dists;
     a.top_counts = top_counts;
     a.cand_counts = cand_counts;
+    a.write_pad = write_pad ? 1 : 0;
 
     int dev = 0, smem_max = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
