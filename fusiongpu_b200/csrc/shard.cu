@@ -1,0 +1,84 @@
+// shard.cu -- the exchange step of a list-sharded search across GPUs.
+//
+// Each GPU searches only the inverted lists it owns and returns its local
+// top-k per query (ascending by distance).  After one all-gather the per-GPU
+// lists sit side by side as [nshards][nq][k]; merge_topk_kernel keeps the k
+// smallest of the nshards*k candidates per query by (distance, global id).
+// The reference is single-GPU (search_pipeline.cu:560 cudaSetDevice(0)); this
+// is the sharded deployment of its search.
+#include "fg_common.cuh"
+
+namespace fg {
+
+constexpr int MG_WARPS = 4;  // queries per CTA, one warp each
+
+__global__ void __launch_bounds__(MG_WARPS * 32)
+    merge_topk_kernel(const float* __restrict__ dists, const int32_t* __restrict__ ids, int nshards, int nq, int k,
+                      int npow, int32_t* __restrict__ out_ids, float* __restrict__ out_d) {
+    extern __shared__ __align__(16) unsigned long long keys[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * MG_WARPS + w;
+    if (q >= nq) return;
+    unsigned long long* s = keys + (size_t)w * npow;
+    const int n = nshards * k;
+    for (int i = lane; i < npow; i += 32) {
+        unsigned long long key = ~0ull;
+        if (i < n) {
+            const int sh = i / k, j = i % k;
+            const size_t o = ((size_t)sh * nq + q) * k + j;
+            const int32_t id = ids[o];
+            // padding (-1) sorts after every real id at equal distance
+            key = ((unsigned long long)f2key(dists[o]) << 32) | (uint32_t)id;
+        }
+        s[i] = key;
+    }
+    __syncwarp();
+    warp_bitonic_sort(s, npow);
+    for (int j = lane; j < k; j += 32) {
+        const unsigned long long e = s[j];
+        out_ids[(size_t)q * k + j] = (int32_t)(uint32_t)(e & 0xffffffffu);
+        out_d[(size_t)q * k + j] = key2f((uint32_t)(e >> 32));
+    }
+}
+
+__global__ void map_ids_kernel(const int32_t* __restrict__ in, long long n, const int32_t* __restrict__ map,
+                               long long nmap, int32_t* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int32_t v = in[i];
+    out[i] = (v >= 0 && v < nmap) ? map[v] : -1;
+}
+
+int merge_topk(const float* dists, const int32_t* ids, int nshards, int nq, int k, int32_t* out_ids, float* out_d,
+               cudaStream_t s) {
+    FG_REQUIRE(nshards >= 1 && nq >= 0 && k >= 1, "bad merge shape");
+    if (nq == 0) return FG_OK;
+    FG_REQUIRE(dists && ids && out_ids && out_d, "null buffer");
+    const int npow = next_pow2(nshards * k);
+    FG_REQUIRE(npow <= 4096, "nshards * k = %d exceeds 4096", nshards * k);
+    const size_t smem = (size_t)MG_WARPS * npow * 8;
+    FG_CUDA_TRY(cudaFuncSetAttribute(merge_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    merge_topk_kernel<<<(nq + MG_WARPS - 1) / MG_WARPS, MG_WARPS * 32, smem, s>>>(dists, ids, nshards, nq, k, npow,
+                                                                                out_ids, out_d);
+    return check_launch("merge_topk_kernel");
+}
+
+int map_ids(const int32_t* in, long long n, const int32_t* map, long long nmap, int32_t* out, cudaStream_t s) {
+    FG_REQUIRE(n >= 0 && nmap >= 0, "bad sizes");
+    if (n == 0) return FG_OK;
+    FG_REQUIRE(in && out && (map || nmap == 0), "null buffer");
+    map_ids_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(in, n, map, nmap, out);
+    return check_launch("map_ids_kernel");
+}
+
+}  // namespace fg
+
+extern "C" int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nshards, int32_t nq, int32_t k,
+                             int32_t* out_ids, float* out_dists, void* stream) {
+    return fg::merge_topk(dists, ids, nshards, nq, k, out_ids, out_dists, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, int32_t* out,
+                          void* stream) {
+    return fg::map_ids(in, n, map, nmap, out, static_cast<cudaStream_t>(stream));
+}

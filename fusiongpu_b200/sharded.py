@@ -1,0 +1,101 @@
+"""List-sharded search across the GPUs of one box (one process per GPU).
+
+The reference runs on one GPU only (search_pipeline.cu:560).  For a database
+that is sharded by inverted list:
+
+* every GPU keeps all centroids and the codebook (so each computes the same
+  global probe list) but only the lists it owns, with their codes, ids and raw
+  vectors -- lists are dealt out by longest-processing-time on list length;
+* queries are broadcast; each GPU runs the whole search on its lists
+  (``fg_search``: probes it does not own are empty lists), maps its shard-local
+  vector ids to global ids (``fg_map_ids``) and returns its local top-k;
+* one all-gather (NCCL over NVLink) puts the per-GPU top-k side by side and
+  ``fg_merge_topk`` keeps the k best per query by (distance, global id).
+
+Per-shard semantics: phase 1 / threshold / phase 2 run over each shard's share
+of the probes (a probed list owned elsewhere counts as empty, as a pruned or
+empty list does in the reference), so results equal "the search on each shard,
+merged" -- which is what the oracle checks.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def partition_lists(list_sizes: np.ndarray, nshards: int) -> np.ndarray:
+    """Owner shard of every list: longest list first to the least-loaded
+    shard (ties: lower list id first, lower shard first)."""
+    sizes = np.asarray(list_sizes, dtype=np.int64)
+    order = np.lexsort((np.arange(sizes.size), -sizes))
+    load = np.zeros(nshards, dtype=np.int64)
+    owner = np.empty(sizes.size, dtype=np.int32)
+    for c in order:
+        s = int(np.argmin(load))
+        owner[c] = s
+        load[s] += sizes[c]
+    return owner
+
+
+def shard_arrays(index: dict, base: np.ndarray, owner: np.ndarray, rank: int):
+    """The shard index of ``rank`` (same centroids/codebook, lists it does not
+    own emptied), its raw vectors, and the local -> global id map."""
+    off = np.asarray(index["offsets"], dtype=np.int64)
+    lens = np.diff(off)
+    own = owner == rank
+    new_lens = np.where(own, lens, 0)
+    new_off = np.zeros_like(off)
+    new_off[1:] = np.cumsum(new_lens)
+    sel = np.concatenate([np.arange(off[c], off[c + 1]) for c in np.flatnonzero(own)] or [np.zeros(0, np.int64)])
+    l2g = np.asarray(index["ids"])[sel].astype(np.int32)
+    shard = dict(codebook=index["codebook"], centroids=index["centroids"], offsets=new_off.astype(np.int32),
+                 ids=np.arange(sel.size, dtype=np.int32), codes=np.ascontiguousarray(np.asarray(index["codes"])[sel]))
+    return shard, np.ascontiguousarray(base[l2g]), l2g
+
+
+class ShardedIndex:
+    """This process's shard of a list-sharded IVF-PQ index on one GPU."""
+
+    def __init__(self, index: dict, base: np.ndarray, rank: int, world: int, device="cuda", group=None):
+        import torch
+        from .index import IVFPQIndex
+        self.rank, self.world, self.group = rank, world, group
+        self.owner = partition_lists(np.diff(np.asarray(index["offsets"], dtype=np.int64)), world)
+        shard, sbase, l2g = shard_arrays(index, base, self.owner, rank)
+        self.local = IVFPQIndex.from_arrays(shard, sbase, device)
+        self.device = self.local.device
+        self.l2g = torch.from_numpy(l2g).to(self.device)
+        self.n_local = int(l2g.size)
+
+    def local_search(self, queries, params):
+        """This GPU's top-k with global ids."""
+        import torch
+        from . import _lib
+        from .index import _p, _stream
+        ids, d = self.local.search(queries, params)
+        gids = torch.empty_like(ids)
+        _lib.call("fg_map_ids", _p(ids), ids.numel(), _p(self.l2g), self.l2g.numel(), _p(gids), _stream())
+        return gids, d
+
+    def search(self, queries, params):
+        """Global top-k on every rank: local search, all-gather, device merge."""
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        from .index import _p, _stream
+        if self.n_local == 0:
+            nq = queries.shape[0]
+            d = torch.full((nq, params.final_k), float(np.finfo(np.float32).max), device=self.device)
+            gids = torch.full((nq, params.final_k), -1, dtype=torch.int32, device=self.device)
+        else:
+            gids, d = self.local_search(queries, params)
+        if self.world == 1:
+            return gids, d
+        nq, k = d.shape
+        all_d = torch.empty((self.world * nq * k,), dtype=torch.float32, device=self.device)
+        all_i = torch.empty((self.world * nq * k,), dtype=torch.int32, device=self.device)
+        dist.all_gather_into_tensor(all_d, d.reshape(-1), group=self.group)
+        dist.all_gather_into_tensor(all_i, gids.reshape(-1), group=self.group)
+        out_i = torch.empty((nq, k), dtype=torch.int32, device=self.device)
+        out_d = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        _lib.call("fg_merge_topk", _p(all_d), _p(all_i), self.world, nq, k, _p(out_i), _p(out_d), _stream())
+        return out_i, out_d

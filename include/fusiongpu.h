@@ -138,6 +138,19 @@ int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, cons
               int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- sharded search: the exchange step (no counterpart in the single-GPU
+ * reference, whose search runs on device 0 only, search_pipeline.cu:560).
+ * Each GPU searches the lists it owns with fg_search; fg_map_ids turns its
+ * shard-local vector ids into global ones (out[i] = map[in[i]], negative or
+ * out-of-range ids become -1); after an all-gather of the per-GPU results
+ * laid out [nshards][nq][k] (each row ascending by distance),
+ * fg_merge_topk keeps the k smallest per query by (distance, global id).
+ * nshards * k <= 4096. */
+int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, int32_t* out,
+               void* stream);
+int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nshards, int32_t nq, int32_t k,
+                  int32_t* out_ids, float* out_dists, void* stream);
+
 /* ---- index build (device pointers; the reference takes host pointers) ----- */
 
 /* Strided k-means seeding: centroid i = data[(i*stride + r_i % stride) % n],

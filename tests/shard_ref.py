@@ -1,0 +1,41 @@
+"""TEST INFRASTRUCTURE: host statements of the sharded search's exchange step
+(the merge that fg_merge_topk performs on the GPU) and of the sharded
+semantics with the CPU oracle."""
+import numpy as np
+
+from fusiongpu_b200.sharded import partition_lists, shard_arrays
+
+
+def merge_topk_host(dists: np.ndarray, ids: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Host statement of fg_merge_topk: [nshards][nq][k] -> [nq][k] by
+    (distance, id as unsigned, so padding id -1 sorts last)."""
+    ns, nq, kk = dists.shape
+    d = np.transpose(dists, (1, 0, 2)).reshape(nq, ns * kk)
+    i = np.transpose(ids, (1, 0, 2)).reshape(nq, ns * kk)
+    out_i = np.empty((nq, k), np.int32)
+    out_d = np.empty((nq, k), np.float32)
+    for q in range(nq):
+        order = np.lexsort((i[q].astype(np.uint32), d[q]))[:k]
+        out_i[q] = i[q][order]
+        out_d[q] = d[q][order]
+    return out_i, out_d
+
+
+def oracle_sharded_search(index: dict, base: np.ndarray, queries: np.ndarray, world: int, **params):
+    """The sharded semantics restated with the CPU oracle: per-shard search,
+    global ids, host merge."""
+    import oracle
+    owner = partition_lists(np.diff(np.asarray(index["offsets"], dtype=np.int64)), world)
+    ds, is_ = [], []
+    for r in range(world):
+        shard, sbase, l2g = shard_arrays(index, base, owner, r)
+        if l2g.size == 0:
+            nq, k = queries.shape[0], params["final_k"]
+            ds.append(np.full((nq, k), np.finfo(np.float32).max, np.float32))
+            is_.append(np.full((nq, k), -1, np.int32))
+            continue
+        li, ld = oracle.search(shard, sbase, queries, **params)
+        gi = np.where((li >= 0) & (li < l2g.size), l2g[np.clip(li, 0, l2g.size - 1)], -1).astype(np.int32)
+        ds.append(ld)
+        is_.append(gi)
+    return merge_topk_host(np.stack(ds), np.stack(is_), params["final_k"])

@@ -1,0 +1,107 @@
+"""GPU side of the list-sharded search: the merge kernel, shards simulated on
+one GPU, and (with 2+ GPUs) the real NCCL all-gather, each against the
+oracle's statement of the sharded semantics."""
+import ctypes as C
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+import oracle
+from fusiongpu_b200 import datasets as ds
+from tests import shard_ref
+from tests.conftest import cuda_available
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_available(), reason="needs a CUDA GPU")]
+torch = pytest.importorskip("torch")
+
+P = dict(top_m=10, p1_lists=4, limit_k=40, threshold_coeff=1.0, prune_ratio=100.0, rerank_m=120, final_k=10,
+         mini_batch=64, epsilon=0.1, beta=2, ref_compat=False)
+
+
+def _data():
+    base, q = ds.generate(ds.scaled(ds.C1, 12000, 96, n_centres=32, seed=43))
+    index, _ = oracle.build_index(base, 64, 32, kmeans_iters=4, pq_sample=4000, pq_iters=4)
+    return index, base, q
+
+
+def _merge_gpu(d, i, k):
+    from fusiongpu_b200 import _lib
+    from fusiongpu_b200.index import _p, _stream
+    ns, nq, kk = d.shape
+    td = torch.from_numpy(np.ascontiguousarray(d)).cuda()
+    ti = torch.from_numpy(np.ascontiguousarray(i)).cuda()
+    oi = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    _lib.call("fg_merge_topk", _p(td), _p(ti), ns, nq, k, _p(oi), _p(od), _stream())
+    return oi.cpu().numpy(), od.cpu().numpy()
+
+
+def test_merge_kernel_matches_host_statement():
+    rng = np.random.default_rng(3)
+    ns, nq, k = 5, 200, 16
+    d = np.sort(rng.integers(0, 20, size=(ns, nq, k)).astype(np.float32), axis=2)  # many ties
+    i = rng.permutation(ns * nq * k).reshape(ns, nq, k).astype(np.int32)
+    d[:, :, -3:] = np.finfo(np.float32).max
+    i[:, :, -3:] = -1
+    oi, od = _merge_gpu(d, i, k)
+    ei, ed = shard_ref.merge_topk_host(d, i, k)
+    np.testing.assert_array_equal(od, ed)
+    np.testing.assert_array_equal(oi, ei)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_shards_on_one_gpu_match_oracle(world):
+    from fusiongpu_b200.index import SearchParams
+    from fusiongpu_b200.sharded import ShardedIndex
+    index, base, q = _data()
+    p = SearchParams(**P)
+    qd = torch.from_numpy(q).cuda()
+    ds_, is_ = [], []
+    for r in range(world):
+        sh = ShardedIndex(index, base, r, world)
+        gi, d = sh.local_search(qd, p)
+        ds_.append(d.cpu().numpy())
+        is_.append(gi.cpu().numpy())
+    oi, od = _merge_gpu(np.stack(ds_), np.stack(is_), P["final_k"])
+    ei, ed = shard_ref.oracle_sharded_search(index, base, q, world, **P)
+    np.testing.assert_array_equal(od, ed)
+    np.testing.assert_array_equal(oi, ei)
+
+
+def _nccl_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from fusiongpu_b200.index import SearchParams
+    from fusiongpu_b200.sharded import ShardedIndex
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    index, base, q = _data()
+    sh = ShardedIndex(index, base, rank, world, device=f"cuda:{rank}")
+    ids, d = sh.search(torch.from_numpy(q).to(f"cuda:{rank}"), SearchParams(**P))
+    torch.cuda.synchronize()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), ids=ids.cpu().numpy(), dists=d.cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not cuda_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpus_nccl_all_gather_matches_oracle():
+    import torch.multiprocessing as mp
+    index, base, q = _data()
+    ei, ed = shard_ref.oracle_sharded_search(index, base, q, 2, **P)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_nccl_worker, args=(2, port, d), nprocs=2, join=True)
+        for r in range(2):
+            f = np.load(os.path.join(d, f"rank{r}.npz"))
+            np.testing.assert_array_equal(f["dists"], ed)
+            np.testing.assert_array_equal(f["ids"], ei)
