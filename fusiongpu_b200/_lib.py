@@ -34,6 +34,12 @@ class SearchParams(C.Structure):
                 ("beta", C.c_int32), ("ref_compat", C.c_int32)]
 
 
+class TuneResult(C.Structure):
+    _fields_ = [("top_m", C.c_int32), ("p1_lists", C.c_int32), ("limit_k", C.c_int32),
+                ("threshold_coeff", C.c_float), ("coverage_at_elbow", C.c_float), ("n_ranked", C.c_int32),
+                ("n_in_p1", C.c_int32), ("n_ratios", C.c_int32)]
+
+
 # name -> argtypes (all return int status unless noted)
 _P, _I32, _I64, _U32, _F, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_uint32, C.c_float, C.c_size_t
 _SIGS = {
@@ -43,6 +49,7 @@ _SIGS = {
     "fg_coarse_search_tc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P, _P],
     "fg_coarse_search_noalloc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P],
     "fg_batch_logic": [C.POINTER(IvfpqView), _P, _I32, _P, _P, C.POINTER(SearchParams), _P, _P, _P, _P, _P],
+    "fg_probe_budget": [_P, _I32, _P, _P, _I32, _I32, _F, _P, _P, _P],
     "fg_rerank": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
     "fg_search_workspace_size": [C.POINTER(IvfpqView), C.POINTER(SearchParams), _I32, C.POINTER(_SZ)],
     "fg_search": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, C.POINTER(SearchParams), _P, _P, _P, _SZ, _P],
@@ -59,6 +66,9 @@ _SIGS = {
     "fg_pq_train": [_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _P, _SZ, _P],
     "fg_pq_encode": [_P, _I64, _I32, _P, _P, _P, _I32, _P, _P],
     "fg_gather_lists": [_P, _I64, _I32, _P, _P, _P, _P],
+    "fg_rebalance": [_P, _I64, _I32, _P, _P, _I32, _I32, _U32, _P, _P, _I32, C.POINTER(_I32), _P],
+    "fg_tune": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, _P, _I32, C.POINTER(TuneResult), _P, _P, _P, _P, _P],
+    "fg_tune_elbow": [_P, _I32, _I64, C.POINTER(_I32), C.POINTER(_F)],
     "fg_knn_workspace_size": [_I64, _I32, _I32, _I32, C.POINTER(_SZ)],
     "fg_knn_exact": [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P],
 }

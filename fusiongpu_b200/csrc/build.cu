@@ -10,6 +10,8 @@
 // double and rounds once.  Results are therefore reproducible run to run and
 // equal to the CPU oracle's.
 #include <algorithm>
+#include <cmath>
+#include <deque>
 #include <vector>
 
 #include "fg_common.cuh"
@@ -458,6 +460,151 @@ int gather_lists(const uint8_t* codes, int64_t n, int pq_m, const int32_t* order
     if (n == 0) return FG_OK;
     gather_lists_kernel<<<(unsigned)n, 64, 0, s>>>(codes, n, pq_m, order, out_codes, out_ids);
     return check_launch("gather_lists_kernel");
+}
+
+// ---- list rebalancing (build_global.cu:62-169) --------------------------------
+//
+// Oversized lists are split by a local k-means until every list holds at most
+// twice the mean.  The control flow is the reference's FIFO work queue and
+// runs on the host; each split gathers the list's rows on the device, runs
+// k-means (sub_k centroids, `iters` Lloyd steps, the same strided seeding) and
+// the exact assignment there.  Lists are kept with ids ascending, so the
+// result is a pure function of the inputs.
+
+namespace {
+
+struct DevMem {
+    void* p = nullptr;
+    ~DevMem() {
+        if (p) cudaFree(p);
+    }
+    int alloc(size_t bytes) {
+        if (p) cudaFree(p);
+        p = nullptr;
+        if (bytes && cudaMalloc(&p, bytes) != cudaSuccess)
+            return fail(FG_ERR_CUDA, "cudaMalloc of %zu bytes failed", bytes);
+        return FG_OK;
+    }
+};
+
+struct Bucket {
+    std::vector<int32_t> ids;  // ascending point ids
+    std::vector<float> centroid;
+};
+
+}  // namespace
+
+int rebalance(const float* data, int64_t n, int dim, const int32_t* assign, const float* centroids, int k, int iters,
+              uint32_t seed, int32_t* out_assign, float* out_centroids, int cap, int32_t* out_nlist,
+              cudaStream_t s) {
+    FG_REQUIRE(n >= 1 && n <= 0x7fffffffll && dim >= 1 && k >= 1 && iters >= 0 && cap >= 0, "bad rebalance shape");
+    FG_REQUIRE(data && assign && centroids && out_assign && out_nlist && (out_centroids || cap == 0),
+               "null buffer");
+    std::vector<int32_t> a((size_t)n);
+    std::vector<float> cen((size_t)k * dim);
+    FG_CUDA_TRY(cudaMemcpyAsync(a.data(), assign, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    FG_CUDA_TRY(cudaMemcpyAsync(cen.data(), centroids, cen.size() * 4, cudaMemcpyDeviceToHost, s));
+    FG_CUDA_TRY(cudaStreamSynchronize(s));
+
+    std::vector<int64_t> count((size_t)k, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        FG_REQUIRE(a[i] >= 0 && a[i] < k, "assignment %d of point %lld outside [0, %d)", a[i], (long long)i, k);
+        ++count[a[i]];
+    }
+    const double avg = (double)n / k;
+    const size_t split_above = (size_t)(avg * 2);
+    const size_t min_split = 32;
+
+    std::deque<Bucket> queue;
+    {
+        std::vector<Bucket> init((size_t)k);
+        for (int c = 0; c < k; ++c) init[c].ids.reserve((size_t)count[c]);
+        for (int64_t i = 0; i < n; ++i) init[a[i]].ids.push_back((int32_t)i);
+        for (int c = 0; c < k; ++c) {
+            if (init[c].ids.empty()) continue;
+            init[c].centroid.assign(cen.begin() + (size_t)c * dim, cen.begin() + (size_t)(c + 1) * dim);
+            queue.push_back(std::move(init[c]));
+        }
+    }
+
+    // device scratch sized for the largest list that can be split (children
+    // are never larger than their parent)
+    size_t big = 0;
+    for (const Bucket& b : queue) big = std::max(big, b.ids.size());
+    const int big_k = (int)std::max<int64_t>(2, (int64_t)std::ceil((double)big / avg));
+    DevMem d_rows, d_sub, d_cen, d_as, d_ws;
+    bool have_scratch = false;
+    std::vector<int64_t> rows;
+    std::vector<int32_t> sub_as;
+    std::vector<float> sub_cen;
+
+    std::vector<Bucket> done;
+    int rc = FG_OK;
+    while (!queue.empty() && rc == FG_OK) {
+        Bucket b = std::move(queue.front());
+        queue.pop_front();
+        const size_t sz = b.ids.size();
+        if (sz <= split_above || sz < min_split) {
+            done.push_back(std::move(b));
+            continue;
+        }
+        int sub_k = (int)std::ceil((double)sz / avg);
+        if (sub_k < 2) sub_k = 2;
+        if (sub_k > (int)sz / 2) sub_k = (int)sz / 2;
+        if (!have_scratch) {
+            if ((rc = d_rows.alloc(big * 8)) || (rc = d_sub.alloc(big * dim * 4)) ||
+                (rc = d_cen.alloc((size_t)big_k * dim * 4)) || (rc = d_as.alloc(big * 4)) ||
+                (rc = d_ws.alloc(kmeans_workspace((int64_t)big, dim, big_k))))
+                break;
+            have_scratch = true;
+        }
+        rows.assign(b.ids.begin(), b.ids.end());
+        if ((rc = upload_rows(rows, static_cast<int64_t*>(d_rows.p), s))) break;
+        gather_rows_kernel<<<(unsigned)sz, 128, 0, s>>>(data, dim, static_cast<int64_t*>(d_rows.p), (int)sz,
+                                                        static_cast<float*>(d_sub.p));
+        if ((rc = check_launch("gather_rows_kernel"))) break;
+        float* sc = static_cast<float*>(d_cen.p);
+        if ((rc = kmeans(static_cast<float*>(d_sub.p), (int64_t)sz, dim, sub_k, iters, seed, sc, d_ws.p,
+                         kmeans_workspace((int64_t)big, dim, big_k), s)))
+            break;
+        if ((rc = l2_argmin(static_cast<float*>(d_sub.p), (long long)sz, sc, sub_k, dim,
+                            static_cast<int32_t*>(d_as.p), s)))
+            break;
+        sub_as.resize(sz);
+        sub_cen.resize((size_t)sub_k * dim);
+        FG_CUDA_TRY(cudaMemcpyAsync(sub_as.data(), d_as.p, sz * 4, cudaMemcpyDeviceToHost, s));
+        FG_CUDA_TRY(cudaMemcpyAsync(sub_cen.data(), sc, sub_cen.size() * 4, cudaMemcpyDeviceToHost, s));
+        FG_CUDA_TRY(cudaStreamSynchronize(s));
+        std::vector<Bucket> kids((size_t)sub_k);
+        for (size_t i = 0; i < sz; ++i) kids[sub_as[i]].ids.push_back(b.ids[i]);
+        int nonempty = 0;
+        for (const Bucket& kb : kids) nonempty += kb.ids.empty() ? 0 : 1;
+        for (int c = 0; c < sub_k; ++c) {
+            if (kids[c].ids.empty()) continue;
+            kids[c].centroid.assign(sub_cen.begin() + (size_t)c * dim, sub_cen.begin() + (size_t)(c + 1) * dim);
+            // a split that leaves every point in one child would repeat forever
+            // (all points equal); that child is final
+            if (nonempty == 1)
+                done.push_back(std::move(kids[c]));
+            else
+                queue.push_back(std::move(kids[c]));
+        }
+    }
+    if (rc) return rc;
+
+    const int nl = (int)done.size();
+    *out_nlist = nl;
+    if (nl > cap) return fail(FG_ERR_WORKSPACE, "rebalancing made %d lists; out_centroids holds %d", nl, cap);
+    std::vector<int32_t> na((size_t)n);
+    std::vector<float> nc((size_t)nl * dim);
+    for (int c = 0; c < nl; ++c) {
+        for (int32_t id : done[c].ids) na[id] = c;
+        std::copy(done[c].centroid.begin(), done[c].centroid.end(), nc.begin() + (size_t)c * dim);
+    }
+    FG_CUDA_TRY(cudaMemcpyAsync(out_assign, na.data(), (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    FG_CUDA_TRY(cudaMemcpyAsync(out_centroids, nc.data(), nc.size() * 4, cudaMemcpyHostToDevice, s));
+    FG_CUDA_TRY(cudaStreamSynchronize(s));
+    return FG_OK;
 }
 
 }  // namespace fg

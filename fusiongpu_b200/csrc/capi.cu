@@ -60,6 +60,10 @@ int pq_encode(const float* data, int64_t n, int dim, const int32_t* assign, cons
               const float* codebook, int pq_m, uint8_t* codes, cudaStream_t s);
 int gather_lists(const uint8_t* codes, int64_t n, int pq_m, const int32_t* order, uint8_t* out_codes,
                  int32_t* out_ids, cudaStream_t s);
+int probe_budget(const int32_t* list_offsets, int nlist, const uint32_t* probe_ids, const float* probe_dists, int nq,
+                 int top_m, float prune_ratio, int32_t* counts, int32_t* offsets, cudaStream_t s);
+int rebalance(const float* data, int64_t n, int dim, const int32_t* assign, const float* centroids, int k, int iters,
+              uint32_t seed, int32_t* out_assign, float* out_centroids, int cap, int32_t* out_nlist, cudaStream_t s);
 bool coarse_tc_supported(int dim, int P);
 size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P);
 int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, long long nq, int P,
@@ -186,6 +190,12 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                        candidate_counts, as_stream(stream), true);
 }
 
+int fg_probe_budget(const int32_t* list_offsets, int32_t nlist, const uint32_t* probe_ids, const float* probe_dists,
+                    int32_t nq, int32_t top_m, float prune_ratio, int32_t* counts, int32_t* offsets, void* stream) {
+    return probe_budget(list_offsets, nlist, probe_ids, probe_dists, nq, top_m, prune_ratio, counts, offsets,
+                        as_stream(stream));
+}
+
 int fg_rerank(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids, const int32_t* top_counts,
               const float* base, int64_t nbase, const fg_search_params* params, int32_t* out_ids, float* out_dists,
               void* stream) {
@@ -308,6 +318,13 @@ int fg_gather_lists(const uint8_t* codes, int64_t n, int32_t pq_m, const int32_t
                     int32_t* out_ids, void* stream) {
     FG_REQUIRE(codes && order && out_codes && out_ids && pq_m >= 1, "bad arguments");
     return gather_lists(codes, n, pq_m, order, out_codes, out_ids, as_stream(stream));
+}
+
+int fg_rebalance(const float* data, int64_t n, int32_t dim, const int32_t* assign, const float* centroids,
+                 int32_t k, int32_t iters, uint32_t seed, int32_t* out_assign, float* out_centroids, int32_t cap,
+                 int32_t* out_nlist, void* stream) {
+    return rebalance(data, n, dim, assign, centroids, k, iters, seed, out_assign, out_centroids, cap, out_nlist,
+                     as_stream(stream));
 }
 
 int fg_knn_workspace_size(int64_t nbase, int32_t dim, int32_t nq, int32_t k, size_t* bytes) {

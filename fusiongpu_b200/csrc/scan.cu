@@ -533,4 +533,64 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     return check_launch("ivfpq_batch_kernel");
 }
 
+// ---- candidate budget: prune + count + offsets (gpu_global.cu:31-77, 709-725) ----
+// counts[q] = total length of the probed lists that survive the prune
+// (distance <= best * prune_ratio); offsets = exclusive scan of counts with
+// offsets[nq] = the batch total.  The probe list is not modified.
+
+constexpr int BUD_NT = 128;
+
+__global__ void __launch_bounds__(BUD_NT)
+    budget_count_kernel(const int32_t* __restrict__ offs, int nlist, const uint32_t* __restrict__ pid,
+                        const float* __restrict__ pd, int top_m, float ratio, int32_t* __restrict__ counts) {
+    const int q = blockIdx.x;
+    const float thr = pd[(size_t)q * top_m] * ratio;
+    long long c = 0;
+    for (int j = threadIdx.x; j < top_m; j += BUD_NT) {
+        const uint32_t id = pid[(size_t)q * top_m + j];
+        if (id != FG_INVALID_PROBE && (int)id < nlist && !(pd[(size_t)q * top_m + j] > thr)) c += offs[id + 1] - offs[id];
+    }
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    __shared__ long long sw[BUD_NT / 32];
+    if ((threadIdx.x & 31) == 0) sw[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long t = 0;
+        for (int w = 0; w < BUD_NT / 32; ++w) t += sw[w];
+        counts[q] = (int32_t)t;
+    }
+}
+
+__global__ void __launch_bounds__(1024) budget_scan_kernel(const int32_t* __restrict__ counts, int nq,
+                                                           int32_t* __restrict__ offsets) {
+    __shared__ int sw[32];
+    int run = 0;
+    for (int b0 = 0; b0 < nq; b0 += 1024) {
+        const int i = b0 + threadIdx.x;
+        const int v = i < nq ? counts[i] : 0;
+        int tot;
+        const int ex = block_exclusive_scan<1024>(v, sw, tot);
+        if (i < nq) offsets[i] = run + ex;
+        run += tot;
+    }
+    if (threadIdx.x == 0) offsets[nq] = run;
+}
+
+int probe_budget(const int32_t* list_offsets, int nlist, const uint32_t* probe_ids, const float* probe_dists, int nq,
+                 int top_m, float prune_ratio, int32_t* counts, int32_t* offsets, cudaStream_t s) {
+    FG_REQUIRE(nq >= 0 && top_m >= 1 && nlist >= 1, "bad budget shape");
+    FG_REQUIRE(list_offsets && counts && (nq == 0 || (probe_ids && probe_dists)), "null buffer");
+    if (nq > 0) {
+        budget_count_kernel<<<nq, BUD_NT, 0, s>>>(list_offsets, nlist, probe_ids, probe_dists, top_m, prune_ratio,
+                                                   counts);
+        int rc = check_launch("budget_count_kernel");
+        if (rc) return rc;
+    }
+    if (offsets) {
+        budget_scan_kernel<<<1, 1024, 0, s>>>(counts, nq, offsets);
+        return check_launch("budget_scan_kernel");
+    }
+    return FG_OK;
+}
+
 }  // namespace fg

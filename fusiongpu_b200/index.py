@@ -107,6 +107,29 @@ def sort_by_list(assign: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tens
     return order, offsets
 
 
+def rebalance_lists(data, assign, centroids, iters: int = 15, seed: int = 42,
+                    device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """Split oversized lists by local k-means (build_global.cu:62-169).
+    Returns (assignment [n] int32, centroids [nlist'][dim]) on the device."""
+    x = _dev(data, torch.float32, device)
+    a = _dev(assign, torch.int32, device)
+    c = _dev(centroids, torch.float32, device)
+    n, d = x.shape
+    k = c.shape[0]
+    out_a = torch.empty(n, dtype=torch.int32, device=device)
+    cap = min(n, 4 * k)
+    while True:
+        out_c = torch.empty((max(cap, 1), d), dtype=torch.float32, device=device)
+        nl = C.c_int32(0)
+        rc = _lib.lib().fg_rebalance(_p(x), n, d, _p(a), _p(c), k, iters, seed, _p(out_a), _p(out_c), cap,
+                                     C.byref(nl), _stream())
+        if rc == 3 and nl.value > cap:  # FG_ERR_WORKSPACE: more lists than cap
+            cap = nl.value
+            continue
+        _lib.check(rc, "fg_rebalance")
+        return out_a, out_c[: nl.value].contiguous()
+
+
 def train_residual_pq_codebooks(data, vec_cluster_ids, clusters, pq_m: int, sample_size: int = 50000,
                                 max_iter: int = 8, device="cuda") -> torch.Tensor:
     x = _dev(data, torch.float32, device)
@@ -195,13 +218,18 @@ class IVFPQIndex:
 
     @classmethod
     def build(cls, base, nlist: int, pq_m: int, kmeans_iters: int = 20, pq_sample: int = 50000,
-              pq_iters: int = 8, seed: int = 42, keep_base: bool = True, device="cuda") -> "IVFPQIndex":
-        """k-means -> assignment -> residual PQ training -> encoding -> lists
-        (build_global.cu:21-258 without the list rebalancing and the CAGRA
-        graph over centroids, which the exact coarse quantizer replaces)."""
+              pq_iters: int = 8, seed: int = 42, keep_base: bool = True, rebalance: bool = True,
+              rebalance_iters: int = 15, device="cuda") -> "IVFPQIndex":
+        """k-means -> assignment -> list rebalancing -> residual PQ training ->
+        encoding -> lists (build_global.cu:21-258 without the CAGRA graph over
+        centroids, which the exact coarse quantizer replaces).  The index has
+        nlist lists or more when rebalancing splits some."""
         x = _dev(base, torch.float32, device)
         cen = run_kmeans_gpu(x, nlist, kmeans_iters, seed, device)
         a = gpu_assign_to_centroids(x, cen, device)
+        if rebalance:
+            a, cen = rebalance_lists(x, a, cen, rebalance_iters, seed, device)
+            nlist = cen.shape[0]
         cb = train_residual_pq_codebooks(x, a, cen, pq_m, pq_sample, pq_iters, device)
         codes = encode_residuals_to_pq_gpu(x, a, cen, cb, device)
         order, offsets = sort_by_list(a, nlist)

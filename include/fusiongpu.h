@@ -121,6 +121,16 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                    const fg_search_params* params, int32_t* top_ids, float* top_dists,
                    int32_t* top_counts, int32_t* candidate_counts, void* stream);
 
+/* ---- candidate budget: replaces prune_and_count_fused_kernel + the offsets
+ * scan (gpu_global.cu:31-77, 709-725).  counts[q] = summed length of the
+ * probed lists whose distance is <= probe_dists[q][0] * prune_ratio (the
+ * lists fg_batch_logic scans); offsets [nq+1] (may be NULL) = exclusive scan
+ * of counts, offsets[nq] = the batch total.  fg_batch_logic does not need it;
+ * it serves callers that size buffers or report pruning statistics. */
+int fg_probe_budget(const int32_t* list_offsets, int32_t nlist, const uint32_t* probe_ids,
+                    const float* probe_dists, int32_t nq, int32_t top_m, float prune_ratio,
+                    int32_t* counts, int32_t* offsets, void* stream);
+
 /* ---- exact rerank: replaces run_gpu_rerank (gpu_global.cu:603-673)
  * Mini-batches of `mini_batch` candidates, exact fp32 squared L2 against the
  * raw base vectors [nbase][dim], merged into a running top-final_k with the
@@ -150,6 +160,46 @@ int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, i
                void* stream);
 int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nshards, int32_t nq, int32_t k,
                   int32_t* out_ids, float* out_dists, void* stream);
+
+/* ---- search-parameter tuner: replaces tune_search_parameters
+ * (tune_parameters.cu:459-1013).  For nq sample queries with their exact k
+ * nearest base vectors gt_ids [nq][k] (ascending distance; fg_knn_exact),
+ * derives the reference's four recommendations:
+ *   top_m           = P99.5 of the coarse rank (1-based, lists ordered by
+ *                     (distance, id)) of each neighbour's list;
+ *   p1_lists        = the elbow of the hits-per-coarse-rank histogram;
+ *   limit_k         = the largest PQ rank inside its own list of the
+ *                     neighbours whose list ranks <= p1_lists (P98 of all PQ
+ *                     ranks when there is none);
+ *   threshold_coeff = the largest ratio, over queries, of the farthest
+ *                     neighbour's PQ distance to the smallest phase-1 cutoff
+ *                     (the min(limit_k, len)-th smallest PQ distance of each
+ *                     non-empty list among the first p1_lists); 2 if none.
+ * A neighbour's list is the lowest-numbered list holding its id.  Optional
+ * HOST outputs (NULL to skip): cluster_ranks, pq_ranks, exact_ranks [nq][k]
+ * (-1 where the id is in no list) and ratios [nq] (NaN where a query gives
+ * none).  Synchronises the stream and allocates its own device scratch. */
+typedef struct {
+    int32_t top_m;
+    int32_t p1_lists;
+    int32_t limit_k;
+    float   threshold_coeff;
+    float   coverage_at_elbow;  /* share of neighbours within the first p1_lists lists */
+    int32_t n_ranked;           /* neighbours found in some list                       */
+    int32_t n_in_p1;            /* of those, in a list ranked <= p1_lists               */
+    int32_t n_ratios;           /* queries that gave a threshold ratio                  */
+} fg_tune_result;
+
+int fg_tune(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries,
+            int32_t nq, const int32_t* gt_ids, int32_t k, fg_tune_result* out,
+            int32_t* cluster_ranks, int32_t* pq_ranks, int32_t* exact_ranks, float* ratios,
+            void* stream);
+
+/* The elbow rule fg_tune applies to the hits-per-coarse-rank histogram
+ * (find_elbow_point, tune_parameters.cu:199-456), on host arrays: hits[i] =
+ * neighbours whose list ranks i+1, total = their sum.  Writes the 1-based
+ * elbow rank and the coverage there. */
+int fg_tune_elbow(const int32_t* hits, int32_t n, int64_t total, int32_t* point, float* coverage);
 
 /* ---- index build (device pointers; the reference takes host pointers) ----- */
 
@@ -200,6 +250,24 @@ int fg_pq_encode(const float* data, int64_t n, int32_t dim, const int32_t* assig
  * bytes), out_ids[r] = order[r].  Replaces build_global.cu:226-240. */
 int fg_gather_lists(const uint8_t* codes, int64_t n, int32_t pq_m, const int32_t* order,
                     uint8_t* out_codes, int32_t* out_ids, void* stream);
+
+/* List rebalancing: replaces build_global.cu:62-169.  With avg = n/k, every
+ * list longer than (size_t)(2*avg) and not shorter than 32 points is split
+ * into sub_k = clamp(ceil(len/avg), 2, len/2) lists by fg_kmeans on its
+ * points (`iters` steps, `seed`; the reference uses 15 and 42) and
+ * fg_assign; the children go to the back of a FIFO queue that starts with the
+ * non-empty input lists in order, and a list leaves the queue as final when it
+ * is small enough.  Final lists are numbered in the order they leave the
+ * queue.  A split whose points all land in one child ends there (the
+ * reference would repeat it forever).  out_assign [n] (may alias assign) and
+ * out_centroids [cap][dim] are device memory; *out_nlist (host) receives the
+ * list count, also when it exceeds cap (then FG_ERR_WORKSPACE and nothing is
+ * written: call again with cap >= *out_nlist).  Synchronises the stream; the
+ * control loop runs on the host and allocates its own device scratch. */
+int fg_rebalance(const float* data, int64_t n, int32_t dim, const int32_t* assign,
+                 const float* centroids, int32_t k, int32_t iters, uint32_t seed,
+                 int32_t* out_assign, float* out_centroids, int32_t cap, int32_t* out_nlist,
+                 void* stream);
 
 /* Exact k nearest base vectors (ground truth), ascending by (distance, id). */
 int fg_knn_workspace_size(int64_t nbase, int32_t dim, int32_t nq, int32_t k, size_t* bytes);

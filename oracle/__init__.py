@@ -165,6 +165,33 @@ def knn_exact(base, queries, k, nthreads=0):
     return oi, od
 
 
+class TuneResult(C.Structure):
+    _fields_ = [("top_m", C.c_int32), ("p1_lists", C.c_int32), ("limit_k", C.c_int32),
+                ("threshold_coeff", C.c_float), ("coverage_at_elbow", C.c_float), ("n_ranked", C.c_int32),
+                ("n_in_p1", C.c_int32), ("n_ratios", C.c_int32)]
+
+
+def tune(index, base, queries, gt, nthreads=0):
+    """The tuner's statistics for given sample queries and ground truth
+    [nq][k].  Returns (result dict, cluster_ranks, pq_ranks, exact_ranks,
+    ratios)."""
+    base = np.ascontiguousarray(base, np.float32)
+    queries = np.ascontiguousarray(queries, np.float32)
+    gt = np.ascontiguousarray(gt, np.int32)
+    nq, k = gt.shape
+    ix, keep = make_index(index)
+    r = TuneResult()
+    cr = np.empty((nq, k), np.int32)
+    pr = np.empty((nq, k), np.int32)
+    er = np.empty((nq, k), np.int32)
+    ra = np.empty(nq, np.float32)
+    _check(lib().fgo_tune(C.byref(ix), _p(base), C.c_int64(base.shape[0]), _p(queries), nq, _p(gt), k,
+                          C.byref(r), _p(cr), _p(pr), _p(er), _p(ra), nthreads), "tune")
+    del keep
+    res = {f: getattr(r, f) for f, _ in TuneResult._fields_}
+    return res, cr, pr, er, ra
+
+
 def mt19937(seed: int, skip: int = 0) -> int:
     lib().fgo_mt19937_first.restype = C.c_uint32
     return int(lib().fgo_mt19937_first(C.c_uint32(seed), skip))
@@ -228,12 +255,33 @@ def pq_encode(data, assignment, centroids, codebook, nthreads=0):
     return codes
 
 
-def build_index(base, nlist, pq_m, kmeans_iters=20, pq_sample=50000, pq_iters=8, nthreads=0):
-    """CPU IVF-PQ build with the oracle's semantics (no rebalancing); lists hold
-    ids in ascending order.  Returns the index dict plus the assignment."""
+def rebalance(data, assignment, centroids, iters=15, seed=42, nthreads=0):
+    """Split oversized lists (build_global.cu:62-169).  Returns the new
+    assignment and centroids."""
+    data = np.ascontiguousarray(data, np.float32)
+    assignment = np.ascontiguousarray(assignment, np.int32)
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    n, d = data.shape
+    out_a = np.empty(n, np.int32)
+    cap = n
+    out_c = np.empty((cap, d), np.float32)
+    nl = C.c_int32(0)
+    _check(lib().fgo_rebalance(_p(data), C.c_int64(n), d, _p(assignment), _p(centroids), centroids.shape[0],
+                               iters, C.c_uint32(seed), _p(out_a), _p(out_c), cap, C.byref(nl), nthreads),
+           "rebalance")
+    return out_a, np.ascontiguousarray(out_c[: nl.value])
+
+
+def build_index(base, nlist, pq_m, kmeans_iters=20, pq_sample=50000, pq_iters=8, nthreads=0,
+                rebalance_lists=True, rebalance_iters=15):
+    """CPU IVF-PQ build with the oracle's semantics: k-means, assignment, list
+    rebalancing (optional), residual PQ; lists hold ids in ascending order.
+    Returns the index dict plus the assignment."""
     base = np.ascontiguousarray(base, np.float32)
     cen = kmeans(base, nlist, kmeans_iters, 42, nthreads)
     a = assign(base, cen, nthreads)
+    if rebalance_lists:
+        a, cen = rebalance(base, a, cen, rebalance_iters, 42, nthreads)
     cb = pq_train(base, a, cen, pq_m, pq_sample, pq_iters, nthreads)
     codes = pq_encode(base, a, cen, cb, nthreads)
     return assemble_lists(a, codes, cen, cb), a

@@ -510,6 +510,138 @@ int fgo_kmeans(const float* data, int64_t n, int dim, int k, int iters, uint32_t
     return rc;
 }
 
+/* List rebalancing (build_global.cu:62-169): a FIFO queue of lists, starting
+ * with the non-empty input lists in order.  A list longer than
+ * (size_t)(2 * n/k) and not shorter than 32 is split by k-means on its points
+ * (sub_k = clamp(ceil(len/avg), 2, len/2), `iters` steps, `seed`) and the
+ * exact assignment; its non-empty children go to the back of the queue.  Any
+ * other list is final and numbered in the order it leaves the queue.  A split
+ * whose points all land in one child makes that child final (the reference
+ * would split it again forever).  Returns the list count in *out_nlist; when
+ * it exceeds cap nothing is written and 3 is returned. */
+typedef struct {
+    int32_t* ids;
+    int64_t len;
+    float* cen;
+} fgo_list;
+
+typedef struct {
+    fgo_list* v;
+    int64_t n, cap;
+} fgo_lists;
+
+static int lists_push(fgo_lists* L, fgo_list x) {
+    if (L->n == L->cap) {
+        int64_t nc = L->cap ? 2 * L->cap : 64;
+        fgo_list* nv = (fgo_list*)realloc(L->v, (size_t)nc * sizeof(fgo_list));
+        if (!nv) return 2;
+        L->v = nv;
+        L->cap = nc;
+    }
+    L->v[L->n++] = x;
+    return 0;
+}
+
+int fgo_rebalance(const float* data, int64_t n, int dim, const int32_t* assign,
+                  const float* centroids, int k, int iters, uint32_t seed, int32_t* out_assign,
+                  float* out_centroids, int cap, int32_t* out_nlist, int nthreads) {
+    if (n < 1 || k < 1 || dim < 1) return 1;
+    const double avg = (double)n / k;
+    const size_t split_above = (size_t)(avg * 2);
+    fgo_lists queue = {0}, done = {0};
+    int64_t head = 0;
+    int rc = 0;
+    int64_t* cnt = (int64_t*)calloc((size_t)k, sizeof(int64_t));
+    if (!cnt) return 2;
+    for (int64_t i = 0; i < n; ++i) {
+        if (assign[i] < 0 || assign[i] >= k) { free(cnt); return 1; }
+        cnt[assign[i]]++;
+    }
+    for (int c = 0; c < k && !rc; ++c) {
+        if (!cnt[c]) continue;
+        fgo_list x;
+        x.len = 0;
+        x.ids = (int32_t*)malloc((size_t)cnt[c] * sizeof(int32_t));
+        x.cen = (float*)malloc((size_t)dim * sizeof(float));
+        if (!x.ids || !x.cen) { rc = 2; break; }
+        memcpy(x.cen, centroids + (size_t)c * dim, (size_t)dim * sizeof(float));
+        rc = lists_push(&queue, x);
+    }
+    free(cnt);
+    /* members in ascending id order; queue slot j = j-th non-empty cluster */
+    if (!rc) {
+        int64_t* slot = (int64_t*)malloc((size_t)k * sizeof(int64_t));
+        if (!slot) rc = 2;
+        else {
+            int64_t j = 0;
+            for (int c = 0; c < k; ++c) slot[c] = -1;
+            for (int64_t i = 0; i < n; ++i) slot[assign[i]] = 0;
+            for (int c = 0; c < k; ++c)
+                if (slot[c] == 0) slot[c] = j++;
+            for (int64_t i = 0; i < n; ++i) {
+                fgo_list* x = &queue.v[slot[assign[i]]];
+                x->ids[x->len++] = (int32_t)i;
+            }
+            free(slot);
+        }
+    }
+    while (!rc && head < queue.n) {
+        fgo_list b = queue.v[head++];
+        if ((size_t)b.len <= split_above || b.len < 32) {
+            rc = lists_push(&done, b);
+            continue;
+        }
+        int sub_k = (int)ceil((double)b.len / avg);
+        if (sub_k < 2) sub_k = 2;
+        if (sub_k > (int)b.len / 2) sub_k = (int)b.len / 2;
+        float* sub = (float*)malloc((size_t)b.len * dim * sizeof(float));
+        float* sc = (float*)malloc((size_t)sub_k * dim * sizeof(float));
+        int32_t* sa = (int32_t*)malloc((size_t)b.len * sizeof(int32_t));
+        int64_t* kc = (int64_t*)calloc((size_t)sub_k, sizeof(int64_t));
+        if (!sub || !sc || !sa || !kc) rc = 2;
+        if (!rc) {
+            for (int64_t i = 0; i < b.len; ++i)
+                memcpy(sub + (size_t)i * dim, data + (size_t)b.ids[i] * dim, (size_t)dim * sizeof(float));
+            rc = fgo_kmeans(sub, b.len, dim, sub_k, iters, seed, sc, nthreads);
+        }
+        if (!rc) rc = fgo_assign(sub, b.len, dim, sc, sub_k, sa, nthreads);
+        int nonempty = 0;
+        if (!rc) {
+            for (int64_t i = 0; i < b.len; ++i) kc[sa[i]]++;
+            for (int c = 0; c < sub_k; ++c) nonempty += kc[c] ? 1 : 0;
+        }
+        for (int c = 0; c < sub_k && !rc; ++c) {
+            if (!kc[c]) continue;
+            fgo_list x;
+            x.len = 0;
+            x.ids = (int32_t*)malloc((size_t)kc[c] * sizeof(int32_t));
+            x.cen = (float*)malloc((size_t)dim * sizeof(float));
+            if (!x.ids || !x.cen) { free(x.ids); free(x.cen); rc = 2; break; }
+            for (int64_t i = 0; i < b.len; ++i)
+                if (sa[i] == c) x.ids[x.len++] = b.ids[i];
+            memcpy(x.cen, sc + (size_t)c * dim, (size_t)dim * sizeof(float));
+            rc = nonempty == 1 ? lists_push(&done, x) : lists_push(&queue, x);
+        }
+        free(sub); free(sc); free(sa); free(kc);
+        free(b.ids); free(b.cen);
+    }
+    if (!rc) {
+        *out_nlist = (int32_t)done.n;
+        if (done.n > cap) rc = 3;
+    }
+    if (!rc) {
+        for (int64_t c = 0; c < done.n; ++c) {
+            for (int64_t i = 0; i < done.v[c].len; ++i) out_assign[done.v[c].ids[i]] = (int32_t)c;
+            memcpy(out_centroids + (size_t)c * dim, done.v[c].cen, (size_t)dim * sizeof(float));
+        }
+    }
+    for (int64_t i = head; i < queue.n; ++i) { free(queue.v[i].ids); free(queue.v[i].cen); }
+    for (int64_t i = 0; i < done.n; ++i) { free(done.v[i].ids); free(done.v[i].cen); }
+    free(queue.v);
+    free(done.v);
+    return rc;
+}
+
 /* Residual PQ training: a strided sample of `sample` residuals (seed 12345),
  * then an independent 256-way k-means per subspace (seed 1234 + m, `iters`
  * Lloyd steps), as pq_utils.h:77-138 structures it. */
@@ -585,5 +717,278 @@ int fgo_pq_encode(const float* data, int64_t n, int dim, const int32_t* assign,
             codes[(size_t)i * pq_m + m] = (uint8_t)bk;
         }
     }
+    return 0;
+}
+
+/* ---- search-parameter tuner (tune_parameters.cu:169-1013) ------------------
+ * Same statistics as the reference's tune_search_parameters for given sample
+ * queries and ground truth: coarse distances as the reference's host code
+ * computes them (separate multiply and add), LUT / PQ / exact distances as its
+ * device kernels do (fmaf per dimension). */
+
+static float l2_host(const float* a, const float* b, int dim) {
+    float d = 0.0f;
+    for (int j = 0; j < dim; ++j) {
+        float df = a[j] - b[j];
+        float sq = df * df;
+        d = d + sq;
+    }
+    return d;
+}
+
+static void tune_lut(const float* q, const float* cen, const float* codebook, int pq_m, int sd, float* lut) {
+    for (int m = 0; m < pq_m; ++m)
+        for (int j = 0; j < 256; ++j) {
+            const float* cb = codebook + ((size_t)m * 256 + j) * sd;
+            float acc = 0.0f;
+            for (int d = 0; d < sd; ++d) {
+                float r = q[m * sd + d] - cen[m * sd + d];
+                float df = r - cb[d];
+                acc = fmaf(df, df, acc);
+            }
+            lut[m * 256 + j] = acc;
+        }
+}
+
+static float tune_pq(const uint8_t* code, const float* lut, int pq_m) {
+    float s = 0.0f;
+    for (int m = 0; m < pq_m; ++m) s = s + lut[m * 256 + code[m]];
+    return s;
+}
+
+typedef struct {
+    float d;
+    int c;
+} fgo_dc;
+
+static int cmp_dc(const void* a, const void* b) {
+    const fgo_dc* x = (const fgo_dc*)a;
+    const fgo_dc* y = (const fgo_dc*)b;
+    if (x->d < y->d) return -1;
+    if (y->d < x->d) return 1;
+    return (x->c > y->c) - (x->c < y->c);
+}
+
+static int cmp_f(const void* a, const void* b) {
+    float x = *(const float*)a, y = *(const float*)b;
+    return (x > y) - (x < y);
+}
+
+static int cmp_i(const void* a, const void* b) {
+    int x = *(const int*)a, y = *(const int*)b;
+    return (x > y) - (x < y);
+}
+
+/* sorted copy's element (int)((float)n * p), clamped (tune_parameters.cu:169-184) */
+static int pct_int(const int* v, int64_t n, float p) {
+    if (n <= 0) return 0;
+    int* s = (int*)malloc((size_t)n * sizeof(int));
+    memcpy(s, v, (size_t)n * sizeof(int));
+    qsort(s, (size_t)n, sizeof(int), cmp_i);
+    int i = (int)((float)n * p);
+    if (i >= n) i = (int)n - 1;
+    if (i < 0) i = 0;
+    int r = s[i];
+    free(s);
+    return r;
+}
+
+/* elbow of the hits-per-rank curve (tune_parameters.cu:199-456) */
+void fgo_tune_elbow(const int* hits, int n, int64_t total, int* point, float* coverage) {
+    *point = 1;
+    *coverage = 0.0f;
+    if (n == 0 || total == 0) return;
+    float* cov = (float*)calloc((size_t)n, sizeof(float));
+    float* lg = (float*)calloc((size_t)n, sizeof(float));
+    float* sm = (float*)calloc((size_t)n, sizeof(float));
+    float* cu = (float*)calloc((size_t)n, sizeof(float));
+    float* vo = (float*)calloc((size_t)n, sizeof(float));
+    int64_t run = 0;
+    for (int i = 0; i < n; ++i) {
+        run += hits[i];
+        cov[i] = (float)run / (float)total;
+        lg[i] = logf((float)hits[i] + 1.0f);
+    }
+    for (int i = 0; i < n; ++i) {
+        if (i == 0 || i == n - 1) {
+            sm[i] = lg[i];
+        } else {
+            float a = 0.25f * lg[i - 1];
+            float b = 0.50f * lg[i];
+            float c = 0.25f * lg[i + 1];
+            sm[i] = (a + b) + c;
+        }
+    }
+    for (int i = 1; i + 1 < n; ++i) {
+        float two = 2.0f * sm[i];
+        cu[i] = (sm[i + 1] - two) + sm[i - 1];
+        float d1 = (float)(hits[i - 1] - hits[i]);
+        float d2 = (float)(hits[i] - hits[i + 1]);
+        if (d1 * d2 < 0.0f) vo[i] = 1.0f;
+    }
+    int best_i = -1;
+    float best = -1e9f;
+    for (int i = 2; i + 1 < n && i < 30; ++i) {
+        if (cov[i] < 0.60f) continue;
+        float cs = fabsf(cu[i]) * 10.0f;
+        float before = (float)(hits[i - 1] - hits[i]) / ((float)hits[i - 1] + 1.0f);
+        float after = (float)(hits[i] - hits[i + 1]) / ((float)hits[i] + 1.0f);
+        float ds = 0.0f;
+        if (after < before) ds = (before - after) * 8.0f;
+        float r = (float)i / 32.0f;
+        float bonus = 4.0f * (1.0f - r * r);
+        float score = ((cs + ds) + bonus) - vo[i] * 5.0f;
+        if (cov[i] >= 0.80f && score > best) {
+            best = score;
+            best_i = i;
+        }
+    }
+    if (best_i >= 0) {
+        *point = best_i + 1;
+        *coverage = cov[best_i];
+    } else {
+        for (int i = 0; i < n; ++i)
+            if (cov[i] >= 0.60f) {
+                *point = i + 1;
+                *coverage = cov[i];
+                break;
+            }
+    }
+    free(cov); free(lg); free(sm); free(cu); free(vo);
+}
+
+int fgo_tune(const fgo_index* idx, const float* base, int64_t nbase, const float* queries, int nq,
+             const int32_t* gt, int k, fgo_tune_result* out, int32_t* cluster_ranks,
+             int32_t* pq_ranks, int32_t* exact_ranks, float* ratios, int nthreads) {
+    const int dim = idx->dim, pq_m = idx->pq_m, sd = idx->sub_dim, nlist = idx->nlist;
+    const int64_t np = (int64_t)nq * k;
+    int32_t* owner = (int32_t*)malloc((size_t)nbase * sizeof(int32_t));
+    int32_t* first = (int32_t*)malloc((size_t)nbase * sizeof(int32_t));
+    int32_t* cr = (int32_t*)malloc((size_t)np * sizeof(int32_t));
+    int32_t* pr = (int32_t*)malloc((size_t)np * sizeof(int32_t));
+    int32_t* er = (int32_t*)malloc((size_t)np * sizeof(int32_t));
+    float* pqt = (float*)malloc((size_t)np * sizeof(float));
+    float* cut = (float*)malloc((size_t)nq * sizeof(float));
+    if (!owner || !first || !cr || !pr || !er || !pqt || !cut) return 2;
+    for (int64_t i = 0; i < nbase; ++i) owner[i] = first[i] = -1;
+    for (int c = 0; c < nlist; ++c)
+        for (int j = idx->offsets[c]; j < idx->offsets[c + 1]; ++j) {
+            int32_t id = idx->ids[j];
+            if (id >= 0 && id < nbase && owner[id] < 0) {
+                owner[id] = c;
+                first[id] = j;
+            }
+        }
+    set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t p = 0; p < np; ++p) {
+        const int q = (int)(p / k);
+        const float* qv = queries + (size_t)q * dim;
+        int32_t id = gt[p];
+        int c = (id >= 0 && id < nbase) ? owner[id] : -1;
+        cr[p] = pr[p] = er[p] = -1;
+        pqt[p] = -1.0f;
+        if (c < 0) continue;
+        float dc = l2_host(qv, idx->centroids + (size_t)c * dim, dim);
+        int before = 0;
+        for (int c2 = 0; c2 < nlist; ++c2) {
+            float d2 = l2_host(qv, idx->centroids + (size_t)c2 * dim, dim);
+            if (d2 < dc || (d2 == dc && c2 < c)) ++before;
+        }
+        cr[p] = before + 1;
+        float* lut = (float*)malloc((size_t)pq_m * 256 * sizeof(float));
+        tune_lut(qv, idx->centroids + (size_t)c * dim, idx->codebook, pq_m, sd, lut);
+        float pt = tune_pq(idx->codes + (size_t)first[id] * pq_m, lut, pq_m);
+        float et = l2_seq(qv, base + (size_t)id * dim, dim);
+        int npq = 0, nex = 0;
+        for (int j = idx->offsets[c]; j < idx->offsets[c + 1]; ++j) {
+            if (tune_pq(idx->codes + (size_t)j * pq_m, lut, pq_m) < pt) ++npq;
+            int32_t v = idx->ids[j];
+            if (v >= 0 && v < nbase && l2_seq(qv, base + (size_t)v * dim, dim) < et) ++nex;
+        }
+        free(lut);
+        pr[p] = npq + 1;
+        er[p] = nex + 1;
+        pqt[p] = pt;
+    }
+    fgo_tune_result r;
+    memset(&r, 0, sizeof(r));
+    int* ranks = (int*)malloc((size_t)np * sizeof(int));
+    int64_t nr = 0;
+    int max_rank = 0;
+    for (int64_t p = 0; p < np; ++p)
+        if (cr[p] > 0) {
+            ranks[nr++] = cr[p];
+            if (cr[p] > max_rank) max_rank = cr[p];
+        }
+    r.top_m = pct_int(ranks, nr, 0.995f);
+    int* hits = (int*)calloc((size_t)(max_rank > 0 ? max_rank : 1), sizeof(int));
+    for (int64_t i = 0; i < nr; ++i) hits[ranks[i] - 1]++;
+    fgo_tune_elbow(hits, max_rank, nr, &r.p1_lists, &r.coverage_at_elbow);
+    r.n_ranked = (int)nr;
+    int* allq = (int*)malloc((size_t)np * sizeof(int));
+    int64_t na = 0, n1 = 0;
+    int mx1 = 0;
+    for (int64_t p = 0; p < np; ++p) {
+        if (pr[p] <= 0) continue;
+        allq[na++] = pr[p];
+        if (cr[p] > 0 && cr[p] <= r.p1_lists) {
+            ++n1;
+            if (pr[p] > mx1) mx1 = pr[p];
+        }
+    }
+    r.limit_k = n1 ? mx1 : pct_int(allq, na, 0.98f);
+    r.n_in_p1 = (int)n1;
+    const int P = r.p1_lists < nlist ? (r.p1_lists > 1 ? r.p1_lists : 1) : nlist;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int q = 0; q < nq; ++q) {
+        const float* qv = queries + (size_t)q * dim;
+        fgo_dc* all = (fgo_dc*)malloc((size_t)nlist * sizeof(fgo_dc));
+        for (int c = 0; c < nlist; ++c) {
+            all[c].d = l2_host(qv, idx->centroids + (size_t)c * dim, dim);
+            all[c].c = c;
+        }
+        qsort(all, (size_t)nlist, sizeof(fgo_dc), cmp_dc);
+        float* lut = (float*)malloc((size_t)pq_m * 256 * sizeof(float));
+        float best = 0.0f;
+        int have = 0;
+        for (int s = 0; s < P; ++s) {
+            int c = all[s].c;
+            int lo = idx->offsets[c], len = idx->offsets[c + 1] - lo;
+            if (len <= 0) continue;
+            tune_lut(qv, idx->centroids + (size_t)c * dim, idx->codebook, pq_m, sd, lut);
+            float* d = (float*)malloc((size_t)len * sizeof(float));
+            for (int j = 0; j < len; ++j) d[j] = tune_pq(idx->codes + (size_t)(lo + j) * pq_m, lut, pq_m);
+            qsort(d, (size_t)len, sizeof(float), cmp_f);
+            int i = r.limit_k - 1 < len - 1 ? r.limit_k - 1 : len - 1;
+            if (i < 0) i = 0;
+            if (!have || d[i] < best) best = d[i];
+            have = 1;
+            free(d);
+        }
+        cut[q] = have ? best : NAN;
+        free(lut);
+        free(all);
+    }
+    float mx = 0.0f;
+    int nrat = 0;
+    for (int q = 0; q < nq; ++q) {
+        float ratio = NAN;
+        int64_t far = (int64_t)q * k + (k - 1);
+        if (!isnan(cut[q]) && pr[far] > 0 && pqt[far] >= 0.0f && cut[q] > 0.0f) {
+            ratio = pqt[far] / cut[q];
+            if (!nrat || ratio > mx) mx = ratio;
+            ++nrat;
+        }
+        if (ratios) ratios[q] = ratio;
+    }
+    r.threshold_coeff = nrat ? mx : 2.0f;
+    r.n_ratios = nrat;
+    if (cluster_ranks) memcpy(cluster_ranks, cr, (size_t)np * sizeof(int32_t));
+    if (pq_ranks) memcpy(pq_ranks, pr, (size_t)np * sizeof(int32_t));
+    if (exact_ranks) memcpy(exact_ranks, er, (size_t)np * sizeof(int32_t));
+    *out = r;
+    free(owner); free(first); free(cr); free(pr); free(er); free(pqt); free(cut);
+    free(ranks); free(hits); free(allq);
     return 0;
 }

@@ -81,12 +81,28 @@ int fgo_kmeans_update(const float* data, int64_t n, int dim, const int32_t* assi
                       float* centroids, int32_t* counts);
 int fgo_kmeans(const float* data, int64_t n, int dim, int k, int iters, uint32_t seed,
                float* centroids, int nthreads);
+int fgo_rebalance(const float* data, int64_t n, int dim, const int32_t* assign,
+                  const float* centroids, int k, int iters, uint32_t seed, int32_t* out_assign,
+                  float* out_centroids, int cap, int32_t* out_nlist, int nthreads);
 int fgo_pq_train(const float* data, int64_t n, int dim, const int32_t* assign,
                  const float* centroids, int pq_m, int sample, int iters, float* codebook,
                  int nthreads);
 int fgo_pq_encode(const float* data, int64_t n, int dim, const int32_t* assign,
                   const float* centroids, const float* codebook, int pq_m, uint8_t* codes,
                   int nthreads);
+
+/* Search-parameter tuner (tune_parameters.cu:459-1013): same fields as
+ * fg_tune_result of the product's C ABI. */
+typedef struct {
+    int32_t top_m, p1_lists, limit_k;
+    float threshold_coeff, coverage_at_elbow;
+    int32_t n_ranked, n_in_p1, n_ratios;
+} fgo_tune_result;
+
+void fgo_tune_elbow(const int* hits, int n, int64_t total, int* point, float* coverage);
+int fgo_tune(const fgo_index* idx, const float* base, int64_t nbase, const float* queries, int nq,
+             const int32_t* gt, int k, fgo_tune_result* out, int32_t* cluster_ranks,
+             int32_t* pq_ranks, int32_t* exact_ranks, float* ratios, int nthreads);
 
 #ifdef __cplusplus
 }

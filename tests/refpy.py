@@ -162,3 +162,35 @@ def rerank(queries, top_ids, top_counts, base, p):
         out_i[q] = fid
         out_d[q] = fd
     return out_i, out_d
+
+
+def rebalance(data, assignment, centroids, kmeans, assign, iters=15, seed=42):
+    """The FIFO split loop of build_global.cu:62-169 in plain Python, with the
+    k-means and assignment steps passed in (the oracle's).  Returns the new
+    assignment and centroids."""
+    from collections import deque
+    n = data.shape[0]
+    k = centroids.shape[0]
+    avg = n / k
+    split_above = int(avg * 2)
+    queue = deque()
+    for c in range(k):
+        members = np.flatnonzero(assignment == c)
+        if members.size:
+            queue.append((members, centroids[c]))
+    done = []
+    while queue:
+        ids, cen = queue.popleft()
+        if ids.size <= split_above or ids.size < 32:
+            done.append((ids, cen))
+            continue
+        sub_k = max(2, int(np.ceil(ids.size / avg)))
+        sub_k = min(sub_k, ids.size // 2)
+        sc = kmeans(data[ids], sub_k, iters, seed)
+        sa = assign(data[ids], sc)
+        kids = [(ids[sa == c], sc[c]) for c in range(sub_k) if np.any(sa == c)]
+        (done if len(kids) == 1 else queue).extend(kids)
+    out_a = np.empty(n, np.int32)
+    for c, (ids, _) in enumerate(done):
+        out_a[ids] = c
+    return out_a, np.stack([c for _, c in done]).astype(np.float32)

@@ -243,6 +243,41 @@ def test_build_steps_match_oracle(fg):
         np.testing.assert_array_equal(got[k], eidx[k])
 
 
+def test_rebalance_bit_exact(fg):
+    from tests.test_oracle_cpu import skewed_lists
+    x, a, cen = skewed_lists()
+    na, nc = fg.rebalance_lists(torch.from_numpy(x).cuda(), torch.from_numpy(a).cuda(), torch.from_numpy(cen).cuda())
+    ea, ec = oracle.rebalance(x, a, cen)
+    assert ec.shape[0] > np.unique(a).size
+    np.testing.assert_array_equal(_np(na), ea)
+    np.testing.assert_array_equal(_np(nc), ec)
+    # identical points: the split loop must end
+    z = np.zeros((400, 8), np.float32)
+    z[:40] = 1.0
+    zc = oracle.kmeans(z, 8, 2)
+    za = oracle.assign(z, zc)
+    na, nc = fg.rebalance_lists(torch.from_numpy(z).cuda(), torch.from_numpy(za).cuda(), torch.from_numpy(zc).cuda())
+    ea, ec = oracle.rebalance(z, za, zc)
+    np.testing.assert_array_equal(_np(na), ea)
+    np.testing.assert_array_equal(_np(nc), ec)
+
+
+def test_rebalanced_build_bit_exact(fg):
+    # blobs of unequal spread: two k-means steps leave lists above twice the mean
+    rng = np.random.default_rng(7)
+    centres = rng.normal(0, 4, size=(3, 64))
+    base = np.concatenate([rng.normal(centres[0], 0.5, size=(5000, 64)),
+                           rng.normal(centres[1], 1.0, size=(2000, 64)),
+                           rng.normal(centres[2], 3.0, size=(1000, 64))]).astype(np.float32)
+    base = np.ascontiguousarray(base[rng.permutation(base.shape[0])])
+    idx = fg.IVFPQIndex.build(torch.from_numpy(base).cuda(), 32, 16, kmeans_iters=2, pq_sample=4000, pq_iters=3)
+    eidx, _ = oracle.build_index(base, 32, 16, kmeans_iters=2, pq_sample=4000, pq_iters=3)
+    assert eidx["centroids"].shape[0] > 32
+    got = idx.to_numpy()
+    for k in ("centroids", "codebook", "offsets", "ids", "codes"):
+        np.testing.assert_array_equal(got[k], eidx[k])
+
+
 def test_errors_are_reported(fg):
     from fusiongpu_b200 import _lib
     index, base, q = dataset("int128")

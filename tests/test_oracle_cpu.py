@@ -144,3 +144,38 @@ def test_pq_training_quality_matches_reference_pq_utils():
     rc = oracle.ref_pq_encode(base, a, cen, ref)
     oc = oracle.pq_encode(base, a, cen, ref)
     assert (rc == oc).mean() > 0.999
+
+
+def skewed_lists(seed=3, n=12000, k=16):
+    """k-means lists with lists 0-4 merged into list 0 (about five times the
+    mean; lists 1-4 empty), so that rebalancing has to split."""
+    rng = np.random.default_rng(seed)
+    x = np.ascontiguousarray(rng.normal(size=(n, 32)), dtype=np.float32)
+    cen = oracle.kmeans(x, k, 4)
+    a = oracle.assign(x, cen)
+    a[a < 5] = 0
+    return x, a, cen
+
+
+def test_rebalance_matches_python_restatement():
+    x, a, cen = skewed_lists()
+    na, nc = oracle.rebalance(x, a, cen)
+    ra, rc = refpy.rebalance(x, a, cen, oracle.kmeans, oracle.assign)
+    np.testing.assert_array_equal(na, ra)
+    np.testing.assert_array_equal(nc, rc)
+    lens = np.bincount(na, minlength=nc.shape[0])
+    assert nc.shape[0] > np.unique(a).size and lens.min() > 0
+    assert (lens <= int(2 * x.shape[0] / 16)).all()
+
+
+def test_rebalance_stops_on_identical_points():
+    # every point equal: each split would put all points in child 0 again
+    x = np.zeros((400, 8), np.float32)
+    x[:40] = 1.0
+    cen = oracle.kmeans(x, 8, 2)
+    a = oracle.assign(x, cen)
+    na, nc = oracle.rebalance(x, a, cen)
+    ra, rc = refpy.rebalance(x, a, cen, oracle.kmeans, oracle.assign)
+    np.testing.assert_array_equal(na, ra)
+    np.testing.assert_array_equal(nc, rc)
+    assert np.bincount(na).sum() == 400

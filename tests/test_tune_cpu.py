@@ -1,0 +1,117 @@
+"""Tuner and C++ host layer checks that need no GPU: the elbow rule of the
+product and of the oracle against the reference's own find_elbow_point, the
+oracle's tuner against golden vectors from the reference's tuner, and the C++
+programs / compat header building and starting."""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+from fusiongpu_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden", "ref_tune.npz")
+BIN = os.path.join(ROOT, "fusiongpu_b200", "bin")
+
+
+def histograms(n_cases=300):
+    """Seeded hits-per-rank curves: decaying with noise, rebounds, flat runs,
+    zeros, and the degenerate empty / all-zero cases."""
+    rng = np.random.default_rng(2024)
+    out = [np.zeros(0, np.int32), np.zeros(5, np.int32), np.array([7], np.int32), np.array([3, 3], np.int32)]
+    for _ in range(n_cases):
+        n = int(rng.integers(1, 70))
+        decay = rng.uniform(0.3, 0.97)
+        h = rng.uniform(50, 3000) * decay ** np.arange(n) * rng.uniform(0.5, 1.5, n)
+        if rng.random() < 0.3:
+            h[rng.integers(0, n)] *= rng.uniform(2, 10)
+        if rng.random() < 0.2:
+            h[rng.random(n) < 0.3] = 0
+        out.append(np.floor(h).astype(np.int32))
+    return out
+
+
+def _product_elbow(h):
+    pt, cov = C.c_int32(0), C.c_float(0)
+    _lib.call("fg_tune_elbow", C.c_void_p(h.ctypes.data), h.size, int(h.sum()), C.byref(pt), C.byref(cov))
+    return pt.value, cov.value
+
+
+def _oracle_elbow(h):
+    pt, cov = C.c_int(0), C.c_float(0)
+    oracle.lib().fgo_tune_elbow(C.c_void_p(h.ctypes.data), h.size, C.c_int64(int(h.sum())), C.byref(pt),
+                                C.byref(cov))
+    return pt.value, cov.value
+
+
+def test_elbow_product_matches_oracle():
+    for h in histograms():
+        h = np.ascontiguousarray(h)
+        assert _product_elbow(h) == _oracle_elbow(h), h
+
+
+def test_elbow_matches_reference():
+    L = oracle.ref_lib("tune", 64, 16)
+    if L is None:
+        pytest.skip("oracle/_ref not built")
+    L.ref_elbow.restype = C.c_int
+    for h in histograms():
+        h = np.ascontiguousarray(h)
+        if h.sum() == 0 or h.size == 0:
+            continue  # the reference returns 1 without touching coverage; covered by the oracle test
+        cov = C.c_float(0)
+        p = L.ref_elbow(C.c_void_p(h.ctypes.data), h.size, int(h.sum()), C.byref(cov))
+        assert (p, cov.value) == _product_elbow(h), h
+
+
+def test_tune_oracle_matches_reference_golden():
+    if not os.path.exists(GOLDEN):
+        pytest.skip("tests/golden/ref_tune.npz not generated")
+    f = np.load(GOLDEN)
+    index = {k[len("index_"):]: f[k] for k in f.files if k.startswith("index_")}
+    base, rows, k = f["base"], f["rows"], int(f["k"])
+    q = np.ascontiguousarray(base[rows])
+    gt, _ = oracle.knn_exact(base, q, k)
+    res, cr, pr, er, ra = oracle.tune(index, base, q, gt)
+    assert res["top_m"] == int(f["ref_top_m"])
+    assert res["p1_lists"] == int(f["ref_p1_lists"])
+    assert res["limit_k"] == int(f["ref_limit_k"])
+    assert np.float32(res["threshold_coeff"]) == f["ref_threshold_coeff"]
+    np.testing.assert_array_equal(cr[cr > 0], f["ref_cluster_ranks"])
+    np.testing.assert_array_equal(pr[pr > 0], f["ref_pq_ranks"])
+    np.testing.assert_array_equal(er[er > 0], f["ref_exact_ranks"])
+    np.testing.assert_array_equal(ra[~np.isnan(ra)], f["ref_ratios"])
+
+
+@pytest.mark.parametrize("prog", ["fg_build_global", "fg_search_pipeline", "fg_tune_parameters"])
+def test_programs_start_and_print_usage(prog):
+    exe = os.path.join(BIN, prog)
+    if not os.path.exists(exe):
+        from fusiongpu_b200 import build
+        build.programs()
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1 and "Usage" in r.stderr
+
+
+def test_compat_header_compiles_for_reference_callers(tmp_path):
+    src = os.path.join(ROOT, "tests", "compat", "compat_search.cpp")
+    for dim, m in ((128, 32), (64, 16)):
+        r = subprocess.run(["/usr/bin/g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only",
+                            f"-DDIM={dim}", f"-DPQ_M={m}", "-I", os.path.join(ROOT, "include"),
+                            "-I", os.path.join(ROOT, "fusiongpu_b200", "host"), "-I", "/usr/local/cuda/include", src],
+                           capture_output=True, text=True, timeout=120)
+        assert r.returncode == 0, r.stderr
+
+
+def test_compat_header_compiles_with_reference_defs():
+    defs = os.path.join(os.environ.get("FG_REFERENCE_DIR", "/root/reference"), "defs.h")
+    if not os.path.exists(defs):
+        pytest.skip("reference sources not present")
+    src = os.path.join(ROOT, "tests", "compat", "compat_search.cpp")
+    r = subprocess.run(["/usr/bin/g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-include", defs,
+                        "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "fusiongpu_b200", "host"),
+                        "-I", "/usr/local/cuda/include", src], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
