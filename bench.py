@@ -50,6 +50,8 @@ def parse():
                     help="build the index, then run only this stage warmup+1 times (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
+    ap.add_argument("--workload", default="C2", choices=["C2", "C4"],
+                    help="C2: IVF-PQ headline (default); C4: graph index (1M x 768 fp16, IP)")
     return ap.parse_args()
 
 
@@ -145,6 +147,8 @@ def setup(device, quick):
 
 def main():
     args = parse()
+    if args.workload == "C4":
+        return main_c4(args)
     if args.impl == "reference":
         return main_reference(args)
     import torch
@@ -440,6 +444,147 @@ def main_reference(args):
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
+
+
+# ---- C4: graph index ------------------------------------------------------------
+
+# the IVF partition doubles as the entry index of the search: finer than the
+# mixture's 2000 clusters, so that a list's medoid lies in the list's own cluster
+C4_BUILD = dict(graph_degree=64, intermediate_degree=128, nlist=4096, probe_lists=8, kmeans_iters=10, seed=42,
+                metric="ip")
+C4_SEARCH = dict(itopk=128, search_width=4, max_iterations=0, k=10, seed=7, metric="ip", entry_probes=16)
+C4_SWEEP = (32, 64, 128, 256)
+
+
+def main_c4(args):
+    """C4: QPS and recall@10 of the graph search (batch of 10,000 fp16
+    queries, itopk 128, search width 4) on a degree-64 graph over 1M x 768
+    fp16 unit vectors (inner product); itopk swept for the recall curve.  A
+    step is one search of the whole batch."""
+    import torch
+    from fusiongpu_b200 import datasets as ds
+    from fusiongpu_b200.graph import GraphBuildParams, GraphIndex, GraphSearchParams, knn_ip
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    spec = ds.scaled(ds.C4, 100_000, 2_000, n_centres=200) if args.quick else ds.C4
+    t0 = time.time()
+    base, queries = ds.generate(spec)
+    t_gen = time.time() - t0
+    print(f"[c4] generated {spec.n_base} x {spec.dim} in {t_gen:.1f} s", file=sys.stderr, flush=True)
+    xb = torch.from_numpy(base).to(device)
+    bp = dict(C4_BUILD, nlist=512 if args.quick else C4_BUILD["nlist"])
+    torch.cuda.synchronize(device)
+    t0 = time.time()
+    gi = GraphIndex.build(xb, GraphBuildParams(**bp))
+    torch.cuda.synchronize(device)
+    t_build = time.time() - t0
+    print(f"[c4] graph built in {t_build:.1f} s", file=sys.stderr, flush=True)
+    qd = torch.from_numpy(queries).to(device)
+    gt, _ = knn_ip(xb, qd, 10)
+    gt = gt.cpu().numpy()
+    nq = queries.shape[0]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    sweep = []
+    clocks = ClockSampler(local)
+    with clocks:
+        for itopk in C4_SWEEP:
+            print(f"[c4] itopk {itopk}", file=sys.stderr, flush=True)
+            sp = GraphSearchParams(**dict(C4_SEARCH, itopk=itopk))
+            for _ in range(args.warmup):
+                ids, dd, cnt = gi.search(qd, sp, counters=True)
+            torch.cuda.synchronize(device)
+            got = ids.cpu().numpy()
+            rec = float(np.mean([len(set(got[i]) & set(gt[i])) / 10 for i in range(nq)]))
+            evals, expanded, bad = (int(v) for v in cnt.cpu().numpy())
+            if bad:
+                raise RuntimeError(f"graph search skipped {bad} out-of-range accesses")
+            tot = 0.0
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                gi.search(qd, sp)
+                e1.record(stream)
+                e1.synchronize()
+                tot += e0.elapsed_time(e1)
+            ms = tot / args.steps
+            alg = evals * spec.dim * 2 + expanded * bp["graph_degree"] * 4
+            sweep.append(dict(itopk=itopk, recall=rec, ms_per_step=ms, qps=nq / (ms / 1e3),
+                              distance_evals_per_query=evals / nq, expanded_per_query=expanded / nq,
+                              algorithmic_bytes=alg, achieved_gbs=alg / (ms / 1e3) / 1e9))
+    op = next(s for s in sweep if s["itopk"] == C4_SEARCH["itopk"])
+    # end to end: pinned fp16 queries in, ids out
+    sp = GraphSearchParams(**C4_SEARCH)
+    hq = torch.from_numpy(queries).pin_memory()
+    hid = torch.empty((nq, sp.k), dtype=torch.int32).pin_memory()
+    qdev = torch.empty_like(qd)
+    tot = 0.0
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        qdev.copy_(hq, non_blocking=True)
+        ids, _ = gi.search(qdev, sp)
+        hid.copy_(ids, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= args.warmup:
+            tot += e0.elapsed_time(e1)
+    e2e = nq / (tot / args.steps / 1e3)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    out = {
+        "metric": "QPS of the C4 graph search (itopk 128, search width 4) with its recall@10",
+        "value": op["qps"],
+        "unit": "queries/s",
+        "recall@10": op["recall"],
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": op["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded Gaussian mixture: 2000 N(0,I) centres, sigma 0.3, normalised, fp16)",
+        "config": dict(workload=f"{spec.name}: {spec.n_base} x {spec.dim} fp16, {nq} queries, inner product",
+                       build=bp, search=C4_SEARCH, itopk_sweep=list(C4_SWEEP),
+                       l2="flushed (256 MB write) between timed steps", quick=bool(args.quick)),
+        "sweep": sweep,
+        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * sp.k * 4)},
+        "gpu_launches": args.steps * len(sweep),
+        "roofline": {"kernel": "graph_search_kernel", "bound": "hbm", "achieved": op["achieved_gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": op["achieved_gbs"] / peak,
+                     "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "traffic": None,
+                     "algorithmic_bytes": op["algorithmic_bytes"],
+                     "bytes_rule": "distance evals x dim x 2 + expanded nodes x degree x 4 (device counters)"},
+        "clocks": clocks.summary(),
+        "build_s": t_build,
+        "generate_s": t_gen,
+    }
+    if not args.no_cpu:
+        import oracle
+        sample = 200 if not args.quick else 100
+        g = gi.graph.cpu().numpy()
+        qs = np.ascontiguousarray(queries[:sample])
+        cores = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        oracle.graph_search(base, g, qs, nthreads=cores, entry_centroids=gi.entry_centroids.cpu().numpy(),
+                            entry_nodes=gi.entry_nodes.cpu().numpy(), **C4_SEARCH)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+                               "sample": f"first {sample} queries, same graph and parameters (oracle restatement)",
+                               "seconds": dt}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":

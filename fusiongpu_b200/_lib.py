@@ -40,6 +40,16 @@ class TuneResult(C.Structure):
                 ("n_in_p1", C.c_int32), ("n_ratios", C.c_int32)]
 
 
+class GraphBuildParams(C.Structure):
+    _fields_ = [("graph_degree", C.c_int32), ("intermediate_degree", C.c_int32), ("nlist", C.c_int32),
+                ("probe_lists", C.c_int32), ("kmeans_iters", C.c_int32), ("seed", C.c_uint32), ("metric", C.c_int32)]
+
+
+class GraphSearchParams(C.Structure):
+    _fields_ = [("itopk", C.c_int32), ("search_width", C.c_int32), ("max_iterations", C.c_int32), ("k", C.c_int32),
+                ("seed", C.c_uint32), ("metric", C.c_int32), ("entry_probes", C.c_int32)]
+
+
 # name -> argtypes (all return int status unless noted)
 _P, _I32, _I64, _U32, _F, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_uint32, C.c_float, C.c_size_t
 _SIGS = {
@@ -70,6 +80,11 @@ _SIGS = {
     "fg_tune": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, _P, _I32, C.POINTER(TuneResult), _P, _P, _P, _P, _P],
     "fg_tune_elbow": [_P, _I32, _I64, C.POINTER(_I32), C.POINTER(_F)],
     "fg_knn_workspace_size": [_I64, _I32, _I32, _I32, C.POINTER(_SZ)],
+    "fg_graph_build": [_P, _I32, _I64, _I32, C.POINTER(GraphBuildParams), _P, _P, _P, _P],
+    "fg_graph_search_workspace_size": [_I32, _I32, _I32, _I32, C.POINTER(GraphSearchParams), C.POINTER(_SZ)],
+    "fg_graph_search": [_P, _I32, _I64, _I32, _P, _I32, _P, _P, _I32, _P, _I32, C.POINTER(GraphSearchParams), _P, _P,
+                        _P, _P, _SZ, _P],
+    "fg_knn": [_P, _I64, _I32, _P, _I32, _I32, _I32, _P, _P, _P, _SZ, _P],
     "fg_knn_exact": [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P],
 }
 

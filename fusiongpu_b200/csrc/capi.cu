@@ -40,7 +40,7 @@ int batch_logic(const fg_ivfpq_view*, const float*, int, const uint32_t*, const 
 int rerank(const float*, int, int, const int32_t*, const int32_t*, const float*, long long, const fg_search_params*,
            int32_t*, float*, cudaStream_t);
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
-             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s);
+             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s, int metric = FG_METRIC_L2);
 size_t knn_like_workspace(long long nq, int ncols, int k);
 int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int32_t* amin, cudaStream_t s);
 int kmeans_init(const float* data, int64_t n, int dim, int k, uint32_t seed, float* centroids, int64_t* d_rows,
@@ -334,15 +334,21 @@ int fg_knn_workspace_size(int64_t nbase, int32_t dim, int32_t nq, int32_t k, siz
     return FG_OK;
 }
 
-int fg_knn_exact(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq, int32_t k,
-                 int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes, void* stream) {
+int fg_knn(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq, int32_t k, int32_t metric,
+           int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes, void* stream) {
     FG_REQUIRE(nbase >= 1 && nbase <= 0x7fffffffll && dim >= 1 && nq >= 0 && k >= 1 && k <= nbase && k <= 4096,
                "bad knn arguments");
+    FG_REQUIRE(metric == FG_METRIC_L2 || metric == FG_METRIC_IP, "unknown metric %d", metric);
     if (nq == 0) return FG_OK;
     FG_REQUIRE(base && queries && out_ids && out_dists, "null buffer");
     int rc = need_ws(ws, ws_bytes, 1024);
     if (rc) return rc;
-    return knn_like(base, nbase, dim, queries, nq, k, out_ids, out_dists, ws, ws_bytes, as_stream(stream));
+    return knn_like(base, nbase, dim, queries, nq, k, out_ids, out_dists, ws, ws_bytes, as_stream(stream), metric);
+}
+
+int fg_knn_exact(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq, int32_t k,
+                 int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes, void* stream) {
+    return fg_knn(base, nbase, dim, queries, nq, k, FG_METRIC_L2, out_ids, out_dists, ws, ws_bytes, stream);
 }
 
 }  // extern "C"

@@ -6,7 +6,8 @@
 //
 // Distances are sum_j fmaf(x_j - y_j, x_j - y_j, acc) in dimension order, the
 // same arithmetic the oracle uses, so rankings match it exactly (ties broken
-// by the lower column index).
+// by the lower column index).  The inner-product metric (graph build and its
+// ground truth) uses -(sum_j fmaf(x_j, y_j, acc)) so that smaller is nearer.
 #include <algorithm>
 
 #include "fg_common.cuh"
@@ -24,8 +25,9 @@ enum { EPI_MATRIX = 0, EPI_ARGMIN = 1 };
 
 // Each CTA owns 64 rows of X; blockIdx.y picks a run of `ytiles` 64-row tiles
 // of Y.  EPI_MATRIX writes D[x][y] (row stride ldd); EPI_ARGMIN keeps the
-// nearest y per x row (grid.y must be 1) and writes amin[x].
-template <int EPI>
+// nearest y per x row (grid.y must be 1) and writes amin[x].  METRIC is
+// FG_METRIC_L2 or FG_METRIC_IP.
+template <int EPI, int METRIC = FG_METRIC_L2>
 __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict__ X, long long nx,
                                                         const float* __restrict__ Y, int ny, int dim,
                                                         float* __restrict__ D, long long ldd,
@@ -74,11 +76,21 @@ __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict_
                 for (int a = 0; a < 4; ++a)
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
-                        const float df = xa[a] - yb[b];
-                        acc[a][b] = fmaf(df, df, acc[a][b]);
+                        if (METRIC == FG_METRIC_IP) {
+                            acc[a][b] = fmaf(xa[a], yb[b], acc[a][b]);
+                        } else {
+                            const float df = xa[a] - yb[b];
+                            acc[a][b] = fmaf(df, df, acc[a][b]);
+                        }
                     }
             }
             __syncthreads();
+        }
+        if (METRIC == FG_METRIC_IP) {
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = -acc[a][b];
         }
         if (EPI == EPI_MATRIX) {
 #pragma unroll
@@ -229,11 +241,14 @@ size_t rows_topk_stage_bytes(long long rows, int ncols, int k) {
 }
 
 int l2_matrix(const float* X, long long nx, const float* Y, int ny, int dim, float* D, long long ldd,
-              cudaStream_t s) {
+              cudaStream_t s, int metric = FG_METRIC_L2) {
     if (nx <= 0 || ny <= 0) return FG_OK;
     const int nyt = (ny + L2_T - 1) / L2_T;
     dim3 grid((unsigned)((nx + L2_T - 1) / L2_T), nyt);
-    l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
+    if (metric == FG_METRIC_IP)
+        l2_tile_kernel<EPI_MATRIX, FG_METRIC_IP><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
+    else
+        l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
     return check_launch("l2_tile_kernel(matrix)");
 }
 
@@ -267,7 +282,7 @@ size_t knn_like_workspace(long long nq, int ncols, int k) {
 }
 
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
-             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s) {
+             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s, int metric) {
     FG_REQUIRE(ny <= 0x7fffffffll, "too many columns");
     const int ncols = (int)ny;
     long long rows = chunk_rows(ws_bytes, nq, ncols, k);
@@ -281,7 +296,7 @@ int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq
         float* sv = nseg > 1 ? cv.take<float>((size_t)r * nseg * k) : nullptr;
         int32_t* si = nseg > 1 ? cv.take<int32_t>((size_t)r * nseg * k) : nullptr;
         if (!cv.ok()) return fail(FG_ERR_WORKSPACE, "workspace too small");
-        int rc = l2_matrix(Q + q0 * dim, r, Y, ncols, dim, D, ncols, s);
+        int rc = l2_matrix(Q + q0 * dim, r, Y, ncols, dim, D, ncols, s, metric);
         if (rc) return rc;
         rc = rows_topk(D, ncols, r, ncols, k, out_i + q0 * k, out_v + q0 * k, k, sv, si, s);
         if (rc) return rc;

@@ -30,7 +30,7 @@
 namespace fg {
 
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
-             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s);
+             float* out_v, void* ws, size_t ws_bytes, cudaStream_t s, int metric = FG_METRIC_L2);
 
 constexpr size_t kNoAllocScratchBytes = 16u << 20;
 constexpr int kNoAllocMaxDevices = 64;

@@ -25,6 +25,19 @@ extern "C" {
 
 #define FG_INVALID_PROBE 0xFFFFFFFFu
 
+/* Distance used by the exact k-NN and the graph index: squared L2, or the
+ * negated inner product (smaller is nearer in both). */
+typedef enum {
+    FG_METRIC_L2 = 0,
+    FG_METRIC_IP = 1
+} fg_metric;
+
+/* Element type of the graph index's vectors. */
+typedef enum {
+    FG_DTYPE_F32 = 0,
+    FG_DTYPE_F16 = 1
+} fg_dtype;
+
 typedef enum {
     FG_OK = 0,
     FG_ERR_INVALID_ARG = 1,   /* a size, pointer or parameter is out of range         */
@@ -201,6 +214,78 @@ int fg_tune(const fg_ivfpq_view* index, const float* base, int64_t nbase, const 
  * elbow rank and the coverage there. */
 int fg_tune_elbow(const int32_t* hits, int32_t n, int64_t total, int32_t* point, float* coverage);
 
+/* ---- graph index (no counterpart in the reference, whose only graph is
+ * cuVS CAGRA over its centroids, cagra_adapter.cuh:10-68): a fixed-degree
+ * k-NN graph after the CAGRA design, for the C4 configuration.
+ *
+ * fg_graph_build: 1. IVF partition of the data (fg_kmeans with nlist lists,
+ * kmeans_iters steps, seed; exact assignment).  2. Initial graph of degree
+ * intermediate_degree: each point's exact nearest neighbours (metric) among
+ * the members of its list's probe_lists nearest lists (itself dropped, ties
+ * by id).  3. Pruning to graph_degree: neighbour v_i (rank i) of u scores the
+ * number of detours u->v_j->v_i with j < i and rank(v_i in N(v_j)) < i;
+ * fewest detours first, ties by rank.  4-5. Final list: the first
+ * graph_degree/2 pruned neighbours, then up to graph_degree/2 reverse
+ * neighbours (sources u ordered by (rank, u)), then the rest of the pruned
+ * list, without duplicates; -1 pads.  data: [n][dim] of dtype (device);
+ * graph: [n][graph_degree] int32 (device).  Optional entry points for the
+ * search (device, may be NULL): entry_centroids [nlist][dim] float (the IVF
+ * centroids) and entry_nodes [nlist] (each list's member nearest its
+ * centroid by the metric, ties by id; -1 for an empty list).  Synchronises;
+ * allocates its own scratch. */
+typedef struct {
+    int32_t graph_degree;         /* D, even (64)                             */
+    int32_t intermediate_degree;  /* initial k-NN degree, >= D (128)          */
+    int32_t nlist;                /* IVF lists that supply the candidates     */
+    int32_t probe_lists;          /* lists whose members are candidates       */
+    int32_t kmeans_iters;
+    uint32_t seed;
+    int32_t metric;               /* fg_metric                                */
+} fg_graph_build_params;
+
+int fg_graph_build(const void* data, int32_t dtype, int64_t n, int32_t dim,
+                   const fg_graph_build_params* params, int32_t* graph,
+                   float* entry_centroids, int32_t* entry_nodes, void* stream);
+
+/* fg_graph_search: CTA per query.  A top list of itopk (distance, id)
+ * entries is seeded with search_width*degree start nodes: the entry nodes of
+ * the query's entry_probes nearest entry centroids (exact metric distance,
+ * fmaf in dimension order, ties by list id; selected for the whole batch by
+ * one tiled pass before the search), then pseudo-random nodes (murmur3
+ * finaliser of seed, query and slot) for the remaining slots.  Each
+ * iteration expands the first search_width unexplored entries: their
+ * neighbours not yet visited (open-addressing hash of 8192 slots in shared
+ * memory, reset to the top list when half full) get distances (one warp per
+ * vector, 16-byte loads, lane-strided fmaf then a fixed xor-butterfly sum)
+ * and are merged in by (distance, id).  Stops when no unexplored entry
+ * remains or after max_iterations (0: 2*ceil(itopk / search_width) + 10).
+ * data / queries: [n][dim] / [nq][dim] of dtype, rows 16 bytes aligned (dim
+ * multiple of 8 for f16, 4 for f32); entry_centroids / entry_nodes /
+ * n_entries as fg_graph_build writes them (NULL / 0 when entry_probes is 0);
+ * out_ids/out_dists [nq][k] ascending (IP distance = -dot).  counters
+ * (device, may be NULL): [0] += distance evaluations, [1] += expanded nodes,
+ * [2] += index checks that failed (a graph entry or buffer index out of
+ * range; the access is skipped, so a corrupt graph gives wrong results
+ * instead of a fault).  The workspace (fg_graph_search_workspace_size) holds
+ * the entry selection; none is needed when entry_probes is 0. */
+typedef struct {
+    int32_t itopk;           /* internal top-list size (128)        */
+    int32_t search_width;    /* parents per iteration (4)           */
+    int32_t max_iterations;  /* 0 = automatic                       */
+    int32_t k;               /* results per query, <= itopk         */
+    uint32_t seed;           /* pseudo-random start nodes           */
+    int32_t metric;          /* fg_metric                           */
+    int32_t entry_probes;    /* nearest entry lists seeded (0: none), <= 4096 */
+} fg_graph_search_params;
+
+int fg_graph_search_workspace_size(int32_t dtype, int32_t dim, int32_t nq, int32_t n_entries,
+                                   const fg_graph_search_params* params, size_t* bytes);
+int fg_graph_search(const void* data, int32_t dtype, int64_t n, int32_t dim, const int32_t* graph,
+                    int32_t degree, const float* entry_centroids, const int32_t* entry_nodes,
+                    int32_t n_entries, const void* queries, int32_t nq,
+                    const fg_graph_search_params* params, int32_t* out_ids, float* out_dists,
+                    uint64_t* counters, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- index build (device pointers; the reference takes host pointers) ----- */
 
 /* Strided k-means seeding: centroid i = data[(i*stride + r_i % stride) % n],
@@ -274,6 +359,11 @@ int fg_knn_workspace_size(int64_t nbase, int32_t dim, int32_t nq, int32_t k, siz
 int fg_knn_exact(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq,
                  int32_t k, int32_t* out_ids, float* out_dists, void* workspace,
                  size_t workspace_bytes, void* stream);
+/* The same with a metric: FG_METRIC_IP ranks by -(q . x) (sum of fmaf in
+ * dimension order, negated), written to out_dists. */
+int fg_knn(const float* base, int64_t nbase, int32_t dim, const float* queries, int32_t nq,
+           int32_t k, int32_t metric, int32_t* out_ids, float* out_dists, void* workspace,
+           size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

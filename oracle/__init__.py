@@ -335,3 +335,46 @@ def ref_pq_encode(data, assignment, centroids, codebook):
                            _p(np.ascontiguousarray(centroids, np.float32)), centroids.shape[0],
                            _p(np.ascontiguousarray(codebook, np.float32)), _p(codes)), "ref_pq_encode")
     return codes
+
+
+def graph_build(data, graph_degree=64, intermediate_degree=128, nlist=64, probe_lists=4, kmeans_iters=10, seed=42,
+                metric="ip", nthreads=0, entries=False):
+    """The product's graph build restated on the CPU (fp32 data).  With
+    entries=True also returns the entry centroids and entry nodes."""
+    data = np.ascontiguousarray(data, np.float32)
+    n, dim = data.shape
+    g = np.empty((n, graph_degree), np.int32)
+    ec = np.empty((nlist, dim), np.float32)
+    en = np.empty(nlist, np.int32)
+    _check(lib().fgo_graph_build(_p(data), C.c_int64(n), dim, graph_degree, intermediate_degree, nlist, probe_lists,
+                                 kmeans_iters, C.c_uint32(seed), 1 if metric == "ip" else 0, _p(g), _p(ec), _p(en),
+                                 nthreads), "graph_build")
+    return (g, ec, en) if entries else g
+
+
+def graph_search(data, graph, queries, itopk=128, search_width=4, max_iterations=0, k=10, seed=7, metric="ip",
+                 nthreads=0, entry_centroids=None, entry_nodes=None, entry_probes=0):
+    """The product's graph search restated on the CPU.  data/queries are
+    float32 or float16 arrays.  Returns (ids, dists, [evals, expanded])."""
+    dtype = 1 if data.dtype == np.float16 else 0
+    data = np.ascontiguousarray(data, np.float16 if dtype else np.float32)
+    queries = np.ascontiguousarray(queries, np.float16 if dtype else np.float32)
+    graph = np.ascontiguousarray(graph, np.int32)
+    n, dim = data.shape
+    nq = queries.shape[0]
+    oi = np.empty((nq, k), np.int32)
+    od = np.empty((nq, k), np.float32)
+    cnt = np.zeros(2, np.uint64)
+    if entry_probes:
+        ec = np.ascontiguousarray(entry_centroids, np.float32)
+        en = np.ascontiguousarray(entry_nodes, np.int32)
+        ne = en.size
+    else:
+        ec = np.zeros((1, dim), np.float32)
+        en = np.zeros(1, np.int32)
+        ne = 0
+    _check(lib().fgo_graph_search(_p(data), dtype, C.c_int64(n), dim, _p(graph), graph.shape[1], _p(ec), _p(en), ne,
+                                  entry_probes, _p(queries), nq, itopk, search_width, max_iterations, k,
+                                  C.c_uint32(seed), 1 if metric == "ip" else 0, _p(oi), _p(od), _p(cnt), nthreads),
+           "graph_search")
+    return oi, od, cnt

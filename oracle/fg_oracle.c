@@ -992,3 +992,381 @@ int fgo_tune(const fgo_index* idx, const float* base, int64_t nbase, const float
     free(ranks); free(hits); free(allq);
     return 0;
 }
+
+/* ---- graph index (the product's CAGRA-style build and search) ---------------
+ * No reference implementation exists (the reference's only graph is cuVS
+ * CAGRA over its centroids, a library absent here); this restates the
+ * product's documented algorithm step by step so the CUDA kernels can be
+ * checked bit for bit. */
+
+static float half_bits_to_float(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff, bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else { /* subnormal: normalise */
+            int sh = 0;
+            while (!(m & 0x400)) { m <<= 1; ++sh; }
+            m &= 0x3ff;
+            bits = sign | ((uint32_t)(127 - 15 + 1 - sh) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 127 - 15) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static float dist_metric(const float* a, const float* b, int dim, int metric) {
+    if (metric == 1) {
+        float acc = 0.0f;
+        for (int j = 0; j < dim; ++j) acc = fmaf(a[j], b[j], acc);
+        return -acc;
+    }
+    return l2_seq(a, b, dim);
+}
+
+typedef struct {
+    float d;
+    int32_t id;
+} fgo_did;
+
+static int cmp_did(const void* x, const void* y) {
+    const fgo_did* a = (const fgo_did*)x;
+    const fgo_did* b = (const fgo_did*)y;
+    if (a->d < b->d) return -1;
+    if (b->d < a->d) return 1;
+    return (a->id > b->id) - (a->id < b->id);
+}
+
+static int cmp_u32(const void* x, const void* y) {
+    uint32_t a = *(const uint32_t*)x, b = *(const uint32_t*)y;
+    return (a > b) - (a < b);
+}
+
+int fgo_graph_build(const float* data, int64_t n, int dim, int D, int I, int L, int P, int iters,
+                    uint32_t seed, int metric, int32_t* graph, float* entry_centroids,
+                    int32_t* entry_nodes, int nthreads) {
+    if (n < 2 || D < 2 || (D & 1) || I < D || L < 1 || L > n || P < 1 || P > L) return 1;
+    float* cen = (float*)malloc((size_t)L * dim * sizeof(float));
+    int32_t* as = (int32_t*)malloc((size_t)n * sizeof(int32_t));
+    int32_t* order = (int32_t*)malloc((size_t)n * sizeof(int32_t));
+    int64_t* off = (int64_t*)calloc((size_t)L + 1, sizeof(int64_t));
+    int32_t* g0 = (int32_t*)malloc((size_t)n * I * sizeof(int32_t));
+    int32_t* pr = (int32_t*)malloc((size_t)n * D * sizeof(int32_t));
+    int32_t* nn = (int32_t*)malloc((size_t)L * P * sizeof(int32_t));
+    if (!cen || !as || !order || !off || !g0 || !pr || !nn) return 2;
+    int rc = fgo_kmeans(data, n, dim, L, iters, seed, cen, nthreads);
+    if (!rc) rc = fgo_assign(data, n, dim, cen, L, as, nthreads);
+    if (rc) return rc;
+    for (int64_t i = 0; i < n; ++i) off[as[i] + 1]++;
+    for (int c = 0; c < L; ++c) off[c + 1] += off[c];
+    {
+        int64_t* fill = (int64_t*)malloc((size_t)L * sizeof(int64_t));
+        memcpy(fill, off, (size_t)L * sizeof(int64_t));
+        for (int64_t i = 0; i < n; ++i) order[fill[as[i]]++] = (int32_t)i;
+        free(fill);
+    }
+    /* nearest lists of every list */
+    for (int c = 0; c < L; ++c) {
+        fgo_did* all = (fgo_did*)malloc((size_t)L * sizeof(fgo_did));
+        for (int c2 = 0; c2 < L; ++c2) {
+            all[c2].d = l2_seq(cen + (size_t)c * dim, cen + (size_t)c2 * dim, dim);
+            all[c2].id = c2;
+        }
+        qsort(all, (size_t)L, sizeof(fgo_did), cmp_did);
+        for (int j = 0; j < P; ++j) nn[(size_t)c * P + j] = all[j].id;
+        free(all);
+    }
+    /* initial k-NN graph */
+    for (int64_t i = 0; i < n * I; ++i) g0[i] = -1;
+    for (int c = 0; c < L; ++c) {
+        int lists[4096];
+        int nl = 0;
+        lists[nl++] = c;
+        for (int j = 0; j < P && nl < P; ++j)
+            if (nn[(size_t)c * P + j] != c) lists[nl++] = nn[(size_t)c * P + j];
+        int64_t nc = 0;
+        for (int l = 0; l < nl; ++l) nc += off[lists[l] + 1] - off[lists[l]];
+        uint32_t* cand = (uint32_t*)malloc((size_t)(nc > 0 ? nc : 1) * sizeof(uint32_t));
+        int64_t t = 0;
+        for (int l = 0; l < nl; ++l)
+            for (int64_t r = off[lists[l]]; r < off[lists[l] + 1]; ++r) cand[t++] = (uint32_t)order[r];
+        qsort(cand, (size_t)nc, sizeof(uint32_t), cmp_u32);
+        const int64_t kk = nc < I + 1 ? nc : I + 1;
+        set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 16)
+        for (int64_t r = off[c]; r < off[c + 1]; ++r) {
+            const int32_t self = order[r];
+            fgo_did* d = (fgo_did*)malloc((size_t)nc * sizeof(fgo_did));
+            for (int64_t j = 0; j < nc; ++j) {
+                d[j].d = dist_metric(data + (size_t)self * dim, data + (size_t)cand[j] * dim, dim, metric);
+                d[j].id = (int32_t)cand[j];
+            }
+            qsort(d, (size_t)nc, sizeof(fgo_did), cmp_did);
+            int o = 0;
+            for (int64_t j = 0; j < kk && o < I; ++j)
+                if (d[j].id != self) g0[(size_t)self * I + o++] = d[j].id;
+            free(d);
+        }
+        free(cand);
+    }
+    /* pruning by detour count */
+    set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t u = 0; u < n; ++u) {
+        const int32_t* nb = g0 + (size_t)u * I;
+        uint32_t* key = (uint32_t*)malloc((size_t)I * sizeof(uint32_t));
+        for (int i = 0; i < I; ++i) {
+            if (nb[i] < 0) {
+                key[i] = (0xffffu << 16) | (uint32_t)i;
+                continue;
+            }
+            int cnt = 0;
+            for (int j = 0; j < i; ++j) {
+                if (nb[j] < 0) continue;
+                const int32_t* wl = g0 + (size_t)nb[j] * I;
+                for (int x = 0; x < i; ++x)
+                    if (wl[x] == nb[i]) { ++cnt; break; }
+            }
+            key[i] = ((uint32_t)(cnt < 0xffff ? cnt : 0xffff) << 16) | (uint32_t)i;
+        }
+        qsort(key, (size_t)I, sizeof(uint32_t), cmp_u32);
+        for (int r = 0; r < D; ++r) pr[(size_t)u * D + r] = nb[key[r] & 0xffffu];
+        free(key);
+    }
+    /* reverse edges: for each v, sources u in (rank, u) order */
+    int64_t* rcount = (int64_t*)calloc((size_t)n + 1, sizeof(int64_t));
+    for (int i = 0; i < D; ++i)
+        for (int64_t u = 0; u < n; ++u) {
+            int32_t v = pr[(size_t)u * D + i];
+            if (v >= 0) rcount[v + 1]++;
+        }
+    for (int64_t v = 0; v < n; ++v) rcount[v + 1] += rcount[v];
+    int32_t* rsrc = (int32_t*)malloc((size_t)(rcount[n] > 0 ? rcount[n] : 1) * sizeof(int32_t));
+    int64_t* rfill = (int64_t*)malloc((size_t)n * sizeof(int64_t));
+    memcpy(rfill, rcount, (size_t)n * sizeof(int64_t));
+    for (int i = 0; i < D; ++i)
+        for (int64_t u = 0; u < n; ++u) {
+            int32_t v = pr[(size_t)u * D + i];
+            if (v >= 0) rsrc[rfill[v]++] = (int32_t)u;
+        }
+    /* final lists */
+    for (int64_t u = 0; u < n; ++u) {
+        int32_t* out = graph + (size_t)u * D;
+        const int32_t* pu = pr + (size_t)u * D;
+        int cnt = 0, half = D / 2, taken = 0;
+        for (int r = 0; r < half; ++r) {
+            int32_t v = pu[r], dup = 0;
+            for (int x = 0; x < cnt; ++x) dup |= out[x] == v;
+            if (v >= 0 && !dup) out[cnt++] = v;
+        }
+        for (int64_t e = rcount[u]; e < rcount[u + 1] && taken < D - half && cnt < D; ++e) {
+            int32_t v = rsrc[e], dup = 0;
+            for (int x = 0; x < cnt; ++x) dup |= out[x] == v;
+            if (!dup) { out[cnt++] = v; ++taken; }
+        }
+        for (int r = half; r < D && cnt < D; ++r) {
+            int32_t v = pu[r], dup = 0;
+            for (int x = 0; x < cnt; ++x) dup |= out[x] == v;
+            if (v >= 0 && !dup) out[cnt++] = v;
+        }
+        for (; cnt < D; ++cnt) out[cnt] = -1;
+    }
+    /* entry points: centroids and each list's medoid by the metric */
+    if (entry_centroids) memcpy(entry_centroids, cen, (size_t)L * dim * sizeof(float));
+    if (entry_nodes)
+        for (int c = 0; c < L; ++c) {
+            float best = FLT_MAX;
+            int32_t bid = -1;
+            for (int64_t r = off[c]; r < off[c + 1]; ++r) {
+                const int32_t id = order[r];
+                const float d = dist_metric(data + (size_t)id * dim, cen + (size_t)c * dim, dim, metric);
+                if (bid < 0 || d < best || (d == best && id < bid)) {
+                    best = d;
+                    bid = id;
+                }
+            }
+            entry_nodes[c] = bid;
+        }
+    free(rcount); free(rsrc); free(rfill);
+    free(cen); free(as); free(order); free(off); free(g0); free(pr); free(nn);
+    return 0;
+}
+
+static uint32_t gmix32(uint32_t h) {
+    h ^= h >> 16;
+    h *= 0x85ebca6bu;
+    h ^= h >> 13;
+    h *= 0xc2b2ae35u;
+    h ^= h >> 16;
+    return h;
+}
+
+/* one warp's distance: lane l sums its 16-byte chunks l, l+32, ... with fmaf,
+ * then the xor butterfly 16, 8, 4, 2, 1 */
+static float warp_dist_emul(const float* x, const float* q, int dim, int E, int metric) {
+    float v[32], w[32];
+    const int nch = dim / E;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int c = l; c < nch; c += 32)
+            for (int e = 0; e < E; ++e) {
+                const float a = x[c * E + e], b = q[c * E + e];
+                if (metric == 1) {
+                    acc = fmaf(a, b, acc);
+                } else {
+                    const float df = a - b;
+                    acc = fmaf(df, df, acc);
+                }
+            }
+        v[l] = acc;
+    }
+    for (int o = 16; o; o >>= 1) {
+        for (int l = 0; l < 32; ++l) w[l] = v[l] + v[l ^ o];
+        memcpy(v, w, sizeof(v));
+    }
+    return metric == 1 ? -v[0] : v[0];
+}
+
+static uint32_t fkey(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+static float fkey_inv(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static int cmp_u64(const void* x, const void* y) {
+    uint64_t a = *(const uint64_t*)x, b = *(const uint64_t*)y;
+    return (a > b) - (a < b);
+}
+
+#define FGO_GS_HASH 8192
+
+int fgo_graph_search(const void* data, int dtype, int64_t n, int dim, const int32_t* graph, int D,
+                     const float* entry_cen, const int32_t* entry_nodes, int n_entries,
+                     int entry_probes, const void* queries, int nq, int itopk, int width,
+                     int max_iter, int k, uint32_t seed, int metric, int32_t* out_ids,
+                     float* out_dists, uint64_t* counters, int nthreads) {
+    const int E = dtype == 1 ? 8 : 4;
+    if (dim % E || k < 1 || k > itopk || width < 1) return 1;
+    if (max_iter == 0) max_iter = 2 * ((itopk + width - 1) / width) + 10;
+    const int WD = width * D;
+    uint64_t evals = 0, expanded = 0;
+    set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : evals, expanded)
+    for (int q = 0; q < nq; ++q) {
+        float* qv = (float*)malloc((size_t)dim * sizeof(float));
+        float* xv = (float*)malloc((size_t)dim * sizeof(float));
+        uint8_t* vis = (uint8_t*)calloc((size_t)n, 1);
+        int32_t* vlist = (int32_t*)malloc((size_t)(FGO_GS_HASH + WD + itopk) * sizeof(int32_t));
+        uint64_t* top = (uint64_t*)malloc((size_t)itopk * sizeof(uint64_t));
+        uint8_t* ex = (uint8_t*)calloc((size_t)itopk, 1);
+        uint64_t* cand = (uint64_t*)malloc((size_t)WD * sizeof(uint64_t));
+        uint64_t* mt = (uint64_t*)malloc((size_t)itopk * sizeof(uint64_t));
+        uint8_t* me = (uint8_t*)malloc((size_t)itopk);
+        int32_t* slot = (int32_t*)malloc((size_t)WD * sizeof(int32_t));
+        int nvis = 0, ntop = 0;
+        for (int j = 0; j < dim; ++j)
+            qv[j] = dtype == 1 ? half_bits_to_float(((const uint16_t*)queries)[(size_t)q * dim + j])
+                               : ((const float*)queries)[(size_t)q * dim + j];
+        for (int iter = -1; iter < max_iter; ++iter) {
+            if (iter < 0) {
+                int S = 0;
+                if (entry_probes > 0 && n_entries > 0) {
+                    S = entry_probes < n_entries ? entry_probes : n_entries;
+                    if (S > WD) S = WD;
+                    fgo_dc* ed = (fgo_dc*)malloc((size_t)n_entries * sizeof(fgo_dc));
+                    for (int c = 0; c < n_entries; ++c) {
+                        ed[c].d = dist_metric(qv, entry_cen + (size_t)c * dim, dim, metric);
+                        ed[c].c = c;
+                    }
+                    qsort(ed, (size_t)n_entries, sizeof(fgo_dc), cmp_dc);
+                    for (int s = 0; s < S; ++s) slot[s] = entry_nodes[ed[s].c];
+                    free(ed);
+                }
+                for (int s = S; s < WD; ++s) {
+                    uint32_t x = gmix32(seed ^ gmix32((uint32_t)((int64_t)q * WD + s) * 0x9e3779b9u + 0x7f4a7c15u));
+                    slot[s] = (int32_t)((uint64_t)x % (uint64_t)n);
+                }
+            } else {
+                int32_t par[2048];
+                int np = 0;
+                for (int t = 0; t < ntop && np < width; ++t)
+                    if (!ex[t]) {
+                        par[np++] = (int32_t)(top[t] & 0xffffffffu);
+                        ex[t] = 1;
+                    }
+                if (np == 0) break;
+                expanded += (uint64_t)np;
+                if (nvis > FGO_GS_HASH / 2) {
+                    for (int x = 0; x < nvis; ++x) vis[vlist[x]] = 0;
+                    nvis = 0;
+                    for (int t = 0; t < ntop; ++t) {
+                        int32_t v = (int32_t)(top[t] & 0xffffffffu);
+                        vis[v] = 1;
+                        vlist[nvis++] = v;
+                    }
+                }
+                for (int s = 0; s < WD; ++s) {
+                    int pi = s / D;
+                    slot[s] = pi < np ? graph[(size_t)par[pi] * D + (s - pi * D)] : -1;
+                }
+            }
+            int m = 0;
+            for (int s = 0; s < WD; ++s) {
+                int32_t v = slot[s];
+                if (v < 0 || v >= n || vis[v]) continue;
+                vis[v] = 1;
+                vlist[nvis++] = v;
+                for (int j = 0; j < dim; ++j)
+                    xv[j] = dtype == 1 ? half_bits_to_float(((const uint16_t*)data)[(size_t)v * dim + j])
+                                       : ((const float*)data)[(size_t)v * dim + j];
+                float d = warp_dist_emul(xv, qv, dim, E, metric);
+                cand[m++] = ((uint64_t)fkey(d) << 32) | (uint32_t)v;
+            }
+            evals += (uint64_t)m;
+            qsort(cand, (size_t)m, sizeof(uint64_t), cmp_u64);
+            /* merge */
+            int i = 0, j = 0, r = 0;
+            while (r < itopk && (i < ntop || j < m)) {
+                if (i < ntop && (j >= m || top[i] < cand[j])) {
+                    mt[r] = top[i];
+                    me[r++] = ex[i++];
+                } else {
+                    mt[r] = cand[j++];
+                    me[r++] = 0;
+                }
+            }
+            ntop = r;
+            memcpy(top, mt, (size_t)r * sizeof(uint64_t));
+            memcpy(ex, me, (size_t)r);
+        }
+        for (int r = 0; r < k; ++r) {
+            if (r < ntop) {
+                out_ids[(size_t)q * k + r] = (int32_t)(top[r] & 0xffffffffu);
+                out_dists[(size_t)q * k + r] = fkey_inv((uint32_t)(top[r] >> 32));
+            } else {
+                out_ids[(size_t)q * k + r] = -1;
+                out_dists[(size_t)q * k + r] = FLT_MAX;
+            }
+        }
+        free(qv); free(xv); free(vis); free(vlist); free(top); free(ex); free(cand); free(mt); free(me);
+        free(slot);
+    }
+    if (counters) {
+        counters[0] = evals;
+        counters[1] = expanded;
+    }
+    return 0;
+}

@@ -104,6 +104,19 @@ int fgo_tune(const fgo_index* idx, const float* base, int64_t nbase, const float
              const int32_t* gt, int k, fgo_tune_result* out, int32_t* cluster_ranks,
              int32_t* pq_ranks, int32_t* exact_ranks, float* ratios, int nthreads);
 
+/* Graph index: the product's build and search, restated (fg_graph_build /
+ * fg_graph_search of the product's C ABI; no reference implementation).
+ * data for the build is fp32; for the search dtype 0 = fp32, 1 = fp16 bits.
+ * metric 0 = L2, 1 = inner product (distance = -dot). */
+int fgo_graph_build(const float* data, int64_t n, int dim, int D, int I, int L, int P, int iters,
+                    uint32_t seed, int metric, int32_t* graph, float* entry_centroids,
+                    int32_t* entry_nodes, int nthreads);
+int fgo_graph_search(const void* data, int dtype, int64_t n, int dim, const int32_t* graph, int D,
+                     const float* entry_cen, const int32_t* entry_nodes, int n_entries,
+                     int entry_probes, const void* queries, int nq, int itopk, int width,
+                     int max_iter, int k, uint32_t seed, int metric, int32_t* out_ids,
+                     float* out_dists, uint64_t* counters, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -194,3 +194,135 @@ def rebalance(data, assignment, centroids, kmeans, assign, iters=15, seed=42):
     for c, (ids, _) in enumerate(done):
         out_a[ids] = c
     return out_a, np.stack([c for _, c in done]).astype(np.float32)
+
+
+# ---- graph index (the product's CAGRA-style build and search) ----------------
+# Integer-valued vectors keep every distance exact in float32, so plain numpy
+# arithmetic gives the same values as the kernels' fmaf chains; what these
+# loops check is the control logic: candidate lists, pruning, reverse edges,
+# visited-set resets, parent choice, merging and termination.
+
+def _mix32(h):
+    h &= 0xFFFFFFFF
+    h ^= h >> 16
+    h = (h * 0x85EBCA6B) & 0xFFFFFFFF
+    h ^= h >> 13
+    h = (h * 0xC2B2AE35) & 0xFFFFFFFF
+    h ^= h >> 16
+    return h
+
+
+def graph_seed_node(seed, q, s, S, n):
+    x = _mix32(seed ^ _mix32((((q * S + s) & 0xFFFFFFFF) * 0x9E3779B9 + 0x7F4A7C15) & 0xFFFFFFFF))
+    return x % n
+
+
+def _dist(a, b, metric):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return float(-(a @ b)) if metric == "ip" else float(((a - b) ** 2).sum())
+
+
+def graph_build(data, D, I, L, P, iters, seed, metric, kmeans, assign, coarse):
+    """Steps 1-5 of the graph build with the oracle's k-means/assign/coarse."""
+    n = data.shape[0]
+    cen = kmeans(data, L, iters, seed)
+    a = assign(data, cen)
+    lists = [np.flatnonzero(a == c) for c in range(L)]
+    nn, _ = coarse(cen, cen, P)
+    g0 = -np.ones((n, I), np.int64)
+    for c in range(L):
+        chosen = [c] + [int(x) for x in nn[c] if int(x) != c][: P - 1]
+        cand = np.sort(np.concatenate([lists[l] for l in chosen]))
+        kk = min(len(cand), I + 1)
+        for u in lists[c]:
+            d = sorted((_dist(data[u], data[v], metric), int(v)) for v in cand)[:kk]
+            row = [v for _, v in d if v != u][:I]
+            g0[u, :len(row)] = row
+    pr = -np.ones((n, D), np.int64)
+    for u in range(n):
+        nb = g0[u]
+        keys = []
+        for i in range(I):
+            if nb[i] < 0:
+                keys.append((0xFFFF, i))
+                continue
+            cnt = sum(1 for j in range(i) if nb[j] >= 0 and nb[i] in g0[nb[j], :i])
+            keys.append((cnt, i))
+        keys.sort()
+        pr[u] = [nb[i] for _, i in keys[:D]]
+    rev = [[] for _ in range(n)]
+    for i in range(D):
+        for u in range(n):
+            if pr[u, i] >= 0:
+                rev[pr[u, i]].append(u)
+    out = -np.ones((n, D), np.int64)
+    for u in range(n):
+        row = []
+        for v in pr[u, :D // 2]:
+            if v >= 0 and v not in row:
+                row.append(int(v))
+        taken = 0
+        for v in rev[u]:
+            if taken >= D - D // 2 or len(row) >= D:
+                break
+            if v not in row:
+                row.append(v)
+                taken += 1
+        for v in pr[u, D // 2:]:
+            if len(row) >= D:
+                break
+            if v >= 0 and v not in row:
+                row.append(int(v))
+        out[u, :len(row)] = row
+    return out.astype(np.int32)
+
+
+def graph_search(data, graph, queries, itopk, width, max_iter, k, seed, metric, hash_slots=8192,
+                 entry_centroids=None, entry_nodes=None, entry_probes=0):
+    n, D = graph.shape
+    if max_iter == 0:
+        max_iter = 2 * ((itopk + width - 1) // width) + 10
+    WD = width * D
+    out_i = -np.ones((len(queries), k), np.int32)
+    out_d = np.full((len(queries), k), FLT_MAX, np.float32)
+    evals = expanded = 0
+    for q, qv in enumerate(queries):
+        top = []        # [(dist, id, explored)]
+        vis = set()
+        for it in range(-1, max_iter):
+            if it < 0:
+                S = 0
+                if entry_probes:
+                    S = min(entry_probes, len(entry_nodes), WD)
+                    ed = sorted((_dist(qv, c, metric), ci) for ci, c in enumerate(entry_centroids))
+                    first = [int(entry_nodes[ci]) for _, ci in ed[:S]]
+                else:
+                    first = []
+                slots = first + [graph_seed_node(seed, q, s, WD, n) for s in range(S, WD)]
+            else:
+                par = []
+                for e in top:
+                    if len(par) == width:
+                        break
+                    if not e[2]:
+                        par.append(e[1])
+                        e[2] = True
+                if not par:
+                    break
+                expanded += len(par)
+                if len(vis) > hash_slots // 2:
+                    vis = {e[1] for e in top}
+                slots = [int(graph[par[s // D], s % D]) if s // D < len(par) else -1 for s in range(WD)]
+            fresh = []
+            for v in slots:
+                if 0 <= v < n and v not in vis:
+                    vis.add(v)
+                    fresh.append(v)
+            evals += len(fresh)
+            cand = [[np.float32(_dist(data[v], qv, metric)), v, False] for v in fresh]
+            top = sorted(top + cand, key=lambda e: (e[0], e[1]))[:itopk]
+        for r, e in enumerate(top[:k]):
+            out_i[q, r] = e[1]
+            out_d[q, r] = e[0]
+    return out_i, out_d, (evals, expanded)
