@@ -46,10 +46,12 @@ def parse():
     ap.add_argument("--impl", default="fusiongpu", choices=["fusiongpu", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=4000, help="queries in the CPU-baseline sample")
     ap.add_argument("--nprobe", type=int, default=0, help="time this nprobe only (profiling)")
-    ap.add_argument("--profile", default="", choices=["", "scan", "coarse", "rerank", "search"],
+    ap.add_argument("--profile", default="", choices=["", "scan", "coarse", "rerank", "search", "graph"],
                     help="build the index, then run only this stage warmup+1 times (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
+    ap.add_argument("--index-dir", default="", help="--profile: load the C2 index from here (build and save it "
+                                                   "there when absent), so a profiler sees only the search")
     ap.add_argument("--workload", default="C2", choices=["C2", "C4"],
                     help="C2: IVF-PQ headline (default); C4: graph index (1M x 768 fp16, IP)")
     return ap.parse_args()
@@ -296,7 +298,14 @@ def profile_stage(args, device):
     from fusiongpu_b200.index import IVFPQIndex, SearchParams, run_gpu_batch_logic, run_gpu_rerank
     spec, nlist = workload(args.quick)
     base, queries = ds.generate(spec)
-    idx = IVFPQIndex.build(torch.from_numpy(base).to(device), nlist, CONFIG["pq_m"], device=device)
+    d = args.index_dir
+    if d and os.path.exists(os.path.join(d, "ivf_data.bin")):
+        idx = IVFPQIndex.load(d, CONFIG["pq_m"], spec.dim, base=base, device=device)
+    else:
+        idx = IVFPQIndex.build(torch.from_numpy(base).to(device), nlist, CONFIG["pq_m"], device=device)
+        if d:
+            os.makedirs(d, exist_ok=True)
+            idx.save(d)
     qd = torch.from_numpy(queries).to(device)
     nprobe = args.nprobe or 8
     p = search_params(nprobe, SearchParams)
@@ -482,6 +491,15 @@ def main_c4(args):
     t_build = time.time() - t0
     print(f"[c4] graph built in {t_build:.1f} s", file=sys.stderr, flush=True)
     qd = torch.from_numpy(queries).to(device)
+    if args.profile == "graph":
+        # warmup+1 launches of the search alone: the target of
+        # `ncu -k regex:graph_search -s <warmup> -c 1`
+        sp = GraphSearchParams(**C4_SEARCH)
+        for _ in range(args.warmup + 1):
+            gi.search(qd, sp)
+        torch.cuda.synchronize(device)
+        print(json.dumps({"profile": "graph", "nq": int(queries.shape[0]), "itopk": sp.itopk}))
+        return
     gt, _ = knn_ip(xb, qd, 10)
     gt = gt.cpu().numpy()
     nq = queries.shape[0]

@@ -23,8 +23,8 @@
 // search  One CTA per query.  An internal top list of `itopk` (distance, id)
 //         entries with explored flags; each iteration takes the first
 //         `search_width` unexplored entries as parents, gathers their D
-//         neighbours, drops those already visited (open-addressing hash in
-//         shared memory, reset to the current top list when half full),
+//         neighbours, drops those already visited (4096-slot open-addressing
+//         hash in shared memory, reset to the current top list when half full),
 //         computes the new distances (one warp per vector, 16-byte loads,
 //         fixed reduction order), sorts them and merges them into the top
 //         list (merge path).  Starts from search_width*D pseudo-random nodes
@@ -371,12 +371,22 @@ int graph_build(const void* data, int dtype, long long n, int dim, const fg_grap
 
 // ============================== search =========================================
 
-constexpr int GS_NT = 256;
+#ifndef FG_GS_NT
+#define FG_GS_NT 128
+#endif
+#ifndef FG_GS_HASH_BITS
+#define FG_GS_HASH_BITS 12
+#endif
+#ifndef FG_GS_CHUNKS
+#define FG_GS_CHUNKS 2
+#endif
+constexpr int GS_NT = FG_GS_NT;
 constexpr int GS_WARPS = GS_NT / 32;
-constexpr int GS_HASH_BITS = 13;  // 8192 slots (32 KB), reset at half load
+constexpr int GS_HASH_BITS = FG_GS_HASH_BITS;  // 4096 slots (16 KB), reset at half load
 constexpr int GS_HASH = 1 << GS_HASH_BITS;
 constexpr uint32_t GS_EMPTY = 0xffffffffu;
-constexpr int GS_UNROLL = 4;  // vectors in flight per warp
+constexpr int GS_UNROLL = 4;         // vectors in flight per warp
+constexpr int GS_CHUNKS = FG_GS_CHUNKS;  // 16-byte chunks per lane and vector loaded per round
 
 // murmur3's 32-bit finaliser (a published mixing function)
 __host__ __device__ __forceinline__ uint32_t mix32(uint32_t h) {
@@ -465,20 +475,30 @@ __device__ __forceinline__ void warp_dist(const T* __restrict__ data, long long 
     float acc[GS_UNROLL];
 #pragma unroll
     for (int u = 0; u < GS_UNROLL; ++u) acc[u] = 0.0f;
-    for (int c0 = 0; c0 < nch; c0 += 32 * 2) {
-        uint4 v[GS_UNROLL][2];
+    for (int c0 = 0; c0 < nch; c0 += 32 * GS_CHUNKS) {
+        uint4 v[GS_UNROLL][GS_CHUNKS];
 #pragma unroll
         for (int u = 0; u < GS_UNROLL; ++u)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < GS_CHUNKS; ++h) {
                 const int c = c0 + h * 32 + lane;
                 v[u][h] = __ldg(row[u] + (c < nch ? c : 0));
             }
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < GS_CHUNKS; ++h) {
             const int c = c0 + h * 32 + lane;
             if (c >= nch) continue;
-            const float* q = qv + c * E;
+            // the query chunk as float4 reads (16 bytes per lane: no bank conflicts)
+            float q[E];
+            const float4* q4 = reinterpret_cast<const float4*>(qv + c * E);
+#pragma unroll
+            for (int e4 = 0; e4 < E / 4; ++e4) {
+                const float4 t = q4[e4];
+                q[4 * e4] = t.x;
+                q[4 * e4 + 1] = t.y;
+                q[4 * e4 + 2] = t.z;
+                q[4 * e4 + 3] = t.w;
+            }
 #pragma unroll
             for (int u = 0; u < GS_UNROLL; ++u) {
                 float f[E];

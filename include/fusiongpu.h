@@ -254,7 +254,7 @@ int fg_graph_build(const void* data, int32_t dtype, int64_t n, int32_t dim,
  * one tiled pass before the search), then pseudo-random nodes (murmur3
  * finaliser of seed, query and slot) for the remaining slots.  Each
  * iteration expands the first search_width unexplored entries: their
- * neighbours not yet visited (open-addressing hash of 8192 slots in shared
+ * neighbours not yet visited (open-addressing hash of 4096 slots in shared
  * memory, reset to the top list when half full) get distances (one warp per
  * vector, 16-byte loads, lane-strided fmaf then a fixed xor-butterfly sum)
  * and are merged in by (distance, id).  Stops when no unexplored entry

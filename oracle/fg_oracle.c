@@ -1251,7 +1251,7 @@ static int cmp_u64(const void* x, const void* y) {
     return (a > b) - (a < b);
 }
 
-#define FGO_GS_HASH 8192
+#define FGO_GS_HASH 4096
 
 int fgo_graph_search(const void* data, int dtype, int64_t n, int dim, const int32_t* graph, int D,
                      const float* entry_cen, const int32_t* entry_nodes, int n_entries,

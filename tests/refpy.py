@@ -278,7 +278,7 @@ def graph_build(data, D, I, L, P, iters, seed, metric, kmeans, assign, coarse):
     return out.astype(np.int32)
 
 
-def graph_search(data, graph, queries, itopk, width, max_iter, k, seed, metric, hash_slots=8192,
+def graph_search(data, graph, queries, itopk, width, max_iter, k, seed, metric, hash_slots=4096,
                  entry_centroids=None, entry_nodes=None, entry_probes=0):
     n, D = graph.shape
     if max_iter == 0:
