@@ -52,8 +52,9 @@ def parse():
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
     ap.add_argument("--index-dir", default="", help="--profile: load the C2 index from here (build and save it "
                                                    "there when absent), so a profiler sees only the search")
-    ap.add_argument("--workload", default="C2", choices=["C2", "C4"],
-                    help="C2: IVF-PQ headline (default); C4: graph index (1M x 768 fp16, IP)")
+    ap.add_argument("--workload", default="C2", choices=["C2", "C3", "C4"],
+                    help="C2: IVF-PQ headline (default); C3: 10M x 96 IVF-PQ (HBM-bound scan); "
+                         "C4: graph index (1M x 768 fp16, IP)")
     return ap.parse_args()
 
 
@@ -151,6 +152,8 @@ def main():
     args = parse()
     if args.workload == "C4":
         return main_c4(args)
+    if args.workload == "C3":
+        return main_c3(args)
     if args.impl == "reference":
         return main_reference(args)
     import torch
@@ -451,6 +454,156 @@ def main_reference(args):
                          "sample": f"{sample} queries per step (recall from the first 1000); the reference "
                                    "ships no CPU search, so its C restatement (oracle/) runs"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ---- C3: 10M x 96 IVF-PQ, codes far beyond L2 ----------------------------------------
+
+C3_CONFIG = dict(nlist=16384, pq_m=48, k=10, rerank_m=4096, nprobe=64, p1_lists=12, limit_k=50, threshold_coeff=1.0,
+                 mini_batch=128, epsilon=0.1, beta=2, batches=[1, 100, 10000])
+
+
+def main_c3(args):
+    """C3: QPS and recall@10 at nprobe 64 with an exact rerank of the top 4096
+    (intended mode) over 10M x 96 unit vectors; latency at batches of 1 and
+    100.  The scan reads 480 MB of codes per pass (far beyond L2): its
+    roofline is HBM."""
+    import torch
+    from fusiongpu_b200 import datasets as ds
+    from fusiongpu_b200.index import IVFPQIndex, SearchParams, knn_exact, recall_at, run_gpu_batch_logic
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = dict(C3_CONFIG)
+    # quick: 3M vectors, so that the 144 MB of codes still exceed the 126 MB L2
+    spec = ds.scaled(ds.C3, 3_000_000, 2_000, n_centres=4096) if args.quick else ds.C3
+    if args.quick:
+        cfg["nlist"] = 4096
+    t0 = time.time()
+    base, queries = ds.generate(spec)
+    print(f"[c3] generated {spec.n_base} x {spec.dim} in {time.time() - t0:.1f} s", file=sys.stderr, flush=True)
+    t0 = time.time()
+    xb = torch.from_numpy(base).to(device)
+    idx = IVFPQIndex.build(xb, cfg["nlist"], cfg["pq_m"], kmeans_iters=20, pq_sample=50000, pq_iters=8, device=device)
+    torch.cuda.synchronize(device)
+    t_build = time.time() - t0
+    print(f"[c3] index built in {t_build:.1f} s ({idx.nlist} lists)", file=sys.stderr, flush=True)
+    qd = torch.from_numpy(queries).to(device)
+    p = SearchParams(top_m=cfg["nprobe"], p1_lists=cfg["p1_lists"], limit_k=cfg["limit_k"],
+                     threshold_coeff=cfg["threshold_coeff"], prune_ratio=100.0, rerank_m=cfg["rerank_m"],
+                     final_k=cfg["k"], mini_batch=cfg["mini_batch"], epsilon=cfg["epsilon"], beta=cfg["beta"],
+                     ref_compat=False)
+    if args.profile in ("scan", "search", "rerank"):
+        # warmup+1 launches of one stage alone (the target of ncu -s <warmup> -c 1)
+        pid, pdist = idx.coarse(qd, cfg["nprobe"])
+        ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pdist, p)
+        torch.cuda.synchronize(device)
+        from fusiongpu_b200.index import run_gpu_rerank
+        for _ in range(args.warmup + 1):
+            if args.profile == "scan":
+                run_gpu_batch_logic(idx, qd, pid, pdist, p)
+            elif args.profile == "rerank":
+                run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+            else:
+                idx.search(qd, p)
+        torch.cuda.synchronize(device)
+        print(json.dumps({"profile": args.profile, "workload": spec.name, "nq": int(queries.shape[0])}))
+        return
+    gt, _ = knn_exact(xb, qd, 10, device=device)
+    gt = gt.cpu().numpy()
+    nq = queries.shape[0]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    ids = torch.empty((nq, cfg["k"]), dtype=torch.int32, device=device)
+    dd = torch.empty((nq, cfg["k"]), dtype=torch.float32, device=device)
+
+    def timed(fn, steps):
+        tot = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / steps
+
+    clocks = ClockSampler(local)
+    with clocks:
+        for _ in range(args.warmup):
+            idx.search(qd, p, out=(ids, dd))
+        torch.cuda.synchronize(device)
+        rec = recall_at(ids.cpu().numpy(), gt, 10)
+        ms = timed(lambda: idx.search(qd, p, out=(ids, dd)), args.steps)
+        lat = {}
+        for b in cfg["batches"]:
+            if b >= nq:
+                lat[str(b)] = ms
+                continue
+            qb = qd[:b].contiguous()
+            for _ in range(args.warmup):
+                idx.search(qb, p)
+            lat[str(b)] = timed(lambda: idx.search(qb, p), args.steps)
+        # roofline of the scan kernel alone
+        pid, pdist = idx.coarse(qd, cfg["nprobe"])
+        lens = (idx.offsets[1:] - idx.offsets[:-1]).to(torch.int64)
+        code_bytes = int(lens[pid.long()].sum().item()) * idx.pq_m
+        for _ in range(args.warmup):
+            run_gpu_batch_logic(idx, qd, pid, pdist, p)
+        scan_ms = timed(lambda: run_gpu_batch_logic(idx, qd, pid, pdist, p), args.steps)
+        ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pdist, p)
+        cand_bytes = 4 * int(cc.to(torch.int64).sum().item())
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    alg = code_bytes + cand_bytes
+    achieved = alg / (scan_ms / 1e3) / 1e9
+    # end to end: pinned host queries in, ids and distances out
+    hq = torch.from_numpy(queries).pin_memory()
+    hid = torch.empty((nq, cfg["k"]), dtype=torch.int32).pin_memory()
+    hdd = torch.empty((nq, cfg["k"]), dtype=torch.float32).pin_memory()
+    qdev = torch.empty_like(qd)
+
+    def one():
+        qdev.copy_(hq, non_blocking=True)
+        idx.search(qdev, p, out=(ids, dd))
+        hid.copy_(ids, non_blocking=True)
+        hdd.copy_(dd, non_blocking=True)
+
+    one()
+    e2e_ms = timed(one, args.steps)
+    out = {
+        "metric": "QPS of the C3 IVF-PQ search (nprobe 64, exact rerank of the top 4096) with its recall@10",
+        "value": nq / (ms / 1e3),
+        "unit": "queries/s",
+        "recall@10": rec,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture: 16384 normalised centres, sigma 0.05, unit vectors)",
+        "config": dict(cfg, workload=f"{spec.name}: {spec.n_base} x {spec.dim} fp32, {nq} queries, L2",
+                       lists=idx.nlist, l2="flushed (256 MB write) between timed steps", quick=bool(args.quick),
+                       mode="intended (full rerank_m gather)"),
+        "latency_ms_by_batch": lat,
+        "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"kernel": "ivfpq_batch_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "traffic": None,
+                     "algorithmic_bytes": alg, "ms_per_launch": scan_ms},
+        "clocks": clocks.summary(),
+        "build_s": t_build,
     }
     print(json.dumps(out), flush=True)
 

@@ -19,6 +19,25 @@
 namespace fg {
 
 int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int32_t* amin, cudaStream_t s);
+bool coarse_tc_supported(int dim, int P);
+size_t assign_tc_workspace(long long n, int k, int dim);
+int assign_tc(const float* X, long long n, int dim, const float* C, int k, int32_t* out, void* ws, size_t ws_bytes,
+              cudaStream_t s);
+
+// Nearest centroid of every point: the tensor-core path for dim <= 128 when the
+// workspace holds it, else the exact CUDA-core tiles (identical results).
+bool assign_on_tc(long long n, int k, int dim) { return coarse_tc_supported(dim, 1) && k >= 64 && n >= 4096; }
+
+size_t assign_workspace(long long n, int k, int dim) {
+    return assign_on_tc(n, k, dim) ? assign_tc_workspace(n, k, dim) : 0;
+}
+
+int assign_auto(const float* X, long long n, int dim, const float* C, int k, int32_t* out, void* ws, size_t ws_bytes,
+                cudaStream_t s) {
+    if (assign_on_tc(n, k, dim) && ws && ws_bytes >= assign_tc_workspace(n, k, dim))
+        return assign_tc(X, n, dim, C, k, out, ws, ws_bytes, s);
+    return l2_argmin(X, n, C, k, dim, out, s);
+}
 
 // ---- MT19937 on the host (seeding only; k or `sample` draws) -------------------
 
@@ -237,9 +256,8 @@ int kmeans_update(const float* data, int dim, const int32_t* order, const int32_
 }
 
 size_t kmeans_workspace(int64_t n, int dim, int k) {
-    (void)dim;
-    return round_up((size_t)n * 4, 256) * 2 + round_up((size_t)(k + 1) * 4, 256) +
-           round_up((size_t)k * 8, 256) + sort_workspace(n, k) + 1024;
+    return round_up((size_t)n * 4, 256) * 2 + round_up((size_t)(k + 1) * 4, 256) + round_up((size_t)k * 8, 256) +
+           std::max(sort_workspace(n, k), assign_workspace(n, k, dim)) + 1024;
 }
 
 int kmeans(const float* data, int64_t n, int dim, int k, int iters, uint32_t seed, float* centroids, void* ws,
@@ -256,7 +274,7 @@ int kmeans(const float* data, int64_t n, int dim, int k, int iters, uint32_t see
     const size_t sws_bytes = ws_bytes - used;
     int rc = kmeans_init(data, n, dim, k, seed, centroids, rows, s);
     for (int it = 0; it < iters && !rc; ++it) {
-        rc = l2_argmin(data, n, centroids, k, dim, as, s);
+        rc = assign_auto(data, n, dim, centroids, k, as, sws, sws_bytes, s);
         if (!rc) rc = sort_by_list(as, n, k, order, offs, sws, sws_bytes, s);
         if (!rc) rc = kmeans_update(data, dim, order, offs, k, centroids, s);
     }

@@ -60,6 +60,9 @@ int pq_encode(const float* data, int64_t n, int dim, const int32_t* assign, cons
               const float* codebook, int pq_m, uint8_t* codes, cudaStream_t s);
 int gather_lists(const uint8_t* codes, int64_t n, int pq_m, const int32_t* order, uint8_t* out_codes,
                  int32_t* out_ids, cudaStream_t s);
+size_t assign_workspace(long long n, int k, int dim);
+int assign_auto(const float* X, long long n, int dim, const float* C, int k, int32_t* out, void* ws, size_t ws_bytes,
+                cudaStream_t s);
 int probe_budget(const int32_t* list_offsets, int nlist, const uint32_t* probe_ids, const float* probe_dists, int nq,
                  int top_m, float prune_ratio, int32_t* counts, int32_t* offsets, cudaStream_t s);
 int rebalance(const float* data, int64_t n, int dim, const int32_t* assign, const float* centroids, int k, int iters,
@@ -256,7 +259,15 @@ int fg_assign(const float* data, int64_t n, int32_t dim, const float* centroids,
     FG_REQUIRE(n >= 0 && dim >= 1 && k >= 1, "bad assign shape");
     if (n == 0) return FG_OK;
     FG_REQUIRE(data && centroids && out_assign, "null buffer");
-    return l2_argmin(data, n, centroids, k, dim, out_assign, as_stream(stream));
+    cudaStream_t s = as_stream(stream);
+    const size_t wb = assign_workspace(n, k, dim);
+    if (!wb) return l2_argmin(data, n, centroids, k, dim, out_assign, s);
+    // tensor-core path: stream-ordered scratch, released after the last use
+    void* ws = nullptr;
+    FG_CUDA_TRY(cudaMallocAsync(&ws, wb, s));
+    const int rc = assign_auto(data, n, dim, centroids, k, out_assign, ws, wb, s);
+    FG_CUDA_TRY(cudaFreeAsync(ws, s));
+    return rc;
 }
 
 int fg_sort_by_list_workspace_size(int64_t n, int32_t k, size_t* bytes) {

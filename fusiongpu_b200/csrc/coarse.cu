@@ -37,9 +37,11 @@ __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict_
     __shared__ float rd[L2_T][17];
     __shared__ int ri[L2_T][17];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const long long x0 = (long long)blockIdx.x * L2_T;
+    // EPI_MATRIX: grid.x runs over Y tiles (up to 2^31 - 1), grid.y over X tiles;
+    // EPI_ARGMIN: grid.x runs over X tiles, every CTA sweeps all of Y
+    const long long x0 = (long long)(EPI == EPI_MATRIX ? blockIdx.y : blockIdx.x) * L2_T;
     const int nyt = (ny + L2_T - 1) / L2_T;
-    const int yt0 = blockIdx.y * ytiles;
+    const int yt0 = (EPI == EPI_MATRIX ? blockIdx.x : blockIdx.y) * ytiles;
     const int yt1 = min(nyt, yt0 + ytiles);
     float best[4];
     int bidx[4];
@@ -244,12 +246,21 @@ int l2_matrix(const float* X, long long nx, const float* Y, int ny, int dim, flo
               cudaStream_t s, int metric = FG_METRIC_L2) {
     if (nx <= 0 || ny <= 0) return FG_OK;
     const int nyt = (ny + L2_T - 1) / L2_T;
-    dim3 grid((unsigned)((nx + L2_T - 1) / L2_T), nyt);
-    if (metric == FG_METRIC_IP)
-        l2_tile_kernel<EPI_MATRIX, FG_METRIC_IP><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
-    else
-        l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, D, ldd, nullptr, 1);
-    return check_launch("l2_tile_kernel(matrix)");
+    // at most 65535 X tiles per launch (grid.y)
+    const long long xrows = 65535ll * L2_T;
+    for (long long r0 = 0; r0 < nx; r0 += xrows) {
+        const long long nr = std::min(xrows, nx - r0);
+        dim3 grid((unsigned)nyt, (unsigned)((nr + L2_T - 1) / L2_T));
+        if (metric == FG_METRIC_IP)
+            l2_tile_kernel<EPI_MATRIX, FG_METRIC_IP><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd,
+                                                                           ldd, nullptr, 1);
+        else
+            l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd, ldd, nullptr,
+                                                             1);
+        const int rc = check_launch("l2_tile_kernel(matrix)");
+        if (rc) return rc;
+    }
+    return FG_OK;
 }
 
 int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int32_t* amin,

@@ -573,3 +573,44 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
 }
 
 }  // namespace fg
+
+namespace fg {
+
+// ---- k-means assignment on the tensor cores ------------------------------------
+// The nearest centroid of every point is the coarse search with top_m = 1: the
+// split-bf16 GEMM bounds and filters, the exact rescore (the same fmaf chain as
+// l2_argmin) ranks by (distance, id) and the certificate or the exact fallback
+// makes the result identical to l2_argmin's.  Points go through in chunks that
+// keep the workspace near 1.5 GB.
+
+static long long assign_chunk(long long n, int k, int dim) {
+    const long long probe = 65536;
+    const size_t per = coarse_tc_workspace(probe, k, dim, 1) / (size_t)probe + 8;
+    long long r = (long long)(((size_t)1536 << 20) / std::max<size_t>(per, 1));
+    r = std::max(4096ll, std::min(r, 262144ll));
+    return std::max(1ll, std::min(r, n));
+}
+
+size_t assign_tc_workspace(long long n, int k, int dim) {
+    const long long r = assign_chunk(n, k, dim);
+    return coarse_tc_workspace(r, k, dim, 1) + round_up((size_t)r * 4, 256) + 512;
+}
+
+int assign_tc(const float* X, long long n, int dim, const float* C, int k, int32_t* out, void* ws, size_t ws_bytes,
+              cudaStream_t s) {
+    if (n <= 0) return FG_OK;
+    const long long r = assign_chunk(n, k, dim);
+    Carve cv(ws, ws_bytes);
+    float* d = cv.take<float>((size_t)r);
+    const size_t used = round_up(cv.used, 256);
+    if (!cv.ok() || used > ws_bytes) return fail(FG_ERR_WORKSPACE, "assignment workspace too small");
+    for (long long q0 = 0; q0 < n; q0 += r) {
+        const long long nr = std::min(r, n - q0);
+        const int rc = coarse_tc(C, k, dim, X + (size_t)q0 * dim, nr, 1, reinterpret_cast<uint32_t*>(out + q0), d,
+                                 static_cast<char*>(ws) + used, ws_bytes - used, s, nullptr);
+        if (rc) return rc;
+    }
+    return FG_OK;
+}
+
+}  // namespace fg

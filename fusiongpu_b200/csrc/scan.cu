@@ -515,15 +515,19 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.cand_counts = cand_counts;
     a.write_pad = write_pad ? 1 : 0;
 
-    int dev = 0, smem_max = 0;
+    int dev = 0, smem_max = 0, smem_sm = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    // a roomy buffer (fewer cuts) when it fits, else the minimum rsel + one round
+    FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    // a roomy buffer (fewer cuts) when it fits and costs no resident CTA, else
+    // the minimum rsel + one round
     a.cap = 2 * a.rsel + SCAN_NT;
     ScanLayout L = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
-    if (L.total > smem_max) {
+    const ScanLayout Lmin = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.rsel + SCAN_NT, a.sort_n);
+    auto per_sm = [&](int bytes) { return smem_sm / (bytes + 1024); };
+    if (L.total > smem_max || per_sm(Lmin.total) > per_sm(L.total)) {
         a.cap = a.rsel + SCAN_NT;
-        L = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
+        L = Lmin;
     }
     if (L.total > smem_max)
         return fail(FG_ERR_UNSUPPORTED, "scan needs %d bytes of shared memory (max %d): rerank_m=%d "

@@ -295,7 +295,11 @@ int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_
                    float* centroids, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Nearest centroid by exact squared L2, lowest index on ties.  Replaces
- * gpu_assign_to_centroids / gpu_assign_initial_clusters (kmeans_gpu.cuh:329-394). */
+ * gpu_assign_to_centroids / gpu_assign_initial_clusters (kmeans_gpu.cuh:329-394).
+ * For dim <= 128 (k >= 64, n >= 4096) the assignment runs on the tensor cores
+ * (the coarse search with top_m = 1: split-bf16 tcgen05 GEMM, exact rescore,
+ * certificate or exact fallback) with stream-ordered scratch; the result is
+ * identical to the CUDA-core path.  fg_kmeans uses the same dispatch. */
 int fg_assign(const float* data, int64_t n, int32_t dim, const float* centroids, int32_t k,
               int32_t* out_assign, void* stream);
 

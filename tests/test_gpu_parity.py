@@ -356,3 +356,14 @@ def test_reference_kernels_agree_with_oracle(kind, pname):
     xi, xd = oracle.rerank(q, oi, oc, base, **p)
     np.testing.assert_array_equal(fd[clean], xd[clean])
     assert (fi[clean] == xi[clean]).mean() > 0.999
+
+
+@pytest.mark.parametrize("n,k,dim", [(50000, 300, 96), (20000, 4096, 128), (8192, 64, 32)])
+def test_assign_tensor_cores_bit_exact(fg, n, k, dim):
+    rng = np.random.default_rng(n + k)
+    x = rng.normal(size=(n, dim)).astype(np.float32)
+    c = rng.normal(size=(k, dim)).astype(np.float32)
+    c[k // 2] = c[1]  # duplicate centroids: the lower index wins
+    x[:50] = c[1]     # points exactly on the duplicated centroid
+    got = fg.gpu_assign_to_centroids(torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda())
+    np.testing.assert_array_equal(_np(got), oracle.assign(x, c))
