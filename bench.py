@@ -622,26 +622,54 @@ def main_c4(args):
     """C4: QPS and recall@10 of the graph search (batch of 10,000 fp16
     queries, itopk 128, search width 4) on a degree-64 graph over 1M x 768
     fp16 unit vectors (inner product); itopk swept for the recall curve.  A
-    step is one search of the whole batch."""
+    step is one search of the whole batch.  Under torchrun the rows are
+    partitioned across the GPUs (one graph per GPU, queries broadcast, one
+    NCCL all-gather and a device merge per step; strong scaling)."""
     import torch
+    import torch.distributed as dist
     from fusiongpu_b200 import datasets as ds
     from fusiongpu_b200.graph import GraphBuildParams, GraphIndex, GraphSearchParams, knn_ip
+    from fusiongpu_b200.sharded import ShardedGraphIndex
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     spec = ds.scaled(ds.C4, 100_000, 2_000, n_centres=200) if args.quick else ds.C4
     t0 = time.time()
     base, queries = ds.generate(spec)
     t_gen = time.time() - t0
     print(f"[c4] generated {spec.n_base} x {spec.dim} in {t_gen:.1f} s", file=sys.stderr, flush=True)
-    xb = torch.from_numpy(base).to(device)
     bp = dict(C4_BUILD, nlist=512 if args.quick else C4_BUILD["nlist"])
+    # every shard keeps the full entry partition: its lists must stay finer than
+    # the mixture's clusters, whose members every shard holds a share of
     torch.cuda.synchronize(device)
     t0 = time.time()
-    gi = GraphIndex.build(xb, GraphBuildParams(**bp))
+    if world == 1:
+        xb = torch.from_numpy(base).to(device)
+        gi = GraphIndex.build(xb, GraphBuildParams(**bp))
+        searcher = gi
+    else:
+        xb = None
+        gi = ShardedGraphIndex(base, rank, world, GraphBuildParams(**bp), device=device)
+        searcher = gi
     torch.cuda.synchronize(device)
-    t_build = time.time() - t0
+    t_build = max_over_ranks(time.time() - t0)
     print(f"[c4] graph built in {t_build:.1f} s", file=sys.stderr, flush=True)
     qd = torch.from_numpy(queries).to(device)
     if args.profile == "graph":
@@ -649,15 +677,20 @@ def main_c4(args):
         # `ncu -k regex:graph_search -s <warmup> -c 1`
         sp = GraphSearchParams(**C4_SEARCH)
         for _ in range(args.warmup + 1):
-            gi.search(qd, sp)
+            searcher.search(qd, sp)
         torch.cuda.synchronize(device)
         print(json.dumps({"profile": "graph", "nq": int(queries.shape[0]), "itopk": sp.itopk}))
         return
-    gt, _ = knn_ip(xb, qd, 10)
-    gt = gt.cpu().numpy()
+    gt = None
+    if rank == 0:
+        full = xb if xb is not None else torch.from_numpy(base).to(device)
+        g, _ = knn_ip(full, qd, 10)
+        gt = g.cpu().numpy()
+        del full
     nq = queries.shape[0]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    local_graph = gi if world == 1 else gi.local
     sweep = []
     clocks = ClockSampler(local)
     with clocks:
@@ -665,46 +698,54 @@ def main_c4(args):
             print(f"[c4] itopk {itopk}", file=sys.stderr, flush=True)
             sp = GraphSearchParams(**dict(C4_SEARCH, itopk=itopk))
             for _ in range(args.warmup):
-                ids, dd, cnt = gi.search(qd, sp, counters=True)
+                ids, dd = searcher.search(qd, sp)
+            # device counters of this GPU's graph (a separate, untimed pass)
+            _, _, cnt = local_graph.search(qd, sp, counters=True)
             torch.cuda.synchronize(device)
-            got = ids.cpu().numpy()
-            rec = float(np.mean([len(set(got[i]) & set(gt[i])) / 10 for i in range(nq)]))
             evals, expanded, bad = (int(v) for v in cnt.cpu().numpy())
             if bad:
                 raise RuntimeError(f"graph search skipped {bad} out-of-range accesses")
+            rec = None
+            if rank == 0:
+                got = ids.cpu().numpy()
+                rec = float(np.mean([len(set(got[i]) & set(gt[i])) / 10 for i in range(nq)]))
+            barrier()
+            torch.cuda.synchronize(device)
             tot = 0.0
             for _ in range(args.steps):
                 flush.zero_()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                gi.search(qd, sp)
+                searcher.search(qd, sp)
                 e1.record(stream)
                 e1.synchronize()
                 tot += e0.elapsed_time(e1)
-            ms = tot / args.steps
+            barrier()
+            ms = max_over_ranks(tot / args.steps)
             alg = evals * spec.dim * 2 + expanded * bp["graph_degree"] * 4
             sweep.append(dict(itopk=itopk, recall=rec, ms_per_step=ms, qps=nq / (ms / 1e3),
                               distance_evals_per_query=evals / nq, expanded_per_query=expanded / nq,
-                              algorithmic_bytes=alg, achieved_gbs=alg / (ms / 1e3) / 1e9))
-    op = next(s for s in sweep if s["itopk"] == C4_SEARCH["itopk"])
+                              algorithmic_bytes_per_gpu=alg, achieved_gbs_per_gpu=alg / (ms / 1e3) / 1e9))
+    op = next(s_ for s_ in sweep if s_["itopk"] == C4_SEARCH["itopk"])
     # end to end: pinned fp16 queries in, ids out
     sp = GraphSearchParams(**C4_SEARCH)
     hq = torch.from_numpy(queries).pin_memory()
     hid = torch.empty((nq, sp.k), dtype=torch.int32).pin_memory()
     qdev = torch.empty_like(qd)
+    barrier()
     tot = 0.0
     for i in range(args.warmup + args.steps):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         qdev.copy_(hq, non_blocking=True)
-        ids, _ = gi.search(qdev, sp)
+        ids, _ = searcher.search(qdev, sp)
         hid.copy_(ids, non_blocking=True)
         e1.record(stream)
         e1.synchronize()
         if i >= args.warmup:
             tot += e0.elapsed_time(e1)
-    e2e = nq / (tot / args.steps / 1e3)
+    e2e = nq / (max_over_ranks(tot / args.steps) / 1e3)
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -716,32 +757,36 @@ def main_c4(args):
         "value": op["qps"],
         "unit": "queries/s",
         "recall@10": op["recall"],
-        "n_gpus": 1,
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": op["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded Gaussian mixture: 2000 N(0,I) centres, sigma 0.3, normalised, fp16)",
         "config": dict(workload=f"{spec.name}: {spec.n_base} x {spec.dim} fp16, {nq} queries, inner product",
                        build=bp, search=C4_SEARCH, itopk_sweep=list(C4_SWEEP),
+                       parallelism=f"rows partitioned across {world} GPUs (graph per GPU, NCCL all-gather, "
+                                   "device merge)" if world > 1 else "one GPU",
                        l2="flushed (256 MB write) between timed steps", quick=bool(args.quick)),
         "sweep": sweep,
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * sp.k * 4)},
         "gpu_launches": args.steps * len(sweep),
-        "roofline": {"kernel": "graph_search_kernel", "bound": "hbm", "achieved": op["achieved_gbs"], "peak": peak,
-                     "unit": "GB/s", "frac": op["achieved_gbs"] / peak,
+        "roofline": {"kernel": "graph_search_kernel (+ entry selection)", "bound": "hbm",
+                     "achieved": op["achieved_gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+                     "frac": op["achieved_gbs_per_gpu"] / peak,
                      "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "traffic": None,
-                     "algorithmic_bytes": op["algorithmic_bytes"],
-                     "bytes_rule": "distance evals x dim x 2 + expanded nodes x degree x 4 (device counters)"},
+                     "algorithmic_bytes": op["algorithmic_bytes_per_gpu"],
+                     "bytes_rule": "distance evals x dim x 2 + expanded nodes x degree x 4 (device counters), "
+                                   "per GPU, over the whole step"},
         "clocks": clocks.summary(),
         "build_s": t_build,
         "generate_s": t_gen,
     }
-    if not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
         sample = 200 if not args.quick else 100
         g = gi.graph.cpu().numpy()
@@ -756,6 +801,8 @@ def main_c4(args):
                                "seconds": dt}
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -99,3 +99,62 @@ class ShardedIndex:
         out_d = torch.empty((nq, k), dtype=torch.float32, device=self.device)
         _lib.call("fg_merge_topk", _p(all_d), _p(all_i), self.world, nq, k, _p(out_i), _p(out_d), _stream())
         return out_i, out_d
+
+
+def graph_shard_rows(n: int, nshards: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) of shard `rank`: contiguous, sizes differ by at most one."""
+    lo = n * rank // nshards
+    hi = n * (rank + 1) // nshards
+    return lo, hi
+
+
+class ShardedGraphIndex:
+    """This process's slice of a graph index partitioned by rows across GPUs.
+
+    Every GPU builds the graph over its own rows (fg_graph_build), searches the
+    whole query batch on it (fg_graph_search), turns its local ids into global
+    ones (fg_map_ids) and the per-GPU top-k lists are merged after one
+    all-gather (fg_merge_topk, ascending (distance, global id); inner-product
+    distances are -dot, so ascending is best first)."""
+
+    def __init__(self, data, rank: int, world: int, build_params=None, device="cuda", group=None):
+        import torch
+        from .graph import GraphBuildParams, GraphIndex
+        self.rank, self.world, self.group = rank, world, group
+        n = data.shape[0]
+        self.lo, self.hi = graph_shard_rows(n, world, rank)
+        part = data[self.lo:self.hi]
+        dev = torch.device(device) if not isinstance(device, torch.device) else device
+        part = torch.as_tensor(part).to(dev).contiguous() if not torch.is_tensor(part) else part.to(dev).contiguous()
+        bp = build_params or GraphBuildParams()
+        bp = type(bp)(**{**bp.__dict__, "nlist": max(1, min(bp.nlist, part.shape[0] // 4))})
+        self.local = GraphIndex.build(part, bp)
+        self.device = part.device
+        self.l2g = torch.arange(self.lo, self.hi, dtype=torch.int32, device=self.device)
+
+    def local_search(self, queries, params):
+        import torch
+        from . import _lib
+        from .index import _p, _stream
+        ids, d = self.local.search(queries, params)
+        gids = torch.empty_like(ids)
+        _lib.call("fg_map_ids", _p(ids), ids.numel(), _p(self.l2g), self.l2g.numel(), _p(gids), _stream())
+        return gids, d
+
+    def search(self, queries, params):
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        from .index import _p, _stream
+        gids, d = self.local_search(queries, params)
+        if self.world == 1:
+            return gids, d
+        nq, k = d.shape
+        all_d = torch.empty((self.world * nq * k,), dtype=torch.float32, device=self.device)
+        all_i = torch.empty((self.world * nq * k,), dtype=torch.int32, device=self.device)
+        dist.all_gather_into_tensor(all_d, d.reshape(-1), group=self.group)
+        dist.all_gather_into_tensor(all_i, gids.reshape(-1), group=self.group)
+        out_i = torch.empty((nq, k), dtype=torch.int32, device=self.device)
+        out_d = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        _lib.call("fg_merge_topk", _p(all_d), _p(all_i), self.world, nq, k, _p(out_i), _p(out_d), _stream())
+        return out_i, out_d

@@ -39,3 +39,22 @@ def oracle_sharded_search(index: dict, base: np.ndarray, queries: np.ndarray, wo
         ds.append(ld)
         is_.append(gi)
     return merge_topk_host(np.stack(ds), np.stack(is_), params["final_k"])
+
+
+def oracle_sharded_graph(data: np.ndarray, queries: np.ndarray, world: int, build: dict, search: dict):
+    """Graph sharded by rows, restated with the CPU oracle: each shard's graph
+    and entry points built on its own rows (IVF lists capped at rows/4),
+    per-shard search, global ids = local + first row, host merge."""
+    import oracle
+    from fusiongpu_b200.sharded import graph_shard_rows
+    n = data.shape[0]
+    ds, is_ = [], []
+    for r in range(world):
+        lo, hi = graph_shard_rows(n, world, r)
+        part = np.ascontiguousarray(data[lo:hi])
+        b = dict(build, nlist=max(1, min(build["nlist"], part.shape[0] // 4)))
+        g, ec, en = oracle.graph_build(part.astype(np.float32), entries=True, **b)
+        li, ld, _ = oracle.graph_search(part, g, queries, entry_centroids=ec, entry_nodes=en, **search)
+        ds.append(ld)
+        is_.append(np.where(li >= 0, li + lo, -1).astype(np.int32))
+    return merge_topk_host(np.stack(ds), np.stack(is_), search["k"])

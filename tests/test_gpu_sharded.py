@@ -105,3 +105,72 @@ def test_two_gpus_nccl_all_gather_matches_oracle():
             f = np.load(os.path.join(d, f"rank{r}.npz"))
             np.testing.assert_array_equal(f["dists"], ed)
             np.testing.assert_array_equal(f["ids"], ei)
+
+
+# ---- graph sharded by rows --------------------------------------------------------
+
+GB = dict(graph_degree=16, intermediate_degree=32, nlist=24, probe_lists=3, kmeans_iters=3, seed=42, metric="ip")
+GS = dict(itopk=48, search_width=2, k=10, seed=5, metric="ip", entry_probes=4)
+
+
+def _graph_data():
+    rng = np.random.default_rng(22)
+    x = rng.normal(size=(6000, 64)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    q = rng.normal(size=(40, 64)).astype(np.float32)
+    return x.astype(np.float16), q.astype(np.float16)
+
+
+@pytest.mark.parametrize("world", [1, 3])
+def test_graph_shards_on_one_gpu_match_oracle(world):
+    from fusiongpu_b200.graph import GraphBuildParams, GraphSearchParams
+    from fusiongpu_b200.sharded import ShardedGraphIndex
+    x, q = _graph_data()
+    qd = torch.from_numpy(q).cuda()
+    ds_, is_ = [], []
+    for r in range(world):
+        sh = ShardedGraphIndex(torch.from_numpy(x).cuda(), r, world, GraphBuildParams(**GB))
+        gi, d = sh.local_search(qd, GraphSearchParams(**GS))
+        ds_.append(d.cpu().numpy())
+        is_.append(gi.cpu().numpy())
+    oi, od = _merge_gpu(np.stack(ds_), np.stack(is_), GS["k"])
+    ei, ed = shard_ref.oracle_sharded_graph(x, q, world, GB, GS)
+    np.testing.assert_array_equal(od, ed)
+    np.testing.assert_array_equal(oi, ei)
+
+
+def _graph_nccl_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from fusiongpu_b200.graph import GraphBuildParams, GraphSearchParams
+    from fusiongpu_b200.sharded import ShardedGraphIndex
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    x, q = _graph_data()
+    dev = f"cuda:{rank}"
+    sh = ShardedGraphIndex(torch.from_numpy(x).to(dev), rank, world, GraphBuildParams(**GB), device=dev)
+    ids, d = sh.search(torch.from_numpy(q).to(dev), GraphSearchParams(**GS))
+    torch.cuda.synchronize()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), ids=ids.cpu().numpy(), dists=d.cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not cuda_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_graph_two_gpus_nccl_matches_oracle():
+    import torch.multiprocessing as mp
+    x, q = _graph_data()
+    ei, ed = shard_ref.oracle_sharded_graph(x, q, 2, GB, GS)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_graph_nccl_worker, args=(2, port, d), nprocs=2, join=True)
+        for r in range(2):
+            f = np.load(os.path.join(d, f"rank{r}.npz"))
+            np.testing.assert_array_equal(f["dists"], ed)
+            np.testing.assert_array_equal(f["ids"], ei)

@@ -100,3 +100,68 @@ def test_two_rank_exchange_over_gloo():
     gt, _ = oracle.knn_exact(base, q, 10)
     rec = np.mean([len(set(ei[i]) & set(gt[i])) / 10 for i in range(q.shape[0])])
     assert rec > 0.9
+
+
+# ---- graph sharded by rows --------------------------------------------------------
+
+GB = dict(graph_degree=16, intermediate_degree=32, nlist=16, probe_lists=3, kmeans_iters=3, seed=42, metric="ip")
+GS = dict(itopk=32, search_width=2, k=10, seed=5, metric="ip", entry_probes=4)
+
+
+def _graph_data():
+    rng = np.random.default_rng(21)
+    x = rng.normal(size=(1500, 32)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    q = rng.normal(size=(12, 32)).astype(np.float32)
+    return x.astype(np.float16), q.astype(np.float16)
+
+
+def test_graph_shard_rows_partition():
+    for n, w in ((10, 3), (1000, 8), (7, 7)):
+        rows = [sharded.graph_shard_rows(n, w, r) for r in range(w)]
+        assert rows[0][0] == 0 and rows[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(rows, rows[1:]))
+        assert max(h - l for l, h in rows) - min(h - l for l, h in rows) <= 1
+
+
+def _graph_worker(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    x, q = _graph_data()
+    lo, hi = sharded.graph_shard_rows(x.shape[0], world, rank)
+    part = np.ascontiguousarray(x[lo:hi])
+    b = dict(GB, nlist=max(1, min(GB["nlist"], part.shape[0] // 4)))
+    g, ec, en = oracle.graph_build(part.astype(np.float32), entries=True, **b)
+    li, ld, _ = oracle.graph_search(part, g, q, entry_centroids=ec, entry_nodes=en, **GS)
+    gi = np.where(li >= 0, li + lo, -1).astype(np.int32)
+    td, ti = torch.from_numpy(ld), torch.from_numpy(gi)
+    all_d = [torch.empty_like(td) for _ in range(world)]
+    all_i = [torch.empty_like(ti) for _ in range(world)]
+    dist.all_gather(all_d, td)
+    dist.all_gather(all_i, ti)
+    mi, md = shard_ref.merge_topk_host(np.stack([a.numpy() for a in all_d]), np.stack([a.numpy() for a in all_i]),
+                                     GS["k"])
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), ids=mi, dists=md)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_graph_two_rank_exchange_over_gloo():
+    import torch.multiprocessing as mp
+    x, q = _graph_data()
+    ei, ed = shard_ref.oracle_sharded_graph(x, q, 2, GB, GS)
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_graph_worker, args=(2, _free_port(), d), nprocs=2, join=True)
+        for r in range(2):
+            f = np.load(os.path.join(d, f"rank{r}.npz"))
+            np.testing.assert_array_equal(f["ids"], ei)
+            np.testing.assert_array_equal(f["dists"], ed)
+    # the merged result is close to the exact inner-product top-10
+    xf, qf = x.astype(np.float64), q.astype(np.float64)
+    gt = np.argsort(-(qf @ xf.T), axis=1)[:, :10]
+    rec = np.mean([len(set(ei[i]) & set(gt[i])) / 10 for i in range(len(q))])
+    assert rec >= 0.8, rec
