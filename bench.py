@@ -52,9 +52,9 @@ def parse():
     ap.add_argument("--quick", action="store_true", help="small workload (development only)")
     ap.add_argument("--index-dir", default="", help="--profile: load the C2 index from here (build and save it "
                                                    "there when absent), so a profiler sees only the search")
-    ap.add_argument("--workload", default="C2", choices=["C2", "C3", "C4"],
+    ap.add_argument("--workload", default="C2", choices=["C2", "C3", "C4", "C5"],
                     help="C2: IVF-PQ headline (default); C3: 10M x 96 IVF-PQ (HBM-bound scan); "
-                         "C4: graph index (1M x 768 fp16, IP)")
+                         "C4: graph index (1M x 768 fp16, IP); C5: 100M x 128 uint8, lists sharded across GPUs")
     return ap.parse_args()
 
 
@@ -154,6 +154,8 @@ def main():
         return main_c4(args)
     if args.workload == "C3":
         return main_c3(args)
+    if args.workload == "C5":
+        return main_c5(args)
     if args.impl == "reference":
         return main_reference(args)
     import torch
@@ -606,6 +608,146 @@ def main_c3(args):
         "build_s": t_build,
     }
     print(json.dumps(out), flush=True)
+
+
+# ---- C5: 100M x 128 uint8, inverted lists sharded across the GPUs ---------------
+
+C5_CONFIG = dict(nlist=65536, pq_m=32, k=10, rerank_m=256, nprobe=64, p1_lists=12, limit_k=50, threshold_coeff=1.0,
+                 mini_batch=128, epsilon=0.1, beta=2, kmeans_sample=2_000_000, kmeans_iters=20, gt_queries=1000)
+
+
+def main_c5(args):
+    """C5: QPS and recall@10 at nprobe 64 with an exact rerank of the top 256
+    per shard, 10,000 queries broadcast to every GPU; the inverted lists (with
+    their codes, ids and uint8 raw vectors) are dealt to the GPUs by list
+    length.  Every rank builds the same deterministic index, keeps its shard,
+    searches it, and the per-GPU top-k lists meet in one NCCL all-gather and
+    the device merge (strong scaling).  k-means trains on 2M strided rows,
+    then every row is assigned."""
+    import torch
+    import torch.distributed as dist
+    from fusiongpu_b200 import datasets as ds
+    from fusiongpu_b200.index import IVFPQIndex, SearchParams, knn_exact, recall_at
+    from fusiongpu_b200.sharded import ShardedIndex
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = dict(C5_CONFIG)
+    spec = ds.scaled(ds.C5, 10_000_000, 10_000, n_centres=8192) if args.quick else ds.C5
+    if args.quick:
+        cfg.update(nlist=8192, kmeans_sample=400_000)
+    t0 = time.time()
+    base, queries = ds.generate(spec)
+    queries = queries.astype(np.float32)
+    print(f"[c5] generated {spec.n_base} x {spec.dim} uint8 in {time.time() - t0:.1f} s", file=sys.stderr, flush=True)
+    t0 = time.time()
+    idx = IVFPQIndex.build(torch.from_numpy(base).to(device), cfg["nlist"], cfg["pq_m"],
+                           kmeans_iters=cfg["kmeans_iters"], kmeans_sample=cfg["kmeans_sample"], device=device)
+    torch.cuda.synchronize(device)
+    t_build = max_over_ranks(time.time() - t0)
+    print(f"[c5] index built in {t_build:.1f} s ({idx.nlist} lists)", file=sys.stderr, flush=True)
+    p = SearchParams(top_m=cfg["nprobe"], p1_lists=cfg["p1_lists"], limit_k=cfg["limit_k"],
+                     threshold_coeff=cfg["threshold_coeff"], prune_ratio=100.0, rerank_m=cfg["rerank_m"],
+                     final_k=cfg["k"], mini_batch=cfg["mini_batch"], epsilon=cfg["epsilon"], beta=cfg["beta"],
+                     ref_compat=False)
+    qd = torch.from_numpy(queries).to(device)
+    gt = None
+    if rank == 0:
+        ng = cfg["gt_queries"]
+        gt, _ = knn_exact(idx.base, qd[:ng], 10, device=device)
+        gt = gt.cpu().numpy()
+    if world == 1:
+        searcher = idx
+    else:
+        host = idx.to_numpy()
+        del idx
+        torch.cuda.empty_cache()
+        searcher = ShardedIndex(host, base, rank, world, device=device)
+    nq = queries.shape[0]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    clocks = ClockSampler(local)
+    with clocks:
+        for _ in range(args.warmup):
+            ids, dd = searcher.search(qd, p)
+        torch.cuda.synchronize(device)
+        rec = recall_at(ids[:cfg["gt_queries"]].cpu().numpy(), gt, 10) if rank == 0 else None
+        barrier()
+        tot = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            searcher.search(qd, p)
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        barrier()
+        ms = max_over_ranks(tot / args.steps)
+    hq = torch.from_numpy(queries).pin_memory()
+    hid = torch.empty((nq, cfg["k"]), dtype=torch.int32).pin_memory()
+    qdev = torch.empty_like(qd)
+    barrier()
+    tot = 0.0
+    for i in range(1 + args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        qdev.copy_(hq, non_blocking=True)
+        r_ids, _ = searcher.search(qdev, p)
+        hid.copy_(r_ids, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if i:
+            tot += e0.elapsed_time(e1)
+    e2e = nq / (max_over_ranks(tot / args.steps) / 1e3)
+    out = {
+        "metric": "QPS of the C5 sharded IVF-PQ search (nprobe 64, rerank 256 per shard) with its recall@10",
+        "value": nq / (ms / 1e3),
+        "unit": "queries/s",
+        "recall@10": rec,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 (uint8 raw vectors)",
+        "data": "synthetic (seeded Gaussian mixture: 65536 centres in [0,255], sigma 8, clamped, rounded, uint8)",
+        "config": dict(cfg, workload=f"{spec.name}: {spec.n_base} x {spec.dim} uint8, {nq} queries, L2",
+                       lists=int(host["centroids"].shape[0]) if world > 1 else idx.nlist,
+                       parallelism=f"inverted lists dealt to {world} GPUs by length (NCCL all-gather, "
+                                   "device merge)" if world > 1 else "one GPU",
+                       recall_on=f"first {cfg['gt_queries']} queries (exact ground truth)",
+                       l2="flushed (256 MB write) between timed steps", quick=bool(args.quick)),
+        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * cfg["k"] * 4)},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(),
+        "build_s": t_build,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 # ---- C4: graph index ------------------------------------------------------------

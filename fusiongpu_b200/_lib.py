@@ -61,6 +61,8 @@ _SIGS = {
     "fg_batch_logic": [C.POINTER(IvfpqView), _P, _I32, _P, _P, C.POINTER(SearchParams), _P, _P, _P, _P, _P],
     "fg_probe_budget": [_P, _I32, _P, _P, _I32, _I32, _F, _P, _P, _P],
     "fg_rerank": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
+    "fg_rerank_u8": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
+    "fg_search_u8": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, C.POINTER(SearchParams), _P, _P, _P, _SZ, _P],
     "fg_search_workspace_size": [C.POINTER(IvfpqView), C.POINTER(SearchParams), _I32, C.POINTER(_SZ)],
     "fg_search": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, C.POINTER(SearchParams), _P, _P, _P, _SZ, _P],
     "fg_map_ids": [_P, _I64, _P, _I64, _P, _P],

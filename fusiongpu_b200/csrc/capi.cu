@@ -37,8 +37,8 @@ int check_launch(const char* what) {
 // implemented in the kernel files
 int batch_logic(const fg_ivfpq_view*, const float*, int, const uint32_t*, const float*, const fg_search_params*,
                 int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad);
-int rerank(const float*, int, int, const int32_t*, const int32_t*, const float*, long long, const fg_search_params*,
-           int32_t*, float*, cudaStream_t);
+int rerank(const float*, int, int, const int32_t*, const int32_t*, const void*, int, long long,
+           const fg_search_params*, int32_t*, float*, cudaStream_t);
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
              float* out_v, void* ws, size_t ws_bytes, cudaStream_t s, int metric = FG_METRIC_L2);
 size_t knn_like_workspace(long long nq, int ncols, int k);
@@ -202,7 +202,14 @@ int fg_probe_budget(const int32_t* list_offsets, int32_t nlist, const uint32_t* 
 int fg_rerank(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids, const int32_t* top_counts,
               const float* base, int64_t nbase, const fg_search_params* params, int32_t* out_ids, float* out_dists,
               void* stream) {
-    return rerank(queries, nq, dim, top_ids, top_counts, base, nbase, params, out_ids, out_dists,
+    return rerank(queries, nq, dim, top_ids, top_counts, base, 0, nbase, params, out_ids, out_dists,
+                  as_stream(stream));
+}
+
+int fg_rerank_u8(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids, const int32_t* top_counts,
+                 const uint8_t* base, int64_t nbase, const fg_search_params* params, int32_t* out_ids,
+                 float* out_dists, void* stream) {
+    return rerank(queries, nq, dim, top_ids, top_counts, base, 1, nbase, params, out_ids, out_dists,
                   as_stream(stream));
 }
 
@@ -216,9 +223,9 @@ int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params*
     return FG_OK;
 }
 
-int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries, int32_t nq,
-              const fg_search_params* params, int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes,
-              void* stream) {
+static int search_any(const fg_ivfpq_view* index, const void* base, int base_u8, int64_t nbase, const float* queries,
+                      int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists, void* ws,
+                      size_t ws_bytes, void* stream) {
     FG_REQUIRE(index && params, "null index or params");
     FG_REQUIRE(nq >= 0, "nq < 0");
     if (nq == 0) return FG_OK;
@@ -242,7 +249,19 @@ int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, cons
     // the rerank reads only the first top_counts[q] entries: skip the padding
     rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false);
     if (rc) return rc;
-    return rerank(queries, nq, index->dim, tid, tc, base, nbase, params, out_ids, out_dists, s);
+    return rerank(queries, nq, index->dim, tid, tc, base, base_u8, nbase, params, out_ids, out_dists, s);
+}
+
+int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries, int32_t nq,
+              const fg_search_params* params, int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes,
+              void* stream) {
+    return search_any(index, base, 0, nbase, queries, nq, params, out_ids, out_dists, ws, ws_bytes, stream);
+}
+
+int fg_search_u8(const fg_ivfpq_view* index, const uint8_t* base, int64_t nbase, const float* queries, int32_t nq,
+                 const fg_search_params* params, int32_t* out_ids, float* out_dists, void* ws, size_t ws_bytes,
+                 void* stream) {
+    return search_any(index, base, 1, nbase, queries, nq, params, out_ids, out_dists, ws, ws_bytes, stream);
 }
 
 int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_t seed, float* centroids,

@@ -143,7 +143,23 @@ __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict_
 }
 
 constexpr int TK_NT = 512;
-constexpr int TK_SEG = 8192;  // columns per stage-1 segment (32 KB of keys)
+constexpr int TK_SEG = 8192;          // columns per stage-1 segment (32 KB of keys), at least
+constexpr int TK_STAGE_MAX = 32768;   // candidates stage 2 selects from, at most
+
+// Stage-1 segment length: TK_SEG, or longer when the per-segment winners of a
+// very wide row (100M columns) would not fit stage 2.
+static int topk_seg_len(int ncols, int k) {
+    if (ncols <= TK_SEG) return ncols;
+    const long long nseg_max = std::max(1, TK_STAGE_MAX / std::max(k, 1));
+    const long long need = (ncols + nseg_max - 1) / nseg_max;  // ceil(ncols / seg) <= nseg_max
+    const long long seg = std::max<long long>(TK_SEG, (need + 3) / 4 * 4);
+    return (int)std::min<long long>(seg, ncols);
+}
+
+static int topk_nseg(int ncols, int k) {
+    const int seg = topk_seg_len(ncols, k);
+    return (ncols + seg - 1) / seg;
+}
 
 // Top-k (ascending by value, ties by column/position) of one segment of one
 // row.  Input value v[row][c0 + i] with row stride ldv; optional payload
@@ -211,8 +227,8 @@ __global__ void __launch_bounds__(TK_NT) topk_segment_kernel(const float* __rest
 int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, int32_t* out_i,
               float* out_v, long long out_ld, float* stage_v, int32_t* stage_i, cudaStream_t s) {
     if (rows <= 0) return FG_OK;
-    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
-    const int seg_len = nseg == 1 ? ncols : TK_SEG;
+    const int nseg = topk_nseg(ncols, k);
+    const int seg_len = nseg == 1 ? ncols : topk_seg_len(ncols, k);
     auto smem_for = [&](int len, int kk) { return round_up_dev(len * 4) + next_pow2(kk) * 8; };
     if (nseg == 1) {
         const int sm = smem_for(seg_len, k);
@@ -223,13 +239,18 @@ int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, i
     }
     const long long sld = (long long)nseg * k;
     int sm = smem_for(seg_len, k);
+    int dev = 0, smem_max = 0;
+    FG_CUDA_TRY(cudaGetDevice(&dev));
+    FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (sm > smem_max || sld > TK_STAGE_MAX)
+        return fail(FG_ERR_UNSUPPORTED, "top-%d of %d columns per row is beyond the two-stage select", k, ncols);
     FG_CUDA_TRY(cudaFuncSetAttribute(topk_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      std::max(sm, smem_for((int)sld, k))));
     topk_segment_kernel<<<dim3((unsigned)rows, nseg), TK_NT, sm, s>>>(v, ldv, ncols, seg_len, nullptr, k,
                                                                      stage_i, stage_v, sld);
     int rc = check_launch("topk_segment_kernel(stage 1)");
     if (rc) return rc;
-    if (sld > TK_SEG * 4) return fail(FG_ERR_UNSUPPORTED, "top-k stage 2 of %lld candidates", sld);
+    if (sld > TK_STAGE_MAX) return fail(FG_ERR_UNSUPPORTED, "top-k stage 2 of %lld candidates", sld);
     sm = smem_for((int)sld, k);
     topk_segment_kernel<<<dim3((unsigned)rows, 1), TK_NT, sm, s>>>(stage_v, sld, (int)sld, (int)sld, stage_i,
                                                                    k, out_i, out_v, out_ld);
@@ -237,7 +258,7 @@ int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, i
 }
 
 size_t rows_topk_stage_bytes(long long rows, int ncols, int k) {
-    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const int nseg = topk_nseg(ncols, k);
     if (nseg == 1) return 0;
     return round_up((size_t)rows * nseg * k * 4, 256) * 2;
 }
@@ -276,7 +297,7 @@ int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int
 
 static long long chunk_rows(size_t ws_bytes, long long nrows, int ncols, int k) {
     // matrix [r][ncols] + stage buffers [r][nseg*k] x2
-    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const int nseg = topk_nseg(ncols, k);
     const size_t per_row = (size_t)ncols * 4 + (nseg > 1 ? (size_t)nseg * k * 8 : 0);
     if (ws_bytes < 1024) return 0;
     long long r = (long long)((ws_bytes - 1024) / per_row);
@@ -286,7 +307,7 @@ static long long chunk_rows(size_t ws_bytes, long long nrows, int ncols, int k) 
 
 size_t knn_like_workspace(long long nq, int ncols, int k) {
     const long long want = std::min<long long>(nq, std::max<long long>(64, (256ll << 20) / ((long long)ncols * 4)));
-    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const int nseg = topk_nseg(ncols, k);
     size_t b = round_up((size_t)want * ncols * 4, 256);
     if (nseg > 1) b += round_up((size_t)want * nseg * k * 4, 256) * 2;
     return b + 1024;
@@ -299,7 +320,7 @@ int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq
     long long rows = chunk_rows(ws_bytes, nq, ncols, k);
     if (rows < 1) return fail(FG_ERR_WORKSPACE, "workspace of %zu bytes holds no row of %d distances",
                               ws_bytes, ncols);
-    const int nseg = (ncols + TK_SEG - 1) / TK_SEG;
+    const int nseg = topk_nseg(ncols, k);
     for (long long q0 = 0; q0 < nq; q0 += rows) {
         const long long r = std::min(rows, nq - q0);
         Carve cv(ws, ws_bytes);

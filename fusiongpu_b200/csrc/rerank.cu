@@ -24,7 +24,7 @@ struct RerankArgs {
     const int32_t* top_ids;
     const int32_t* top_counts;
     int rm;
-    const float* base;
+    const void* base;  // [nbase][dim] float or uint8
     long long nbase;
     int k, mb, nw;
     float eps;
@@ -79,6 +79,49 @@ __device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const fl
     return d;
 }
 
+// The same for uint8 rows (C5's raw vectors): each byte converts exactly to
+// float, so the result equals exact_l2 on a float copy.  Sixteen bytes per load.
+__device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const uint8_t* __restrict__ v, int dim) {
+    float d = 0.0f;
+    if ((dim & 15) == 0) {
+        const uint4* v16 = reinterpret_cast<const uint4*>(v);
+        const int n16 = dim >> 4;
+        int t = 0;
+        for (; t + 4 <= n16; t += 4) {
+            uint4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = __ldg(v16 + t + u);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float xv = (float)((w[e >> 2] >> (8 * (e & 3))) & 0xffu);
+                    const float df = sq[16 * (t + u) + e] - xv;
+                    d = fmaf(df, df, d);
+                }
+            }
+        }
+        for (; t < n16; ++t) {
+            const uint4 x = __ldg(v16 + t);
+            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float xv = (float)((w[e >> 2] >> (8 * (e & 3))) & 0xffu);
+                const float df = sq[16 * t + e] - xv;
+                d = fmaf(df, df, d);
+            }
+        }
+    } else {
+        for (int t = 0; t < dim; ++t) {
+            const float df = sq[t] - (float)__ldg(v + t);
+            d = fmaf(df, df, d);
+        }
+    }
+    return d;
+}
+
+template <class T>
 __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp[RR_NT / 32];
@@ -113,7 +156,8 @@ __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
         for (int i = tid; i < m; i += RR_NT) {
             const int32_t vid = a.top_ids[(size_t)q * a.rm + off + i];
             float dist = FLT_MAX;
-            if (vid >= 0 && (long long)vid < a.nbase) dist = exact_l2(s_q, a.base + (size_t)vid * a.dim, a.dim);
+            if (vid >= 0 && (long long)vid < a.nbase)
+                dist = exact_l2(s_q, static_cast<const T*>(a.base) + (size_t)vid * a.dim, a.dim);
             wd[i] = dist;
             wi[i] = vid;
         }
@@ -180,7 +224,7 @@ __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
 }
 
 int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const int32_t* top_counts,
-           const float* base, long long nbase, const fg_search_params* p, int32_t* out_ids,
+           const void* base, int base_u8, long long nbase, const fg_search_params* p, int32_t* out_ids,
            float* out_dists, cudaStream_t stream) {
     FG_REQUIRE(p, "null params");
     FG_REQUIRE(nq >= 0 && dim > 0, "bad nq/dim");
@@ -189,7 +233,8 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
                "ref_compat needs final_k <= 128 (the reference's block sort has 128 slots)");
     if (nq == 0) return FG_OK;
     FG_REQUIRE(queries && top_ids && top_counts && base && out_ids && out_dists, "null buffer");
-    FG_REQUIRE(dim % 4 != 0 || (aligned(base, 16) && aligned(queries, 16)), "base/queries must be 16-byte aligned");
+    FG_REQUIRE(dim % 4 != 0 || aligned(queries, 16), "queries must be 16-byte aligned");
+    FG_REQUIRE(dim % (base_u8 ? 16 : 4) != 0 || aligned(base, 16), "base must be 16-byte aligned");
     RerankArgs a;
     a.queries = queries;
     a.dim = dim;
@@ -212,8 +257,15 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     if (smem > (size_t)smem_max - 1024)
         return fail(FG_ERR_UNSUPPORTED, "rerank needs %zu bytes of shared memory", smem);
-    FG_CUDA_TRY(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    rerank_kernel<<<nq, RR_NT, smem, stream>>>(a);
+    if (base_u8) {
+        FG_CUDA_TRY(cudaFuncSetAttribute(rerank_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        rerank_kernel<uint8_t><<<nq, RR_NT, smem, stream>>>(a);
+    } else {
+        FG_CUDA_TRY(cudaFuncSetAttribute(rerank_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        rerank_kernel<float><<<nq, RR_NT, smem, stream>>>(a);
+    }
     return check_launch("rerank_kernel");
 }
 

@@ -188,9 +188,28 @@ def knn_exact(base, queries, k: int, device="cuda") -> tuple[torch.Tensor, torch
     return ids, dist
 
 
+def _base_tensor(base, device) -> torch.Tensor | None:
+    """Raw vectors for the rerank: uint8 stays uint8 (fg_search_u8), anything
+    else becomes float32."""
+    if base is None:
+        return None
+    t = base if torch.is_tensor(base) else torch.from_numpy(np.ascontiguousarray(base))
+    if t.dtype == torch.uint8:
+        return t.to(device).contiguous()
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+def kmeans_sample_rows(n: int, sample: int) -> np.ndarray:
+    """Rows k-means trains on when it is given a sample: every
+    (n // sample)-th row, `sample` of them."""
+    step = max(1, n // sample)
+    return (np.arange(min(n, sample), dtype=np.int64) * step)
+
+
 class IVFPQIndex:
     """A device-resident IVF-PQ index (the reference's IVFIndexGPU plus the raw
-    base vectors SearchPipeline keeps for the rerank)."""
+    base vectors SearchPipeline keeps for the rerank; float32, or uint8 for
+    byte-valued datasets)."""
 
     def __init__(self, centroids, codebook, offsets, ids, codes, base=None, device="cuda"):
         self.device = torch.device(device)
@@ -199,7 +218,7 @@ class IVFPQIndex:
         self.offsets = _dev(offsets, torch.int32, device)
         self.ids = _dev(ids, torch.int32, device)
         self.codes = _dev(codes, torch.uint8, device)
-        self.base = _dev(base, torch.float32, device) if base is not None else None
+        self.base = _base_tensor(base, device)
         self.nlist, self.dim = self.centroids.shape
         self.pq_m = self.codes.shape[1]
         self.total = self.ids.shape[0]
@@ -219,13 +238,19 @@ class IVFPQIndex:
     @classmethod
     def build(cls, base, nlist: int, pq_m: int, kmeans_iters: int = 20, pq_sample: int = 50000,
               pq_iters: int = 8, seed: int = 42, keep_base: bool = True, rebalance: bool = True,
-              rebalance_iters: int = 15, device="cuda") -> "IVFPQIndex":
+              rebalance_iters: int = 15, kmeans_sample: int | None = None, device="cuda") -> "IVFPQIndex":
         """k-means -> assignment -> list rebalancing -> residual PQ training ->
         encoding -> lists (build_global.cu:21-258 without the CAGRA graph over
         centroids, which the exact coarse quantizer replaces).  The index has
-        nlist lists or more when rebalancing splits some."""
+        nlist lists or more when rebalancing splits some.  kmeans_sample:
+        train the centroids on that many strided rows (kmeans_sample_rows),
+        then assign every row (the reference trains on all rows)."""
         x = _dev(base, torch.float32, device)
-        cen = run_kmeans_gpu(x, nlist, kmeans_iters, seed, device)
+        xk = x
+        if kmeans_sample and kmeans_sample < x.shape[0]:
+            xk = x[torch.from_numpy(kmeans_sample_rows(x.shape[0], kmeans_sample)).to(x.device)].contiguous()
+        cen = run_kmeans_gpu(xk, nlist, kmeans_iters, seed, device)
+        del xk
         a = gpu_assign_to_centroids(x, cen, device)
         if rebalance:
             a, cen = rebalance_lists(x, a, cen, rebalance_iters, seed, device)
@@ -236,7 +261,11 @@ class IVFPQIndex:
         lcodes = torch.empty_like(codes)
         lids = torch.empty(x.shape[0], dtype=torch.int32, device=x.device)
         _lib.call("fg_gather_lists", _p(codes), x.shape[0], pq_m, _p(order), _p(lcodes), _p(lids), _stream())
-        idx = cls(cen, cb, offsets, lids, lcodes, x if keep_base else None, device)
+        keep = None
+        if keep_base:
+            keep = base if (torch.is_tensor(base) and base.dtype == torch.uint8) or \
+                (isinstance(base, np.ndarray) and base.dtype == np.uint8) else x
+        idx = cls(cen, cb, offsets, lids, lcodes, keep, device)
         idx.assignment = a
         return idx
 
@@ -282,7 +311,8 @@ class IVFPQIndex:
             ids, dist = out
         ws = self.workspace(nq, params)
         cp = params.c()
-        _lib.call("fg_search", C.byref(self._view), _p(self.base), self.base.shape[0], _p(q), nq, C.byref(cp),
+        fn = "fg_search_u8" if self.base.dtype == torch.uint8 else "fg_search"
+        _lib.call(fn, C.byref(self._view), _p(self.base), self.base.shape[0], _p(q), nq, C.byref(cp),
                   _p(ids), _p(dist), _p(ws), ws.numel(), _stream(stream))
         return ids, dist
 
@@ -320,12 +350,13 @@ def run_gpu_rerank(queries, top_ids, top_counts, base, params: SearchParams, dev
     q = _dev(queries, torch.float32, device)
     tid = _dev(top_ids, torch.int32, device)
     tc = _dev(top_counts, torch.int32, device)
-    b = _dev(base, torch.float32, device)
+    b = _base_tensor(base, device)
     nq = q.shape[0]
     ids = torch.empty((nq, params.final_k), dtype=torch.int32, device=device)
     dist = torch.empty((nq, params.final_k), dtype=torch.float32, device=device)
     cp = params.c()
-    _lib.call("fg_rerank", _p(q), nq, q.shape[1], _p(tid), _p(tc), _p(b), b.shape[0], C.byref(cp), _p(ids),
+    fn = "fg_rerank_u8" if b.dtype == torch.uint8 else "fg_rerank"
+    _lib.call(fn, _p(q), nq, q.shape[1], _p(tid), _p(tc), _p(b), b.shape[0], C.byref(cp), _p(ids),
               _p(dist), _stream())
     return ids, dist
 

@@ -152,6 +152,13 @@ int fg_rerank(const float* queries, int32_t nq, int32_t dim, const int32_t* top_
               const int32_t* top_counts, const float* base, int64_t nbase,
               const fg_search_params* params, int32_t* out_ids, float* out_dists, void* stream);
 
+/* The same with uint8 raw vectors [nbase][dim] (C5's base): each byte
+ * converts exactly to float, so results equal fg_rerank on a float copy;
+ * 16-byte loads when dim % 16 == 0 (then the base must be 16-byte aligned). */
+int fg_rerank_u8(const float* queries, int32_t nq, int32_t dim, const int32_t* top_ids,
+                 const int32_t* top_counts, const uint8_t* base, int64_t nbase,
+                 const fg_search_params* params, int32_t* out_ids, float* out_dists, void* stream);
+
 /* ---- full search: coarse + candidate generation + rerank on one stream.
  * Replaces one SearchPipeline::submit_batch (search_pipeline.cu:311-377)
  * minus the host copies. */
@@ -160,6 +167,10 @@ int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params*
 int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries,
               int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists,
               void* workspace, size_t workspace_bytes, void* stream);
+/* fg_search over uint8 raw vectors (fg_rerank_u8 for the last stage). */
+int fg_search_u8(const fg_ivfpq_view* index, const uint8_t* base, int64_t nbase, const float* queries,
+                 int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists,
+                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- sharded search: the exchange step (no counterpart in the single-GPU
  * reference, whose search runs on device 0 only, search_pipeline.cu:560).

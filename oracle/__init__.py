@@ -273,12 +273,17 @@ def rebalance(data, assignment, centroids, iters=15, seed=42, nthreads=0):
 
 
 def build_index(base, nlist, pq_m, kmeans_iters=20, pq_sample=50000, pq_iters=8, nthreads=0,
-                rebalance_lists=True, rebalance_iters=15):
-    """CPU IVF-PQ build with the oracle's semantics: k-means, assignment, list
-    rebalancing (optional), residual PQ; lists hold ids in ascending order.
-    Returns the index dict plus the assignment."""
+                rebalance_lists=True, rebalance_iters=15, kmeans_sample=None):
+    """CPU IVF-PQ build with the oracle's semantics: k-means (on every
+    (n // kmeans_sample)-th row when a sample size is given), assignment of
+    all rows, list rebalancing (optional), residual PQ; lists hold ids in
+    ascending order.  Returns the index dict plus the assignment."""
     base = np.ascontiguousarray(base, np.float32)
-    cen = kmeans(base, nlist, kmeans_iters, 42, nthreads)
+    train = base
+    if kmeans_sample and kmeans_sample < base.shape[0]:
+        step = max(1, base.shape[0] // kmeans_sample)
+        train = np.ascontiguousarray(base[np.arange(kmeans_sample) * step])
+    cen = kmeans(train, nlist, kmeans_iters, 42, nthreads)
     a = assign(base, cen, nthreads)
     if rebalance_lists:
         a, cen = rebalance(base, a, cen, rebalance_iters, 42, nthreads)

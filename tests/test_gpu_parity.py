@@ -367,3 +367,27 @@ def test_assign_tensor_cores_bit_exact(fg, n, k, dim):
     x[:50] = c[1]     # points exactly on the duplicated centroid
     got = fg.gpu_assign_to_centroids(torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda())
     np.testing.assert_array_equal(_np(got), oracle.assign(x, c))
+
+
+def test_uint8_base_search_bit_exact(fg):
+    # C1 vectors are integers in [0, 255]: a uint8 copy holds the same values
+    index, base, q = dataset("int128")
+    assert np.array_equal(base, base.astype(np.uint8).astype(np.float32))
+    idx = fg.IVFPQIndex.from_arrays(index, base.astype(np.uint8))
+    assert idx.base.dtype == torch.uint8
+    for ref_compat in (False, True):
+        p = dict(PARAMS["c1"], ref_compat=ref_compat)
+        ids, d = idx.search(torch.from_numpy(q).cuda(), fg.SearchParams(**p))
+        ei, ed = oracle.search(index, base, q, **p)
+        np.testing.assert_array_equal(_np(ids), ei)
+        np.testing.assert_array_equal(_np(d), ed)
+
+
+def test_sampled_kmeans_build_bit_exact(fg):
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.build(torch.from_numpy(base).cuda(), 64, 32, kmeans_iters=4, pq_sample=5000, pq_iters=3,
+                              kmeans_sample=6000)
+    eidx, _ = oracle.build_index(base, 64, 32, kmeans_iters=4, pq_sample=5000, pq_iters=3, kmeans_sample=6000)
+    got = idx.to_numpy()
+    for k in ("centroids", "codebook", "offsets", "ids", "codes"):
+        np.testing.assert_array_equal(got[k], eidx[k])
