@@ -539,15 +539,22 @@ def main_c3(args):
         torch.cuda.synchronize(device)
         rec = recall_at(ids.cpu().numpy(), gt, 10)
         ms = timed(lambda: idx.search(qd, p, out=(ids, dd)), args.steps)
-        lat = {}
+        lat, lat_graph = {}, {}
         for b in cfg["batches"]:
-            if b >= nq:
-                lat[str(b)] = ms
-                continue
+            b = min(b, nq)
             qb = qd[:b].contiguous()
+            if b < nq:
+                for _ in range(args.warmup):
+                    idx.search(qb, p)
+                lat[str(b)] = timed(lambda: idx.search(qb, p), args.steps)
+            else:
+                lat[str(b)] = ms
+            g = idx.capture(b, p)  # the same search as one CUDA graph replay
+            g.queries.copy_(qb)
             for _ in range(args.warmup):
-                idx.search(qb, p)
-            lat[str(b)] = timed(lambda: idx.search(qb, p), args.steps)
+                g.replay()
+            lat_graph[str(b)] = timed(g.replay, args.steps)
+            del g
         # roofline of the scan kernel alone
         pid, pdist = idx.coarse(qd, cfg["nprobe"])
         lens = (idx.offsets[1:] - idx.offsets[:-1]).to(torch.int64)
@@ -597,6 +604,7 @@ def main_c3(args):
                        lists=idx.nlist, l2="flushed (256 MB write) between timed steps", quick=bool(args.quick),
                        mode="intended (full rerank_m gather)"),
         "latency_ms_by_batch": lat,
+        "latency_ms_by_batch_cuda_graph": lat_graph,
         "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
         "gpu_launches": 4 * args.steps,

@@ -4,7 +4,7 @@
 //   fg_search_pipeline <base> <query> [gt] [-b 128] [-m 20] [-r 10000] [-mb 128]
 //       [-e 0.1] [--beta 2] [-p 100] [-s 2] [-k 10] [--p1_lists 12] [--limit_k 50]
 //       [--threshold_coeff 1.0] [--res ../res] [--pq_m 32] [--intended] [--fused]
-//       [--out results.ivecs] [--repeat 1]
+//       [--graph] [--out results.ivecs] [--repeat 1]
 //
 // Queries are cut into batches and handed round-robin to `-s` stream
 // contexts; each batch runs H2D copy -> coarse search -> candidate generation
@@ -16,7 +16,9 @@
 // By default the search reproduces the reference's results (ref_compat: the
 // 128-lane gather and the other quirks of gpu_global.cu); --intended uses the
 // full rerank depth.  --fused issues one fg_search call per batch instead of
-// the three stage calls (no per-stage times then).
+// the three stage calls (no per-stage times then).  --graph captures a full
+// batch (H2D copy, the search, D2H copy) once per stream context as a CUDA
+// graph and replays it (partial batches run eagerly; no per-stage times).
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
@@ -48,6 +50,7 @@ struct Ctx {
     DevBuf<uint8_t> ws;
     size_t ws_bytes = 0;
     cudaEvent_t e[7];  // h2d start/end, coarse end, batch end, rerank end, d2h end (= done), spare
+    cudaGraphExec_t graph = nullptr;  // a captured full batch (--graph)
     int n = 0;
     int64_t offset = 0;
     bool busy = false;
@@ -58,8 +61,15 @@ struct Ctx {
 class SearchPipeline {
    public:
     SearchPipeline(const DevIndex& idx, const float* d_base, int64_t nbase, const fg_search_params& p, int batch,
-                   int nstreams, int64_t nq, bool fused)
-        : idx_(idx), base_(d_base), nbase_(nbase), p_(p), batch_(batch), fused_(fused), results_((size_t)nq * p.final_k) {
+                   int nstreams, int64_t nq, bool fused, bool graph)
+        : idx_(idx),
+          base_(d_base),
+          nbase_(nbase),
+          p_(p),
+          batch_(batch),
+          fused_(fused),
+          use_graph_(graph),
+          results_((size_t)nq * p.final_k) {
         const int dim = idx.view.dim;
         for (int i = 0; i < nstreams; ++i) {
             auto c = std::make_unique<Ctx>();
@@ -97,6 +107,7 @@ class SearchPipeline {
         qcv_.notify_all();
         worker_.join();
         for (auto& c : ctx_) {
+            if (c->graph) cudaGraphExecDestroy(c->graph);
             for (cudaEvent_t ev : c->e) cudaEventDestroy(ev);
             cudaFreeHost(c->h_q);
             cudaFreeHost(c->h_ids);
@@ -113,41 +124,66 @@ class SearchPipeline {
             c.cv.wait(lk, [&] { return !c.busy; });
             c.busy = true;
         }
-        const int dim = idx_.view.dim, k = p_.final_k;
+        const int dim = idx_.view.dim;
         c.n = n;
         c.offset = offset;
         std::memcpy(c.h_q, queries, (size_t)n * dim * 4);
-        cudaEventRecord(c.e[0], c.s);
-        check_cuda(cudaMemcpyAsync(c.q.p, c.h_q, (size_t)n * dim * 4, cudaMemcpyHostToDevice, c.s), "H2D");
-        cudaEventRecord(c.e[1], c.s);
-        if (fused_) {
-            check(fg_search(&idx_.view, base_, nbase_, c.q.p, n, &p_, c.fi.p, c.fd.p, c.ws.p, c.ws_bytes, c.s),
-                  "fg_search");
-            cudaEventRecord(c.e[2], c.s);
-            cudaEventRecord(c.e[3], c.s);
+        if (use_graph_ && n == batch_) {
+            if (!c.graph) {
+                // the whole batch as one graph: H2D, the search, D2H
+                cudaGraph_t g;
+                check_cuda(cudaStreamBeginCapture(c.s, cudaStreamCaptureModeThreadLocal), "begin capture");
+                enqueue(c, n);
+                check_cuda(cudaStreamEndCapture(c.s, &g), "end capture");
+                check_cuda(cudaGraphInstantiate(&c.graph, g, 0), "graph instantiate");
+                cudaGraphDestroy(g);
+            }
+            cudaEventRecord(c.e[0], c.s);
+            for (int i = 1; i < 5; ++i) cudaEventRecord(c.e[i], c.s);
+            check_cuda(cudaGraphLaunch(c.graph, c.s), "graph launch");
+            cudaEventRecord(c.e[5], c.s);
         } else {
-            check(fg_coarse_search(idx_.view.centroids, idx_.view.nlist, dim, c.q.p, n, p_.top_m, c.pid.p, c.pd.p,
-                                   c.ws.p, c.ws_bytes, c.s),
-                  "fg_coarse_search");
-            cudaEventRecord(c.e[2], c.s);
-            check(fg_batch_logic(&idx_.view, c.q.p, n, c.pid.p, c.pd.p, &p_, c.top_i.p, c.top_d.p, c.top_c.p,
-                                 c.cand.p, c.s),
-                  "fg_batch_logic");
-            cudaEventRecord(c.e[3], c.s);
-            check(fg_rerank(c.q.p, n, dim, c.top_i.p, c.top_c.p, base_, nbase_, &p_, c.fi.p, c.fd.p, c.s),
-                  "fg_rerank");
+            cudaEventRecord(c.e[0], c.s);
+            enqueue(c, n, true);
+            cudaEventRecord(c.e[5], c.s);
         }
-        cudaEventRecord(c.e[4], c.s);
-        check_cuda(cudaMemcpyAsync(c.h_ids, c.fi.p, (size_t)n * k * 4, cudaMemcpyDeviceToHost, c.s), "D2H");
-        if (!fused_)
-            check_cuda(cudaMemcpyAsync(c.h_cand, c.cand.p, (size_t)n * 4, cudaMemcpyDeviceToHost, c.s), "D2H");
-        cudaEventRecord(c.e[5], c.s);
         {
             std::lock_guard<std::mutex> lk(qm_);
             work_.push(&c);
             ++pending_;
         }
         qcv_.notify_all();
+    }
+
+    // H2D copy, search, D2H copy of one batch on the context's stream; with
+    // `events`, the stage boundaries are recorded (not inside a capture)
+    void enqueue(Ctx& c, int n, bool events = false) {
+        const int dim = idx_.view.dim, k = p_.final_k;
+        check_cuda(cudaMemcpyAsync(c.q.p, c.h_q, (size_t)n * dim * 4, cudaMemcpyHostToDevice, c.s), "H2D");
+        if (events) cudaEventRecord(c.e[1], c.s);
+        if (fused_) {
+            check(fg_search(&idx_.view, base_, nbase_, c.q.p, n, &p_, c.fi.p, c.fd.p, c.ws.p, c.ws_bytes, c.s),
+                  "fg_search");
+            if (events) {
+                cudaEventRecord(c.e[2], c.s);
+                cudaEventRecord(c.e[3], c.s);
+            }
+        } else {
+            check(fg_coarse_search(idx_.view.centroids, idx_.view.nlist, dim, c.q.p, n, p_.top_m, c.pid.p, c.pd.p,
+                                   c.ws.p, c.ws_bytes, c.s),
+                  "fg_coarse_search");
+            if (events) cudaEventRecord(c.e[2], c.s);
+            check(fg_batch_logic(&idx_.view, c.q.p, n, c.pid.p, c.pd.p, &p_, c.top_i.p, c.top_d.p, c.top_c.p,
+                                 c.cand.p, c.s),
+                  "fg_batch_logic");
+            if (events) cudaEventRecord(c.e[3], c.s);
+            check(fg_rerank(c.q.p, n, dim, c.top_i.p, c.top_c.p, base_, nbase_, &p_, c.fi.p, c.fd.p, c.s),
+                  "fg_rerank");
+        }
+        if (events) cudaEventRecord(c.e[4], c.s);
+        check_cuda(cudaMemcpyAsync(c.h_ids, c.fi.p, (size_t)n * k * 4, cudaMemcpyDeviceToHost, c.s), "D2H");
+        if (!fused_)
+            check_cuda(cudaMemcpyAsync(c.h_cand, c.cand.p, (size_t)n * 4, cudaMemcpyDeviceToHost, c.s), "D2H");
     }
 
     void wait_all() {
@@ -216,6 +252,7 @@ class SearchPipeline {
     fg_search_params p_;
     int batch_;
     bool fused_;
+    bool use_graph_;
     std::vector<std::unique_ptr<Ctx>> ctx_;
     size_t next_ = 0;
     std::vector<int32_t> results_;
@@ -231,12 +268,12 @@ class SearchPipeline {
 }  // namespace
 
 int main(int argc, char** argv) {
-    Args a(argc, argv, {"--intended", "--fused"});
+    Args a(argc, argv, {"--intended", "--fused", "--graph"});
     if (a.pos.size() < 2) {
         std::cerr << "Usage: fg_search_pipeline <base> <query> [gt] [-b 128] [-m 20] [-r 10000] [-mb 128] [-e 0.1]\n"
                      "       [--beta 2] [-p 100] [-s 2] [-k 10] [--p1_lists 12] [--limit_k 50]\n"
                      "       [--threshold_coeff 1.0] [--res ../res] [--pq_m 32] [--intended] [--fused]\n"
-                     "       [--out results.ivecs] [--repeat 1]\n";
+                     "       [--graph] [--out results.ivecs] [--repeat 1]\n";
         return 1;
     }
     fg_search_params p;
@@ -258,6 +295,7 @@ int main(int argc, char** argv) {
     const int pq_m = a.geti({"--pq_m"}, 32);
     const int repeat = std::max(1, a.geti({"--repeat"}, 1));
     const bool fused = a.has("--fused");
+    const bool graph = a.has("--graph");
     if (batch < 1 || nstreams < 1) die("batch size and stream count must be positive");
 
     std::vector<float> base, queries;
@@ -282,7 +320,7 @@ int main(int argc, char** argv) {
     StageTimes t;
     std::vector<int32_t> results;
     {
-        SearchPipeline pipe(idx, d_base.p, nbase, p, batch, nstreams, nq, fused);
+        SearchPipeline pipe(idx, d_base.p, nbase, p, batch, nstreams, nq, fused, graph);
         // warm-up: one batch per stream context
         for (int i = 0; i < nstreams; ++i) pipe.submit(queries.data(), (int)std::min<int64_t>(nq, batch), 0);
         pipe.wait_all();
@@ -302,7 +340,8 @@ int main(int argc, char** argv) {
     std::cout << std::fixed << std::setprecision(3) << "\n=========== Per-batch stage times (avg, ms) ===========\n"
               << "  H2D copy:      " << t.h2d / nb << "\n"
               << "  Coarse search: " << t.coarse / nb << "\n"
-              << "  Candidates:    " << t.batch / nb << (fused ? "  (fused: whole search above)" : "") << "\n"
+              << "  Candidates:    " << t.batch / nb << (fused ? "  (fused: whole search above)" : "")
+              << (graph ? "  (graph replays: stages not timed separately)" : "") << "\n"
               << "  Rerank:        " << t.rerank / nb << "\n"
               << "  D2H copy:      " << t.d2h / nb << "\n"
               << "  E2E per batch: " << t.e2e / nb << "\n"

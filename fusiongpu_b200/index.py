@@ -316,6 +316,12 @@ class IVFPQIndex:
                   _p(ids), _p(dist), _p(ws), ws.numel(), _stream(stream))
         return ids, dist
 
+    def capture(self, nq: int, params: SearchParams | None = None) -> "SearchGraph":
+        """A CUDA graph of one search of `nq` queries with these parameters,
+        for replay in launch-bound (small-batch) serving: the search needs no
+        allocation and no host synchronisation once its workspace exists."""
+        return SearchGraph(self, nq, params or SearchParams())
+
     def coarse(self, queries, top_m: int):
         return coarse_search(queries, self.centroids, top_m, self.device)
 
@@ -324,6 +330,33 @@ class IVFPQIndex:
 
     def rerank(self, queries, top_ids, top_counts, params: SearchParams):
         return run_gpu_rerank(queries, top_ids, top_counts, self.base, params, self.device)
+
+
+class SearchGraph:
+    """One captured search: copy queries into `self.queries`, call replay(),
+    read `self.ids` / `self.dists` (all on the index's device)."""
+
+    def __init__(self, index: IVFPQIndex, nq: int, params: SearchParams):
+        self.index, self.params = index, params
+        dev = index.device
+        self.queries = torch.zeros((nq, index.dim), dtype=torch.float32, device=dev)
+        self.ids = torch.empty((nq, params.final_k), dtype=torch.int32, device=dev)
+        self.dists = torch.empty((nq, params.final_k), dtype=torch.float32, device=dev)
+        index.workspace(nq, params)  # allocate before capture
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm up (attributes, tensor maps) outside the graph
+            index.search(self.queries, params, out=(self.ids, self.dists))
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            index.search(self.queries, params, out=(self.ids, self.dists))
+
+    def replay(self, queries=None):
+        if queries is not None:
+            self.queries.copy_(queries, non_blocking=True)
+        self.graph.replay()
+        return self.ids, self.dists
 
 
 def run_gpu_batch_logic(index: IVFPQIndex, queries, probe_ids, probe_dists, params: SearchParams):

@@ -391,3 +391,16 @@ def test_sampled_kmeans_build_bit_exact(fg):
     got = idx.to_numpy()
     for k in ("centroids", "codebook", "offsets", "ids", "codes"):
         np.testing.assert_array_equal(got[k], eidx[k])
+
+
+def test_search_graph_replay_matches_eager(fg):
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    p = fg.SearchParams(**PARAMS["c1"])
+    g = idx.capture(64, p)
+    for s in (0, 64, 128):
+        qb = torch.from_numpy(q[s:s + 64]).cuda()
+        ids, d = g.replay(qb)
+        ei, ed = idx.search(qb, p)
+        np.testing.assert_array_equal(_np(ids), _np(ei))
+        np.testing.assert_array_equal(_np(d), _np(ed))

@@ -78,20 +78,23 @@ def test_build_global_program_bit_exact(work):
     np.testing.assert_array_equal(counts, np.diff(exp["offsets"]))
 
 
-@pytest.mark.parametrize("mode", ["reference", "intended", "fused"])
+@pytest.mark.parametrize("mode", ["reference", "intended", "fused", "graph"])
 def test_search_pipeline_program_bit_exact(work, mode):
     d = work["dir"]
     args = [os.path.join(BIN, "fg_search_pipeline"), "base.fvecs", "q.fvecs", "gt.ivecs", "--res", "res", "--pq_m",
             str(PQ_M), "-b", "64", "-s", "2", "-m", str(SEARCH["top_m"]), "-r", str(SEARCH["rerank_m"]), "-k",
             str(SEARCH["final_k"]), "--out", f"out_{mode}.ivecs"]
-    if mode != "reference":
+    if mode not in ("reference", "graph"):
         args.append("--intended")
     if mode == "fused":
         args.append("--fused")
+    if mode == "graph":
+        args += ["--graph", "-b", "50"]  # 300 queries: six full batches, all replayed
     out = _run(args, cwd=d)
     from fusiongpu_b200 import formats
     ids = formats.read_vecs(str(d / f"out_{mode}.ivecs"), np.int32)
-    exp, _ = oracle.search(work["index"], work["base"], work["q"], ref_compat=(mode == "reference"), **SEARCH)
+    exp, _ = oracle.search(work["index"], work["base"], work["q"], ref_compat=(mode in ("reference", "graph")),
+                           **SEARCH)
     np.testing.assert_array_equal(ids, exp)
     m = re.search(r"RESULT qps=(\S+) recall1=(\S+) recall10=(\S+)", out)
     assert m, out
