@@ -95,7 +95,58 @@ struct GemmArgs {
     int* err;
 };
 
-enum { GEMM_MATRIX = 0, GEMM_FILTER = 1 };
+enum { GEMM_MATRIX = 0, GEMM_FILTER = 1, GEMM_TOPK = 2 };
+constexpr int TC_TOPT = 8;      // GEMM_TOPK: approximate candidates kept per (query, column run, half)
+constexpr int TC_TOPK_MAXP = 4;  // top_m up to which the single-pass GEMM_TOPK path runs
+
+// Norms of the 32 columns col0.. (0 past ncols).
+__device__ __forceinline__ void load_norms(const float* __restrict__ cn, int col0, int ncols, float (&c)[32]) {
+    if (col0 + 32 <= ncols) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(cn + col0 + j));
+            c[j] = c4.x;
+            c[j + 1] = c4.y;
+            c[j + 2] = c4.z;
+            c[j + 3] = c4.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) c[j] = (col0 + j < ncols) ? __ldg(cn + col0 + j) : 0.0f;
+    }
+}
+
+// v[j] for a lane-varying j by a five-level select tree: every index is
+// static, so v stays in registers.
+__device__ __forceinline__ float select32(const float (&v)[32], int j) {
+    float a[16], b[8], c[4], d[2];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) a[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) b[t] = (j & 2) ? a[2 * t + 1] : a[2 * t];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) c[t] = (j & 4) ? b[2 * t + 1] : b[2 * t];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) d[t] = (j & 8) ? c[2 * t + 1] : c[2 * t];
+    return (j & 16) ? d[1] : d[0];
+}
+
+// Insert x into the ascending list bd (x < bd[T-1]); equal keys keep their
+// order, so an earlier column stays ahead.  Every slot's update is
+// independent of the others: no serial compare-swap chain.
+template <int T>
+__device__ __forceinline__ void insert_sorted(float (&bd)[T], int32_t (&bi)[T], float x, int32_t xi) {
+    bool lt[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) lt[t] = x < bd[t];
+#pragma unroll
+    for (int t = T - 1; t > 0; --t) {
+        bd[t] = lt[t - 1] ? bd[t - 1] : (lt[t] ? x : bd[t]);
+        bi[t] = lt[t - 1] ? bi[t - 1] : (lt[t] ? xi : bi[t]);
+    }
+    bd[0] = lt[0] ? x : bd[0];
+    bi[0] = lt[0] ? xi : bi[0];
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(TC_NT, 1)
@@ -185,31 +236,33 @@ __global__ void __launch_bounds__(TC_NT, 1)
         // each (query, column half) belongs to exactly one thread: its segment needs no atomics
         const long long seg = ((qg * gridDim.y + blockIdx.y) * 2 + half) * (long long)g.cap;
         int n = 0;
+        // GEMM_TOPK: the TC_TOPT smallest d~ of this thread's columns, ascending
+        float bd[TC_TOPT];
+        int32_t bi[TC_TOPT];
+#pragma unroll
+        for (int t = 0; t < TC_TOPT; ++t) {
+            bd[t] = INFINITY;
+            bi[t] = -1;
+        }
+        // column norms of the next chunk are loaded one tile ahead, so their
+        // latency hides behind the accumulator wait instead of following it
+        float cnext[32];
+        load_norms(g.cn, tile0 * TC_N + half * 32, g.ncols, cnext);
         for (int i = 0; i < nt; ++i) {
             const int acc = i & 1, ph = (i >> 1) & 1;
+            float c[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) c[j] = cnext[j];
+            const int col0 = (tile0 + i) * TC_N + half * 32;
+            if (i + 1 < nt) load_norms(g.cn, col0 + TC_N, g.ncols, cnext);
             if (!__all_sync(0xffffffffu, tc::mbar_wait_or_fail(&acc_full[acc], ph, fail))) break;
             tc::fence_after_sync();
             float v[32];
             tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + half * 32), v);
             tc::fence_before_sync();
             tc::mbar_arrive(&acc_empty[acc]);
-            if (!valid) continue;
-            const int col0 = (tile0 + i) * TC_N + half * 32;
-            // all column norms of the chunk first, so no load waits behind a store
-            float c[32];
-            if (col0 + 32 <= g.ncols) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(g.cn + col0 + j));
-                    c[j] = c4.x;
-                    c[j + 1] = c4.y;
-                    c[j + 2] = c4.z;
-                    c[j + 3] = c4.w;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) c[j] = (col0 + j < g.ncols) ? __ldg(g.cn + col0 + j) : 0.0f;
-            }
+            // GEMM_TOPK keeps every lane in the loop: its candidate rounds are warp-collective
+            if (!valid && MODE != GEMM_TOPK) continue;
             const int ncol = min(32, g.ncols - col0);
             if (MODE == GEMM_MATRIX) {
                 uint32_t* o = g.out + (long long)row * g.ldo + col0;
@@ -227,6 +280,34 @@ __global__ void __launch_bounds__(TC_NT, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
+                }
+            } else if (MODE == GEMM_TOPK) {
+                // u = cn - 2 dp orders this thread's columns as d~ = qn + u does
+                // (qn is constant per thread, and adding it is monotone); the
+                // list keeps u and adds qn once, when it is written out
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
+                float m[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) m[j] = fminf(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+                for (int w = 8; w; w >>= 1)
+#pragma unroll
+                    for (int j = 0; j < w; ++j) m[j] = fminf(m[j], m[j + w]);
+                unsigned cand = 0;
+                if (valid && m[0] < bd[TC_TOPT - 1]) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) cand |= (v[j] < bd[TC_TOPT - 1]) ? (1u << j) : 0u;
+                }
+                // one candidate per lane per round: the warp runs as many rounds as
+                // its busiest lane has candidates (one or two once the lists fill)
+                while (__any_sync(0xffffffffu, cand != 0u)) {
+                    if (cand) {
+                        const int j = __ffs(cand) - 1;
+                        cand &= cand - 1u;
+                        const float x = select32(v, j);
+                        if (x < bd[TC_TOPT - 1]) insert_sorted(bd, bi, x, col0 + j);
+                    }
                 }
             } else {
                 unsigned pass = 0;
@@ -250,6 +331,14 @@ __global__ void __launch_bounds__(TC_NT, 1)
             }
         }
         if (MODE == GEMM_FILTER && valid) g.cnt[(qg * gridDim.y + blockIdx.y) * 2 + half] = n;
+        if (MODE == GEMM_TOPK && valid) {
+            const long long o = ((qg * gridDim.y + blockIdx.y) * 2 + half) * (long long)TC_TOPT;
+#pragma unroll
+            for (int t = 0; t < TC_TOPT; ++t) {
+                g.list_k[o + t] = bi[t] >= 0 ? f2key(qnr + bd[t]) : 0xffffffffu;
+                g.list_i[o + t] = bi[t];
+            }
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -257,13 +346,36 @@ __global__ void __launch_bounds__(TC_NT, 1)
     if (tid == 0 && s_fail) atomicExch(g.err, 1);
 }
 
+// Exact squared distance in the oracle's order: one fmaf per dimension, t = 0..dim-1.
+// Rows of 4-float alignment load eight float4 ahead of their fmafs, so one
+// lane keeps eight loads in flight instead of waiting on each.
 __device__ __forceinline__ float l2_seq_dev(const float* __restrict__ a_smem, const float* __restrict__ b, int dim) {
     float d = 0.0f;
     if ((dim & 3) == 0) {
         const float4* b4 = reinterpret_cast<const float4*>(b);
-        for (int t = 0; t < dim / 4; ++t) {
+        const float4* q4 = reinterpret_cast<const float4*>(a_smem);
+        const int n4 = dim >> 2;
+        int t = 0;
+        for (; t + 8 <= n4; t += 8) {
+            float4 x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = __ldg(b4 + t + u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float4 q = q4[t + u];
+                float df = q.x - x[u].x;
+                d = fmaf(df, df, d);
+                df = q.y - x[u].y;
+                d = fmaf(df, df, d);
+                df = q.z - x[u].z;
+                d = fmaf(df, df, d);
+                df = q.w - x[u].w;
+                d = fmaf(df, df, d);
+            }
+        }
+        for (; t < n4; ++t) {
             const float4 x = __ldg(b4 + t);
-            const float4 q = *reinterpret_cast<const float4*>(a_smem + 4 * t);
+            const float4 q = q4[t];
             float df = q.x - x.x;
             d = fmaf(df, df, d);
             df = q.y - x.y;
@@ -280,6 +392,19 @@ __device__ __forceinline__ float l2_seq_dev(const float* __restrict__ a_smem, co
         }
     }
     return d;
+}
+
+// The bound E on |d~ - d| for one query: split-bf16 products, fp32
+// accumulation and the norms' rounding.
+__device__ __forceinline__ float approx_err(float qq, float cc) {
+    return 0x1p-12f * sqrtf(qq) * sqrtf(cc) + 0x1p-16f * (qq + cc);
+}
+
+// Candidates whose approximate distance exceeds the P-th smallest
+// approximate distance dPa by more than 2E cannot be in the exact top P: P
+// others are nearer by more than zero.  The slack covers rounding of thr.
+__device__ __forceinline__ float rescore_limit(float dPa, float E) {
+    return dPa + 2.0f * E + fabsf(dPa) * 0x1p-20f;
 }
 
 constexpr int FIN_WARPS = 4;      // queries per finish CTA (one warp each)
@@ -356,22 +481,141 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
         int n_less;
         warp_radix_select(wk, total, S, hist, kth, n_less);
         warp_collect_smallest(wk, total, S, kth, n_less, sx, [&](int i) { return wi[i]; });
+        for (int i = S + lane; i < L.spow; i += 32) sx[i] = ~0ull;
+        __syncwarp();
+        warp_bitonic_sort(sx, L.spow);  // by approximate key
+        const float E = approx_err(qn[q], __uint_as_float(*max_cn_bits));
+        const float thr = rescore_limit(key2f((uint32_t)(sx[P - 1] >> 32)), E);
+        // rescore exactly the sorted prefix within thr
+        int r = 0;
         for (int i = lane; i < L.spow; i += 32) {
+            const unsigned long long e = sx[i];
             unsigned long long key = ~0ull;
-            if (i < S) {
-                const uint32_t cid = (uint32_t)(sx[i] & 0xffffffffu);
+            const bool take = i < S && key2f((uint32_t)(e >> 32)) <= thr;
+            if (take) {
+                const uint32_t cid = (uint32_t)(e & 0xffffffffu);
+                key = ((unsigned long long)f2key(l2_seq_dev(sq, centroids + (size_t)cid * dim, dim)) << 32) | cid;
+            }
+            r += __popc(__ballot_sync(0xffffffffu, take));
+            ex[i] = key;
+        }
+        __syncwarp();
+        warp_bitonic_sort(ex, next_pow2(r > P ? r : P));
+        const float dp = key2f((uint32_t)(ex[P - 1] >> 32));
+        const float T = key2f(kth);
+        certified = (S >= nlist) || (dp < T - E);
+    }
+    if (!certified) {
+        uint32_t* rk = fb + ((size_t)blockIdx.x * FIN_WARPS + w) * nlist;
+        for (int c = lane; c < nlist; c += 32) rk[c] = f2key(l2_seq_dev(sq, centroids + (size_t)c * dim, dim));
+        __syncwarp();
+        uint32_t kth;
+        int n_less;
+        warp_radix_select(rk, nlist, P, hist, kth, n_less);
+        warp_collect_smallest(rk, nlist, P, kth, n_less, ex, [](int i) { return i; });
+        const int ppow = next_pow2(P);
+        for (int i = P + lane; i < ppow; i += 32) ex[i] = ~0ull;
+        __syncwarp();
+        warp_bitonic_sort(ex, ppow);
+        if (lane == 0) atomicAdd(n_fallback, 1);
+    }
+    for (int j = lane; j < P; j += 32) {
+        const unsigned long long e = ex[j];
+        out_ids[(size_t)q * P + j] = (uint32_t)(e & 0xffffffffu);
+        out_d[(size_t)q * P + j] = key2f((uint32_t)(e >> 32));
+    }
+}
+
+// Warp per query, single-pass path: the TC_TOPT smallest d~ of every (column
+// run, half) list are rescored exactly and sorted by (distance, id).  Every
+// centroid outside a full list has d~ >= that list's largest kept d~, so with
+// B = the smallest such value over the full lists, the first P are the exact
+// top-P when their P-th distance is below B - E.  Otherwise every centroid is
+// rescored through the warp's scratch row.
+__global__ void __launch_bounds__(FIN_WARPS * 32) coarse_topk_finish_kernel(
+    const float* __restrict__ centroids, int nlist, int dim, const float* __restrict__ queries, int nq, int nlists,
+    const uint32_t* __restrict__ list_k, const int32_t* __restrict__ list_i, int P, const float* __restrict__ qn,
+    const unsigned* __restrict__ max_cn_bits, const int* __restrict__ err, uint32_t* __restrict__ fb,
+    uint32_t* __restrict__ out_ids, float* __restrict__ out_d, int* __restrict__ n_fallback) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * FIN_WARPS + w;
+    if (q >= nq) return;
+    const int ncand = nlists * TC_TOPT;
+    const int cpow = next_pow2(ncand);
+    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(P)};
+    // per warp: query, histogram (fallback select), candidate keys [cpow]
+    unsigned char* mine = smem + (size_t)w * ((size_t)L.dim4 * 4 + 256 * 4 + (size_t)cpow * 8);
+    float* sq = reinterpret_cast<float*>(mine);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(mine + L.dim4 * 4);
+    unsigned long long* ex = reinterpret_cast<unsigned long long*>(hist + 256);
+    for (int t = lane; t < dim; t += 32) sq[t] = queries[(size_t)q * dim + t];
+    __syncwarp();
+    // B: the smallest largest-kept d~ over the full lists (an unfilled list holds
+    // every centroid of its columns)
+    float B = INFINITY;
+    for (int l = lane; l < nlists; l += 32) {
+        const size_t o = ((size_t)q * nlists + l) * TC_TOPT + (TC_TOPT - 1);
+        if (list_i[o] >= 0) B = fminf(B, key2f(list_k[o]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) B = fminf(B, __shfl_xor_sync(0xffffffffu, B, o));
+    // (approximate key, centroid) of every kept candidate
+    for (int i = lane; i < cpow; i += 32) {
+        unsigned long long e = ~0ull;
+        if (i < ncand) {
+            const size_t o = (size_t)q * ncand + i;
+            const int32_t cid = list_i[o];
+            if (cid >= 0 && cid < nlist) e = ((unsigned long long)list_k[o] << 32) | (uint32_t)cid;
+        }
+        ex[i] = e;
+    }
+    __syncwarp();
+    // the P-th smallest by P rounds of a warp minimum
+    unsigned long long kp = 0ull;
+    for (int p = 0; p < P; ++p) {
+        unsigned long long mn = ~0ull;
+        for (int i = lane; i < ncand; i += 32) {
+            const unsigned long long e = ex[i];
+            if ((p == 0 || e > kp) && e < mn) mn = e;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long x = __shfl_xor_sync(0xffffffffu, mn, o);
+            mn = x < mn ? x : mn;
+        }
+        kp = mn;
+    }
+    bool certified = false;
+    if (*err == 0 && kp != ~0ull) {
+        const float E = approx_err(qn[q], __uint_as_float(*max_cn_bits));
+        const float thr = rescore_limit(key2f((uint32_t)(kp >> 32)), E);
+        // compact the candidates within thr to the front, in place: a chunk's
+        // entries are all read (ballot) before any lane writes, and writes
+        // land at or below the chunk being read
+        int r = 0;
+        for (int c0 = 0; c0 < ncand; c0 += 32) {
+            const int i = c0 + lane;
+            const unsigned long long e = i < ncand ? ex[i] : ~0ull;
+            const bool take = e != ~0ull && key2f((uint32_t)(e >> 32)) <= thr;
+            const unsigned b = __ballot_sync(0xffffffffu, take);
+            if (take) ex[r + __popc(b & lanemask_lt())] = e;
+            r += __popc(b);
+            __syncwarp();
+        }
+        const int rpow = next_pow2(r > P ? r : P);
+        for (int i = lane; i < rpow; i += 32) {
+            unsigned long long key = ~0ull;
+            if (i < r) {
+                const uint32_t cid = (uint32_t)(ex[i] & 0xffffffffu);
                 key = ((unsigned long long)f2key(l2_seq_dev(sq, centroids + (size_t)cid * dim, dim)) << 32) | cid;
             }
             ex[i] = key;
         }
         __syncwarp();
-        warp_bitonic_sort(ex, L.spow);
+        warp_bitonic_sort(ex, rpow);
         const float dp = key2f((uint32_t)(ex[P - 1] >> 32));
-        const float T = key2f(kth);
-        const float qq = qn[q];
-        const float cc = __uint_as_float(*max_cn_bits);
-        const float E = 0x1p-12f * sqrtf(qq) * sqrtf(cc) + 0x1p-16f * (qq + cc);
-        certified = (S >= nlist) || (dp < T - E);
+        certified = (B == INFINITY) || (dp < B - E);
     }
     if (!certified) {
         uint32_t* rk = fb + ((size_t)blockIdx.x * FIN_WARPS + w) * nlist;
@@ -442,11 +686,26 @@ struct CoarsePlan {
     int fin_cta;
 };
 
-// column runs so that the grid covers the SMs at least once
+// Column runs per query tile.  One CTA fills an SM (its shared memory holds the
+// whole query tile and two centroid stages), so the grid runs in waves of 148
+// CTAs; the split minimises waves x (tiles per CTA + a fixed per-CTA cost of
+// about two tiles for the query-tile load and the pipeline fill).
 void col_split(int mtiles, int ntiles, int& gy, int& tpc) {
-    const int want = std::max(1, std::min(ntiles, (148 + mtiles - 1) / mtiles));
-    tpc = (ntiles + want - 1) / want;
-    gy = (ntiles + tpc - 1) / tpc;
+    constexpr int kSMs = 148, kCtaCost = 2;
+    long long best = -1;
+    gy = 1;
+    tpc = ntiles;
+    for (int want = 1; want <= std::min(ntiles, 1024); ++want) {
+        const int t = (ntiles + want - 1) / want;
+        const int runs = (ntiles + t - 1) / t;
+        const long long waves = ((long long)mtiles * runs + kSMs - 1) / kSMs;
+        const long long cost = waves * (t + kCtaCost);
+        if (best < 0 || cost < best) {
+            best = cost;
+            gy = runs;
+            tpc = t;
+        }
+    }
 }
 
 CoarsePlan coarse_plan(long long nq, int nlist, int P) {
@@ -525,6 +784,39 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      smem));
     const int mtiles = (int)((nq + TC_M - 1) / TC_M);
+
+    const int topk_fsm = FIN_WARPS * ((dim + 3) / 4 * 4 * 4 + 256 * 4 + next_pow2(c.gy1 * 2 * TC_TOPT) * 8);
+    if (P <= TC_TOPK_MAXP && topk_fsm <= 227 * 1024) {
+        // single pass: each (query, column run, half) keeps its TC_TOPT smallest
+        // d~ in registers; a warp per query rescores and certifies them
+        FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem));
+        GemmArgs g{};
+        g.kt = kt;
+        g.q0 = 0;
+        g.nq = (int)nq;
+        g.qn = qn;
+        g.cn = cn;
+        g.err = err;
+        g.ncols = nlist;
+        g.tiles_per_cta = c.tpc1;
+        g.list_k = lk;
+        g.list_i = li;
+        coarse_gemm_kernel<GEMM_TOPK><<<dim3(mtiles, c.gy1), TC_NT, smem, s>>>(ta, tb, g);
+        if ((rc = check_launch("coarse_gemm_kernel(top-k)"))) return rc;
+        const int nlists = c.gy1 * 2;
+        const int fsm = topk_fsm;
+        FG_CUDA_TRY(cudaFuncSetAttribute(coarse_topk_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fsm));
+        coarse_topk_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fsm, s>>>(centroids, nlist, dim, queries, (int)nq,
+                                                                        nlists, lk, li, P, qn, maxc, err, fb,
+                                                                        out_ids, out_d, nfb);
+        if ((rc = check_launch("coarse_topk_finish_kernel"))) return rc;
+        if (n_fallback_host) {
+            FG_CUDA_TRY(cudaMemcpyAsync(n_fallback_host, nfb, sizeof(int), cudaMemcpyDeviceToHost, s));
+            FG_CUDA_TRY(cudaStreamSynchronize(s));
+        }
+        return FG_OK;
+    }
 
     // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
     GemmArgs g{};

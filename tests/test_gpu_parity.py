@@ -85,7 +85,7 @@ def test_coarse_matches_oracle(fg, kind):
 @pytest.mark.parametrize("path", ["tc", "simt"])
 def test_coarse_paths_match_oracle(fg, kind, path):
     index, base, q = dataset(kind)
-    for top_m in (1, 16, 77, 128):
+    for top_m in (1, 2, 3, 4, 5, 16, 77, 128):
         r = fg.coarse_search(q, index["centroids"], top_m, path=path)
         eids, ed = oracle.coarse(index["centroids"], q, top_m)
         np.testing.assert_array_equal(_np(r[1]), ed)
@@ -104,11 +104,12 @@ def test_coarse_tc_fallback_on_ties(fg):
         cen[i, rng.choice(32, 3, replace=False)] = 1.0
     q = rng.integers(0, 2, size=(64, 32)).astype(np.float32)
     q[::2] = 0.0
-    ids, d, nfb = fg.coarse_search(q, cen, 20, path="tc")
-    eids, ed = oracle.coarse(cen, q, 20)
-    np.testing.assert_array_equal(_np(d), ed)
-    np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
-    assert nfb >= 32
+    for top_m in (20, 3, 1):  # the multi-pass path and the single-pass top-8 path
+        ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
+        eids, ed = oracle.coarse(cen, q, top_m)
+        np.testing.assert_array_equal(_np(d), ed)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+        assert nfb >= 32
 
 
 def test_coarse_tc_odd_shapes(fg):
@@ -116,7 +117,7 @@ def test_coarse_tc_odd_shapes(fg):
     rng = np.random.default_rng(11)
     cen = rng.normal(size=(1001, 40)).astype(np.float32)
     q = rng.normal(size=(333, 40)).astype(np.float32)
-    for top_m in (1, 7, 64):
+    for top_m in (1, 2, 4, 7, 64):
         ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
         eids, ed = oracle.coarse(cen, q, top_m)
         np.testing.assert_array_equal(_np(d), ed)
@@ -128,10 +129,11 @@ def test_coarse_tc_many_lists_two_stage(fg):
     rng = np.random.default_rng(10)
     cen = rng.normal(size=(20000, 64)).astype(np.float32)
     q = rng.normal(size=(200, 64)).astype(np.float32)
-    ids, d, nfb = fg.coarse_search(q, cen, 64, path="tc")
-    eids, ed = oracle.coarse(cen, q, 64)
-    np.testing.assert_array_equal(_np(d), ed)
-    np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+    for top_m in (64, 4):
+        ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
+        eids, ed = oracle.coarse(cen, q, top_m)
+        np.testing.assert_array_equal(_np(d), ed)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
 
 
 @pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
