@@ -36,8 +36,11 @@ constexpr int TC_N = 64;        // centroids per tile (UMMA N)
 constexpr int TC_TILE = 128;    // row padding of both operands
 constexpr int TC_KB = 64;       // bf16 elements per K block (one 128-byte swizzle row)
 constexpr int TC_MAX_KB = 6;    // A resident + 2 B stages: 6*16 KB + 2*6*8 KB = 192 KB
-constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, each half of a tile's columns
+constexpr int TC_PARTS = 4;              // column parts of a tile: one epilogue warp per (lane quarter, part)
+constexpr int TC_CPW = TC_N / TC_PARTS;  // 16 columns of each tile per epilogue thread
+constexpr int TC_EPI_WARPS = 4 * TC_PARTS;
 constexpr int TC_NT = 64 + TC_EPI_WARPS * 32;
+constexpr int TC_MAX_TPC = 64;           // tiles per CTA; bounds the staged column norms (16 KB)
 constexpr int RS_NT = 256;
 
 __host__ __device__ inline int tc_kpad(int dim) { return (3 * dim + TC_KB - 1) / TC_KB * TC_KB; }
@@ -70,65 +73,48 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, long long n, int 
     }
 }
 
-// Warp roles of the persistent GEMM CTA (320 threads):
+// Warp roles of the persistent GEMM CTA (576 threads):
 //   warp 0, lane 0: TMA producer (A once, then B tiles through a 2-stage ring)
 //   warp 1, lane 0: MMA issuer (and warp 1 owns the TMEM allocation)
-//   warps 2..9:     epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (its 32
-//                   queries) and columns 32*((w-2)/4) .. +31 of each tile
+//   warps 2..17:    epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (its 32
+//                   queries) and columns 16*((w-2)/4) .. +15 of each tile
 // TMEM holds two 128 x 64 fp32 accumulators, so the epilogue of tile i runs
-// while the MMAs of tile i+1 fill the other one.
+// while the MMAs of tile i+1 fill the other one.  Four epilogue warps per SM
+// sub-partition hide one another's latency; the norms of the CTA's columns
+// are staged in shared memory once.
 struct GemmArgs {
     int kt;              // 64-wide K blocks
     long long q0;        // first query row of this launch (row of the A tensor map)
     int nq;              // query rows of this launch
     int ncols;           // centroid columns [0, ncols)
-    int tiles_per_cta;   // 64-column tiles per CTA (blockIdx.y picks the run)
+    int tiles_per_cta;   // 64-column tiles per CTA (blockIdx.y picks the run), <= TC_MAX_TPC
     const float* qn;     // |q|^2, indexed by q0 + row
     const float* cn;     // |c|^2
     uint32_t* out;       // GEMM_MATRIX: order key of d~ at out[row * ldo + col]
     long long ldo;
     const float* tq;     // GEMM_FILTER: per-query bound
-    int cap;             // GEMM_FILTER: capacity of each (query, CTA column run) segment
-    int* cnt;            // GEMM_FILTER: [nq][gridDim.y * 2] appended counts (may exceed cap)
-    uint32_t* list_k;    // [nq][gridDim.y * 2][cap] keys of d~ (one segment per column half)
-    int32_t* list_i;     // [nq][gridDim.y * 2][cap] centroid ids
+    int cap;             // GEMM_FILTER: capacity of each (query, column run, part) segment
+    int* cnt;            // GEMM_FILTER: [nq][gridDim.y * TC_PARTS] appended counts (may exceed cap)
+    uint32_t* list_k;    // [nq][gridDim.y * TC_PARTS][cap or TC_TOPT] keys of d~
+    int32_t* list_i;     // same shape: centroid ids
     int* err;
 };
 
 enum { GEMM_MATRIX = 0, GEMM_FILTER = 1, GEMM_TOPK = 2 };
-constexpr int TC_TOPT = 8;      // GEMM_TOPK: approximate candidates kept per (query, column run, half)
+constexpr int TC_TOPT = 8;      // GEMM_TOPK: approximate candidates kept per (query, column run, part)
 constexpr int TC_TOPK_MAXP = 4;  // top_m up to which the single-pass GEMM_TOPK path runs
 
-// Norms of the 32 columns col0.. (0 past ncols).
-__device__ __forceinline__ void load_norms(const float* __restrict__ cn, int col0, int ncols, float (&c)[32]) {
-    if (col0 + 32 <= ncols) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            const float4 c4 = __ldg(reinterpret_cast<const float4*>(cn + col0 + j));
-            c[j] = c4.x;
-            c[j + 1] = c4.y;
-            c[j + 2] = c4.z;
-            c[j + 3] = c4.w;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) c[j] = (col0 + j < ncols) ? __ldg(cn + col0 + j) : 0.0f;
-    }
-}
-
-// v[j] for a lane-varying j by a five-level select tree: every index is
+// v[j] for a lane-varying j by a four-level select tree: every index is
 // static, so v stays in registers.
-__device__ __forceinline__ float select32(const float (&v)[32], int j) {
-    float a[16], b[8], c[4], d[2];
+__device__ __forceinline__ float select16(const float (&v)[16], int j) {
+    float a[8], b[4], c[2];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) a[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
+    for (int t = 0; t < 8; ++t) a[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) b[t] = (j & 2) ? a[2 * t + 1] : a[2 * t];
+    for (int t = 0; t < 4; ++t) b[t] = (j & 2) ? a[2 * t + 1] : a[2 * t];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) c[t] = (j & 4) ? b[2 * t + 1] : b[2 * t];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) d[t] = (j & 8) ? c[2 * t + 1] : c[2 * t];
-    return (j & 16) ? d[1] : d[0];
+    for (int t = 0; t < 2; ++t) c[t] = (j & 4) ? b[2 * t + 1] : b[2 * t];
+    return (j & 8) ? c[1] : c[0];
 }
 
 // Insert x into the ascending list bd (x < bd[T-1]); equal keys keep their
@@ -146,6 +132,30 @@ __device__ __forceinline__ void insert_sorted(float (&bd)[T], int32_t (&bi)[T], 
     }
     bd[0] = lt[0] ? x : bd[0];
     bi[0] = lt[0] ? xi : bi[0];
+}
+
+// Ascending bitonic sorting network over 16 (value, column) pairs in registers.
+__device__ __forceinline__ void sort16(float (&v)[16], int32_t (&id)[16]) {
+#pragma unroll
+    for (int k = 2; k <= 16; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const bool up = (i & k) == 0;
+                    const bool sw = up ? (v[i] > v[l]) : (v[i] < v[l]);
+                    const float a = v[i], b = v[l];
+                    const int32_t ia = id[i], ib = id[l];
+                    v[i] = sw ? b : a;
+                    v[l] = sw ? a : b;
+                    id[i] = sw ? ib : ia;
+                    id[l] = sw ? ia : ib;
+                }
+            }
+        }
+    }
 }
 
 template <int MODE>
@@ -168,6 +178,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
     unsigned char* sa = base;
     unsigned char* sb = base + g.kt * A_KB;
     const int stage_bytes = g.kt * B_KB;
+    float* sn = reinterpret_cast<float*>(sb + 2 * stage_bytes);  // [nt * TC_N] column norms
     const int m0 = blockIdx.x * TC_M;
 
     if (tid == 0) {
@@ -225,18 +236,27 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 tc::umma_commit(&acc_full[acc]);  // and the accumulator is ready for the epilogue
             }
         }
-    } else {  // ---- epilogue warps 2..9
+    } else {  // ---- epilogue warps 2..17
+        {
+            const int c0 = tile0 * TC_N, ncn = nt * TC_N;
+            for (int t = tid - 64; t < ncn; t += TC_EPI_WARPS * 32)
+                sn[t] = (c0 + t < g.ncols) ? __ldg(g.cn + c0 + t) : 0.0f;
+            tc::named_bar_sync(1, TC_EPI_WARPS * 32);
+        }
         const int q4 = warp & 3;
-        const int half = (warp - 2) >> 2;  // which 32 columns of each tile
+        const int part = (warp - 2) >> 2;  // which 16 columns of each tile
         const int row = m0 + q4 * 32 + lane;
         const bool valid = row < g.nq;
         const long long qg = g.q0 + row;
         const float qnr = valid ? g.qn[qg] : 0.0f;
         const float bound = (MODE == GEMM_FILTER && valid) ? g.tq[qg] : 0.0f;
-        // each (query, column half) belongs to exactly one thread: its segment needs no atomics
-        const long long seg = ((qg * gridDim.y + blockIdx.y) * 2 + half) * (long long)g.cap;
+        // each (query, column run, part) belongs to exactly one thread: its segment needs no atomics
+        const long long lidx = (qg * gridDim.y + blockIdx.y) * TC_PARTS + part;
+        const long long seg = lidx * (long long)g.cap;
         int n = 0;
-        // GEMM_TOPK: the TC_TOPT smallest d~ of this thread's columns, ascending
+        // GEMM_TOPK: the TC_TOPT smallest u = cn - 2 dp of this thread's columns,
+        // ascending.  u orders the columns as d~ = qn + u does (qn is constant
+        // per thread and adding it is monotone); qn is added when written out.
         float bd[TC_TOPT];
         int32_t bi[TC_TOPT];
 #pragma unroll
@@ -244,31 +264,35 @@ __global__ void __launch_bounds__(TC_NT, 1)
             bd[t] = INFINITY;
             bi[t] = -1;
         }
-        // column norms of the next chunk are loaded one tile ahead, so their
-        // latency hides behind the accumulator wait instead of following it
-        float cnext[32];
-        load_norms(g.cn, tile0 * TC_N + half * 32, g.ncols, cnext);
         for (int i = 0; i < nt; ++i) {
             const int acc = i & 1, ph = (i >> 1) & 1;
-            float c[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) c[j] = cnext[j];
-            const int col0 = (tile0 + i) * TC_N + half * 32;
-            if (i + 1 < nt) load_norms(g.cn, col0 + TC_N, g.ncols, cnext);
             if (!__all_sync(0xffffffffu, tc::mbar_wait_or_fail(&acc_full[acc], ph, fail))) break;
             tc::fence_after_sync();
-            float v[32];
-            tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + half * 32), v);
+            float v[TC_CPW];
+            tc::tmem_ld_32x16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + part * TC_CPW), v);
             tc::fence_before_sync();
             tc::mbar_arrive(&acc_empty[acc]);
             // GEMM_TOPK keeps every lane in the loop: its candidate rounds are warp-collective
             if (!valid && MODE != GEMM_TOPK) continue;
-            const int ncol = min(32, g.ncols - col0);
+            const int col0 = (tile0 + i) * TC_N + part * TC_CPW;
+            const int ncol = min(TC_CPW, g.ncols - col0);
+            float c[TC_CPW];
+            {
+                const float4* s4 = reinterpret_cast<const float4*>(sn + i * TC_N + part * TC_CPW);
+#pragma unroll
+                for (int j = 0; j < TC_CPW / 4; ++j) {
+                    const float4 x = s4[j];
+                    c[4 * j] = x.x;
+                    c[4 * j + 1] = x.y;
+                    c[4 * j + 2] = x.z;
+                    c[4 * j + 3] = x.w;
+                }
+            }
             if (MODE == GEMM_MATRIX) {
                 uint32_t* o = g.out + (long long)row * g.ldo + col0;
-                if (ncol == 32 && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
+                if (ncol == TC_CPW && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
+                    for (int j = 0; j < TC_CPW; j += 4) {
                         uint4 k4;
                         k4.x = f2key(qnr + c[j] - 2.0f * v[j]);
                         k4.y = f2key(qnr + c[j + 1] - 2.0f * v[j + 1]);
@@ -278,26 +302,36 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < TC_CPW; ++j)
                         if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
                 }
             } else if (MODE == GEMM_TOPK) {
-                // u = cn - 2 dp orders this thread's columns as d~ = qn + u does
-                // (qn is constant per thread, and adding it is monotone); the
-                // list keeps u and adds qn once, when it is written out
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
-                float m[16];
+                for (int j = 0; j < TC_CPW; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
+                if (i == 0) {
+                    // the first chunk fills the list through a sorting network
+                    int32_t id[TC_CPW];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) m[j] = fminf(v[2 * j], v[2 * j + 1]);
+                    for (int j = 0; j < TC_CPW; ++j) id[j] = col0 + j;
+                    sort16(v, id);
 #pragma unroll
-                for (int w = 8; w; w >>= 1)
+                    for (int t = 0; t < TC_TOPT; ++t) {
+                        bd[t] = v[t];
+                        bi[t] = v[t] < INFINITY ? id[t] : -1;
+                    }
+                    continue;
+                }
+                float m[TC_CPW / 2];
+#pragma unroll
+                for (int j = 0; j < TC_CPW / 2; ++j) m[j] = fminf(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+                for (int w = TC_CPW / 4; w; w >>= 1)
 #pragma unroll
                     for (int j = 0; j < w; ++j) m[j] = fminf(m[j], m[j + w]);
                 unsigned cand = 0;
                 if (valid && m[0] < bd[TC_TOPT - 1]) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) cand |= (v[j] < bd[TC_TOPT - 1]) ? (1u << j) : 0u;
+                    for (int j = 0; j < TC_CPW; ++j) cand |= (v[j] < bd[TC_TOPT - 1]) ? (1u << j) : 0u;
                 }
                 // one candidate per lane per round: the warp runs as many rounds as
                 // its busiest lane has candidates (one or two once the lists fill)
@@ -305,20 +339,20 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     if (cand) {
                         const int j = __ffs(cand) - 1;
                         cand &= cand - 1u;
-                        const float x = select32(v, j);
+                        const float x = select16(v, j);
                         if (x < bd[TC_TOPT - 1]) insert_sorted(bd, bi, x, col0 + j);
                     }
                 }
             } else {
                 unsigned pass = 0;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < TC_CPW; ++j) {
                     v[j] = qnr + c[j] - 2.0f * v[j];
                     pass |= (j < ncol && v[j] <= bound) ? (1u << j) : 0u;
                 }
                 if (pass) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < TC_CPW; ++j) {
                         if (pass & (1u << j)) {
                             if (n < g.cap) {
                                 g.list_k[seg + n] = f2key(v[j]);
@@ -330,9 +364,9 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 }
             }
         }
-        if (MODE == GEMM_FILTER && valid) g.cnt[(qg * gridDim.y + blockIdx.y) * 2 + half] = n;
+        if (MODE == GEMM_FILTER && valid) g.cnt[lidx] = n;
         if (MODE == GEMM_TOPK && valid) {
-            const long long o = ((qg * gridDim.y + blockIdx.y) * 2 + half) * (long long)TC_TOPT;
+            const long long o = lidx * (long long)TC_TOPT;
 #pragma unroll
             for (int t = 0; t < TC_TOPT; ++t) {
                 g.list_k[o + t] = bi[t] >= 0 ? f2key(qnr + bd[t]) : 0xffffffffu;
@@ -693,9 +727,9 @@ struct CoarsePlan {
 void col_split(int mtiles, int ntiles, int& gy, int& tpc) {
     constexpr int kSMs = 148, kCtaCost = 2;
     long long best = -1;
-    gy = 1;
-    tpc = ntiles;
-    for (int want = 1; want <= std::min(ntiles, 1024); ++want) {
+    gy = (ntiles + TC_MAX_TPC - 1) / TC_MAX_TPC;
+    tpc = (ntiles + gy - 1) / gy;
+    for (int want = (ntiles + TC_MAX_TPC - 1) / TC_MAX_TPC; want <= std::min(ntiles, 1024); ++want) {
         const int t = (ntiles + want - 1) / want;
         const int runs = (ntiles + t - 1) / t;
         const long long waves = ((long long)mtiles * runs + kSMs - 1) / kSMs;
@@ -718,7 +752,7 @@ CoarsePlan coarse_plan(long long nq, int nlist, int P) {
     const int mtiles = (int)((std::max(nq, 1ll) + TC_M - 1) / TC_M);
     col_split(mtiles, (nlist + TC_N - 1) / TC_N, c.gy1, c.tpc1);
     c.cap = (int)std::min<long long>(FIN_TOT, std::max<long long>(4 * expect, c.S + 256));
-    c.cap = std::min(c.cap, c.tpc1 * TC_N / 2);
+    c.cap = std::min(c.cap, c.tpc1 * TC_CPW);
     c.fin_cta = (int)((std::max(nq, 1ll) + FIN_WARPS - 1) / FIN_WARPS);
     return c;
 }
@@ -731,8 +765,8 @@ size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P) {
     b += round_up(round_up((size_t)nq, TC_TILE) * kpad * 2, 256) + round_up(round_up((size_t)nlist, TC_TILE) * kpad * 2, 256);
     b += round_up((size_t)nq * 4, 256) * 2 + round_up((size_t)nlist * 4, 256) + 256 * 3;
     b += round_up((size_t)nq * round_up(c.NS, 4) * 4, 256);     // prefix keys
-    b += round_up((size_t)nq * c.gy1 * 2 * 4, 256);             // segment counts
-    b += round_up((size_t)nq * c.gy1 * 2 * c.cap * 4, 256) * 2; // segments
+    b += round_up((size_t)nq * c.gy1 * TC_PARTS * 4, 256);             // segment counts
+    b += round_up((size_t)nq * c.gy1 * TC_PARTS * c.cap * 4, 256) * 2; // segments
     b += round_up((size_t)c.fin_cta * FIN_WARPS * nlist * 4, 256);  // fallback rows
     return b + 4096;
 }
@@ -758,9 +792,9 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     int* nfb = cv.take<int>(4);
     const long long ldm = (long long)round_up((size_t)c.NS, 4);
     uint32_t* M0 = cv.take<uint32_t>((size_t)nq * ldm);
-    int* cnt = cv.take<int>((size_t)nq * c.gy1 * 2);
-    uint32_t* lk = cv.take<uint32_t>((size_t)nq * c.gy1 * 2 * c.cap);
-    int32_t* li = cv.take<int32_t>((size_t)nq * c.gy1 * 2 * c.cap);
+    int* cnt = cv.take<int>((size_t)nq * c.gy1 * TC_PARTS);
+    uint32_t* lk = cv.take<uint32_t>((size_t)nq * c.gy1 * TC_PARTS * c.cap);
+    int32_t* li = cv.take<int32_t>((size_t)nq * c.gy1 * TC_PARTS * c.cap);
     uint32_t* fb = cv.take<uint32_t>((size_t)c.fin_cta * FIN_WARPS * nlist);
     if (!cv.ok()) return fail(FG_ERR_WORKSPACE, "coarse workspace too small (%zu < %zu)", ws_bytes,
                               coarse_tc_workspace(nq, nlist, dim, P));
@@ -778,14 +812,14 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     CUtensorMap ta, tb;
     if ((rc = make_map(&ta, A, nq_pad, kpad, TC_M))) return rc;
     if ((rc = make_map(&tb, B, nl_pad, kpad, TC_N))) return rc;
-    const int smem = 1024 + kt * TC_M * TC_KB * 2 + 2 * kt * TC_N * TC_KB * 2;
+    const int smem = 1024 + kt * TC_M * TC_KB * 2 + 2 * kt * TC_N * TC_KB * 2 + TC_MAX_TPC * TC_N * 4;
     FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_MATRIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      smem));
     FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      smem));
     const int mtiles = (int)((nq + TC_M - 1) / TC_M);
 
-    const int topk_fsm = FIN_WARPS * ((dim + 3) / 4 * 4 * 4 + 256 * 4 + next_pow2(c.gy1 * 2 * TC_TOPT) * 8);
+    const int topk_fsm = FIN_WARPS * ((dim + 3) / 4 * 4 * 4 + 256 * 4 + next_pow2(c.gy1 * TC_PARTS * TC_TOPT) * 8);
     if (P <= TC_TOPK_MAXP && topk_fsm <= 227 * 1024) {
         // single pass: each (query, column run, half) keeps its TC_TOPT smallest
         // d~ in registers; a warp per query rescores and certifies them
@@ -804,7 +838,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
         g.list_i = li;
         coarse_gemm_kernel<GEMM_TOPK><<<dim3(mtiles, c.gy1), TC_NT, smem, s>>>(ta, tb, g);
         if ((rc = check_launch("coarse_gemm_kernel(top-k)"))) return rc;
-        const int nlists = c.gy1 * 2;
+        const int nlists = c.gy1 * TC_PARTS;
         const int fsm = topk_fsm;
         FG_CUDA_TRY(cudaFuncSetAttribute(coarse_topk_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fsm));
         coarse_topk_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fsm, s>>>(centroids, nlist, dim, queries, (int)nq,
@@ -854,7 +888,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     const int fin_smem = FIN_WARPS * FL.per_warp_bytes();
     FG_CUDA_TRY(cudaFuncSetAttribute(coarse_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem));
     coarse_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fin_smem, s>>>(centroids, nlist, dim, queries, (int)nq, cnt,
-                                                                     c.gy1 * 2, lk, li, c.cap, c.S, P, qn, maxc, err, fb,
+                                                                     c.gy1 * TC_PARTS, lk, li, c.cap, c.S, P, qn, maxc, err, fb,
                                                                      out_ids, out_d, nfb);
     if ((rc = check_launch("coarse_finish_kernel"))) return rc;
     if (n_fallback_host) {

@@ -10,8 +10,15 @@
 // new top-k ids were absent from the previous top-k, the stable counter
 // grows, otherwise it resets; at `beta` the query is finished.
 //
+// The candidate rows of a mini-batch are first copied into shared memory by
+// the whole CTA (coalesced 16-byte loads, all in flight together); each
+// distance chain then runs from shared memory.  The counter is not evaluated
+// on the last mini-batch, where it cannot change the result.
+//
 // ref_compat reproduces the reference's 128-thread block sort, which only
 // sees the first 128 entries of the k + mini_batch window (gpu_global.cu:644-650).
+#include <algorithm>
+
 #include "fg_common.cuh"
 
 namespace fg {
@@ -27,40 +34,59 @@ struct RerankArgs {
     const void* base;  // [nbase][dim] float or uint8
     long long nbase;
     int k, mb, nw;
+    int rch;  // candidate rows staged in shared memory at a time
     float eps;
     int beta;
     int32_t* out_ids;
     float* out_dists;
 };
 
-// Exact squared L2 in dimension order (fmaf, as nvcc contracts the reference's
-// `local_d += diff*diff`), eight 16-byte loads in flight.
-__device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const float* __restrict__ v, int dim) {
+// Shared-memory layout of the rerank CTA; every array starts on 16 bytes.
+struct RerankLayout {
+    int q, fd, fid, wd, wi, nd, ni, rows, fixed;
+};
+
+__host__ __device__ inline RerankLayout rerank_layout(int dim, int k, int mb) {
+    auto r16 = [](int b) { return (b + 15) / 16 * 16; };
+    RerankLayout L;
+    int o = 0;
+    L.q = o;
+    o += r16(dim * 4);
+    L.fd = o;
+    o += r16(k * 4);
+    L.fid = o;
+    o += r16(k * 4);
+    L.wd = o;
+    o += r16(((mb + 3) & ~3) * 4);
+    L.wi = o;
+    o += r16(mb * 4);
+    L.nd = o;
+    o += r16(k * 4);
+    L.ni = o;
+    o += r16(k * 4);
+    L.rows = o;
+    L.fixed = o;
+    return L;
+}
+
+// Candidate rows staged in shared memory: a float row is dim floats, a uint8
+// row dim bytes, each padded to an odd number of 16-byte units so that the
+// lanes of a quarter-warp reading their own rows hit distinct banks.
+template <class T>
+__host__ __device__ inline int row_stride_bytes(int dim) {
+    const int u = ((int)sizeof(T) * dim + 15) / 16;
+    return ((u & 1) ? u : u + 1) * 16;
+}
+
+// Exact squared L2 of a candidate row in shared memory, in dimension order
+// (fmaf, as nvcc contracts the reference's `local_d += diff*diff`).
+__device__ __forceinline__ float exact_l2_row(const float* __restrict__ sq, const float* __restrict__ v, int dim) {
     float d = 0.0f;
     if ((dim & 3) == 0) {
-        const float4* v4 = reinterpret_cast<const float4*>(v);
-        const int n4 = dim >> 2;
-        int t = 0;
-        for (; t + 8 <= n4; t += 8) {
-            float4 x[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) x[u] = __ldg(v4 + t + u);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float4 q = *reinterpret_cast<const float4*>(sq + 4 * (t + u));
-                float df = q.x - x[u].x;
-                d = fmaf(df, df, d);
-                df = q.y - x[u].y;
-                d = fmaf(df, df, d);
-                df = q.z - x[u].z;
-                d = fmaf(df, df, d);
-                df = q.w - x[u].w;
-                d = fmaf(df, df, d);
-            }
-        }
-        for (; t < n4; ++t) {
-            const float4 x = __ldg(v4 + t);
-            const float4 q = *reinterpret_cast<const float4*>(sq + 4 * t);
+#pragma unroll 8
+        for (int t = 0; t < dim; t += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(v + t);
+            const float4 q = *reinterpret_cast<const float4*>(sq + t);
             float df = q.x - x.x;
             d = fmaf(df, df, d);
             df = q.y - x.y;
@@ -72,7 +98,7 @@ __device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const fl
         }
     } else {
         for (int t = 0; t < dim; ++t) {
-            const float df = sq[t] - __ldg(v + t);
+            const float df = sq[t] - v[t];
             d = fmaf(df, df, d);
         }
     }
@@ -80,62 +106,83 @@ __device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const fl
 }
 
 // The same for uint8 rows (C5's raw vectors): each byte converts exactly to
-// float, so the result equals exact_l2 on a float copy.  Sixteen bytes per load.
-__device__ __forceinline__ float exact_l2(const float* __restrict__ sq, const uint8_t* __restrict__ v, int dim) {
+// float, so the result equals the float version on a float copy.
+__device__ __forceinline__ float exact_l2_row(const float* __restrict__ sq, const uint8_t* __restrict__ v, int dim) {
     float d = 0.0f;
     if ((dim & 15) == 0) {
-        const uint4* v16 = reinterpret_cast<const uint4*>(v);
-        const int n16 = dim >> 4;
-        int t = 0;
-        for (; t + 4 <= n16; t += 4) {
-            uint4 x[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) x[u] = __ldg(v16 + t + u);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float xv = (float)((w[e >> 2] >> (8 * (e & 3))) & 0xffu);
-                    const float df = sq[16 * (t + u) + e] - xv;
-                    d = fmaf(df, df, d);
-                }
-            }
-        }
-        for (; t < n16; ++t) {
-            const uint4 x = __ldg(v16 + t);
+#pragma unroll 2
+        for (int t = 0; t < dim; t += 16) {
+            const uint4 x = *reinterpret_cast<const uint4*>(v + t);
             const uint32_t w[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float xv = (float)((w[e >> 2] >> (8 * (e & 3))) & 0xffu);
-                const float df = sq[16 * t + e] - xv;
+                const float df = sq[t + e] - xv;
                 d = fmaf(df, df, d);
             }
         }
     } else {
         for (int t = 0; t < dim; ++t) {
-            const float df = sq[t] - (float)__ldg(v + t);
+            const float df = sq[t] - (float)v[t];
             d = fmaf(df, df, d);
         }
     }
     return d;
 }
 
+// Copies rows [c0, c0 + nr) of this mini-batch (ids in wi) into `rows` with
+// asynchronous 16-byte copies: every copy of the chunk is in flight at once,
+// so a chunk costs about one memory latency.  Rows of invalid ids are skipped.
+// The caller waits (cp_async_wait_all) and synchronises before reading.
 template <class T>
-__global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
+__device__ __forceinline__ void stage_rows(const RerankArgs& a, const int32_t* wi, int c0, int nr,
+                                           unsigned char* rows, int stride) {
+    const int row_bytes = (int)sizeof(T) * a.dim;
+    if ((row_bytes & 15) == 0) {
+        const int per_row = row_bytes >> 4;
+        const int total = nr * per_row;
+        for (int e = threadIdx.x; e < total; e += RR_NT) {
+            const int r = e / per_row, c = e - r * per_row;
+            const int32_t vid = wi[c0 + r];
+            if (vid >= 0 && (long long)vid < a.nbase) {
+                const unsigned char* src = static_cast<const unsigned char*>(a.base) + (size_t)vid * row_bytes + 16 * c;
+                const uint32_t dst = (uint32_t)__cvta_generic_to_shared(rows + (size_t)r * stride + 16 * c);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+        const int total = nr * a.dim;
+        for (int e = threadIdx.x; e < total; e += RR_NT) {
+            const int r = e / a.dim, c = e - r * a.dim;
+            const int32_t vid = wi[c0 + r];
+            if (vid >= 0 && (long long)vid < a.nbase)
+                reinterpret_cast<T*>(rows + (size_t)r * stride)[c] =
+                    static_cast<const T*>(a.base)[(size_t)vid * a.dim + c];
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <class T>
+__global__ void __launch_bounds__(RR_NT, 4) rerank_kernel(const RerankArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp[RR_NT / 32];
     __shared__ int s_stab;
-    float* s_q = reinterpret_cast<float*>(smem);
-    const int dim4 = (a.dim + 3) / 4 * 4;
-    float* fd = s_q + dim4;          // running top-k distances (ascending)
-    int32_t* fid = reinterpret_cast<int32_t*>(fd + a.k);
-    float* wd = reinterpret_cast<float*>(fid + a.k);  // this mini-batch's candidates
-    int32_t* wi = reinterpret_cast<int32_t*>(wd + a.mb);
-    float* nd = reinterpret_cast<float*>(wi + a.mb);  // merged top-k
-    int32_t* ni = reinterpret_cast<int32_t*>(nd + a.k);
+    const RerankLayout L = rerank_layout(a.dim, a.k, a.mb);
+    float* s_q = reinterpret_cast<float*>(smem + L.q);
+    float* fd = reinterpret_cast<float*>(smem + L.fd);      // running top-k distances (ascending)
+    int32_t* fid = reinterpret_cast<int32_t*>(smem + L.fid);
+    float* wd = reinterpret_cast<float*>(smem + L.wd);      // this mini-batch's candidates (+inf padded to 4)
+    int32_t* wi = reinterpret_cast<int32_t*>(smem + L.wi);
+    float* nd = reinterpret_cast<float*>(smem + L.nd);      // merged top-k
+    int32_t* ni = reinterpret_cast<int32_t*>(smem + L.ni);
+    unsigned char* rows = smem + L.rows;                     // [a.rch][stride]
+    const int stride = row_stride_bytes<T>(a.dim);
 
     const int q = blockIdx.x, tid = threadIdx.x, k = a.k;
+    const int total = a.top_counts[q];
     const float* qv = a.queries + (size_t)q * a.dim;
     for (int t = tid; t < a.dim; t += RR_NT) s_q[t] = qv[t];
     for (int t = tid; t < k; t += RR_NT) {
@@ -144,7 +191,6 @@ __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
     }
     if (tid == 0) s_stab = 0;
     __syncthreads();
-    const int total = a.top_counts[q];
 
     for (int off = 0; off < a.rm; off += a.mb) {
         if (off >= total) break;
@@ -153,62 +199,91 @@ __global__ void __launch_bounds__(RR_NT) rerank_kernel(const RerankArgs a) {
         // padding, which sorts after k earlier entries and can never enter the
         // top-k, so only m = min(eff, nw - k) new entries take part.
         const int m = min(eff, a.nw - k);
-        for (int i = tid; i < m; i += RR_NT) {
-            const int32_t vid = a.top_ids[(size_t)q * a.rm + off + i];
-            float dist = FLT_MAX;
-            if (vid >= 0 && (long long)vid < a.nbase)
-                dist = exact_l2(s_q, static_cast<const T*>(a.base) + (size_t)vid * a.dim, a.dim);
-            wd[i] = dist;
-            wi[i] = vid;
-        }
+        for (int i = tid; i < m; i += RR_NT) wi[i] = a.top_ids[(size_t)q * a.rm + off + i];
         __syncthreads();
-        // stable ranks: old entries come before new ones on equal distance
-        for (int j = tid; j < k; j += RR_NT) {  // old entry j (the top-k is sorted)
-            const float d = fd[j];
-            int r = j;
-            for (int u = 0; u < m; ++u) r += wd[u] < d;
-            if (r < k) {
-                nd[r] = d;
-                ni[r] = fid[j];
+        for (int c0 = 0; c0 < m; c0 += a.rch) {
+            const int nr = min(a.rch, m - c0);
+            stage_rows<T>(a, wi, c0, nr, rows, stride);
+            cp_async_wait_all();
+            __syncthreads();
+            for (int i = tid; i < nr; i += RR_NT) {
+                const int32_t vid = wi[c0 + i];
+                wd[c0 + i] = (vid >= 0 && (long long)vid < a.nbase)
+                                 ? exact_l2_row(s_q, reinterpret_cast<const T*>(rows + (size_t)i * stride), a.dim)
+                                 : FLT_MAX;
             }
+            __syncthreads();
         }
-        for (int i = tid; i < m; i += RR_NT) {  // new entry i
-            const float d = wd[i];
-            int lo = 0, hi = k;  // old entries with distance <= d
-            while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (fd[mid] <= d) lo = mid + 1; else hi = mid;
-            }
-            int r = lo;
-            for (int u = 0; u < m; ++u) {
-                const float du = wd[u];
-                r += (du < d) || (du == d && u < i);
-            }
-            if (r < k) {
-                nd[r] = d;
-                ni[r] = wi[i];
-            }
-        }
+        // +inf padding to a multiple of 4 ranks below no distance (all are
+        // finite: exact or FLT_MAX)
+        const int m4 = (m + 3) & ~3;
+        if (tid < m4 - m) wd[m + tid] = INFINITY;
         __syncthreads();
-        int ch = 0;
-        for (int i = tid; i < k; i += RR_NT) {
-            const int32_t nid = ni[i];
-            if (nid == -1) continue;
-            bool found = false;
-            for (int j = 0; j < k; ++j)
-                if (fid[j] == nid) {
-                    found = true;
-                    break;
+        // stable ranks, old and new entries at once: old entries come before
+        // new ones on equal distance, new ones keep their order
+        const float4* w4 = reinterpret_cast<const float4*>(wd);
+        for (int t = tid; t < k + m; t += RR_NT) {
+            if (t < k) {  // old entry t (the top-k is sorted)
+                const float d = fd[t];
+                int r = t;
+#pragma unroll 4
+                for (int u = 0; u < m4 / 4; ++u) {
+                    const float4 x = w4[u];
+                    r += (x.x < d) + (x.y < d) + (x.z < d) + (x.w < d);
                 }
-            ch += found ? 0 : 1;
+                if (r < k) {
+                    nd[r] = d;
+                    ni[r] = fid[t];
+                }
+            } else {  // new entry i
+                const int i = t - k;
+                const float d = wd[i];
+                int lo = 0, hi = k;  // old entries with distance <= d
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (fd[mid] <= d) lo = mid + 1; else hi = mid;
+                }
+                int r = lo;
+#pragma unroll 4
+                for (int u = 0; u < m4 / 4; ++u) {
+                    const float4 x = w4[u];
+                    const int b = 4 * u;
+                    r += (x.x < d) || (x.x == d && b < i);
+                    r += (x.y < d) || (x.y == d && b + 1 < i);
+                    r += (x.z < d) || (x.z == d && b + 2 < i);
+                    r += (x.w < d) || (x.w == d && b + 3 < i);
+                }
+                if (r < k) {
+                    nd[r] = d;
+                    ni[r] = wi[i];
+                }
+            }
         }
-        int chg;
-        (void)block_exclusive_scan<RR_NT>(ch, warp, chg);
-        if (tid == 0) {
-            if ((float)chg / (float)k <= a.eps)
-                s_stab++;
-            else
-                s_stab = 0;
+        __syncthreads();
+        // the stability counter only decides whether another mini-batch runs
+        // (uniform over the block, so the scan's barriers are all or none)
+        const bool last = off + a.mb >= total || off + a.mb >= a.rm;
+        if (!last) {
+            int ch = 0;
+            for (int i = tid; i < k; i += RR_NT) {
+                const int32_t nid = ni[i];
+                if (nid == -1) continue;
+                bool found = false;
+                for (int j = 0; j < k; ++j)
+                    if (fid[j] == nid) {
+                        found = true;
+                        break;
+                    }
+                ch += found ? 0 : 1;
+            }
+            int chg;
+            (void)block_exclusive_scan<RR_NT>(ch, warp, chg);
+            if (tid == 0) {
+                if ((float)chg / (float)k <= a.eps)
+                    s_stab++;
+                else
+                    s_stab = 0;
+            }
         }
         for (int i = tid; i < k; i += RR_NT) {
             fd[i] = nd[i];
@@ -251,7 +326,10 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
     a.beta = p->beta;
     a.out_ids = out_ids;
     a.out_dists = out_dists;
-    const size_t smem = (size_t)((dim + 3) / 4 * 4) * 4 + (size_t)a.k * 16 + (size_t)a.mb * 8;
+    const int stride = base_u8 ? row_stride_bytes<uint8_t>(dim) : row_stride_bytes<float>(dim);
+    const int mmax = std::max(1, std::min(a.mb, a.nw - a.k));  // new entries per mini-batch
+    a.rch = std::max(8, std::min(mmax, 98304 / stride));
+    const size_t smem = (size_t)rerank_layout(dim, a.k, a.mb).fixed + (size_t)a.rch * stride;
     int dev = 0, smem_max = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));

@@ -21,6 +21,9 @@
 // The ADC arithmetic is bit-identical to the reference: each LUT entry is the
 // same fmaf expression as gpu_global.cu:115-157 / 274-313, and the ADC sum runs
 // over subspaces in order with round-to-nearest adds.
+#include <cstdlib>
+#include <string>
+
 #include "fg_common.cuh"
 
 namespace fg {
@@ -42,6 +45,8 @@ struct ScanArgs {
     int top_m, p1, limit_k;
     float coeff, prune_ratio;
     int rerank_m, rsel, ref_compat, lmax, cap, sort_n;
+    int small;      // team kernel: 1 when no query can emit more than rsel candidates (the buffer is never
+                    // cut) and one warp selects each list; 2 the same with team-wide selection
     int write_pad;  // write (-1, FLT_MAX) / ref_compat zeros past each query's count
     int32_t* top_ids;
     float* top_dists;
@@ -92,37 +97,63 @@ __host__ __device__ inline ScanLayout scan_layout(int M, int dim, int top_m, int
     return L;
 }
 
-// ||r - c||^2 of one subspace, the expression of gpu_global.cu:115-157.
+// ||r - c||^2 of one subspace from values in registers: the expression of
+// gpu_global.cu:115-157.  Every LUT entry and every on-the-fly ADC term is
+// this one function, so both scan kernels produce identical floats.
 template <int SD>
-__device__ __forceinline__ float sub_dist(const float* r, const float* c) {
+__device__ __forceinline__ float sd_arith(const float (&r)[SD], const float (&c)[SD]) {
     if constexpr (SD == 4) {
-        const float4 rv = *reinterpret_cast<const float4*>(r);
-        const float4 cv = __ldg(reinterpret_cast<const float4*>(c));
-        const float dx = rv.x - cv.x, dy = rv.y - cv.y, dz = rv.z - cv.z, dw = rv.w - cv.w;
+        const float dx = r[0] - c[0], dy = r[1] - c[1], dz = r[2] - c[2], dw = r[3] - c[3];
         return fmaf(dx, dx, fmaf(dy, dy, fmaf(dz, dz, __fmul_rn(dw, dw))));
     } else if constexpr (SD == 8) {
-        const float4 r0 = *reinterpret_cast<const float4*>(r);
-        const float4 r1 = *reinterpret_cast<const float4*>(r + 4);
-        const float4 c0 = __ldg(reinterpret_cast<const float4*>(c));
-        const float4 c1 = __ldg(reinterpret_cast<const float4*>(c + 4));
-        const float a0 = r0.x - c0.x, a1 = r0.y - c0.y, a2 = r0.z - c0.z, a3 = r0.w - c0.w;
-        const float a4 = r1.x - c1.x, a5 = r1.y - c1.y, a6 = r1.z - c1.z, a7 = r1.w - c1.w;
+        const float a0 = r[0] - c[0], a1 = r[1] - c[1], a2 = r[2] - c[2], a3 = r[3] - c[3];
+        const float a4 = r[4] - c[4], a5 = r[5] - c[5], a6 = r[6] - c[6], a7 = r[7] - c[7];
         const float d = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, __fmul_rn(a3, a3))));
         return fmaf(a4, a4, fmaf(a5, a5, fmaf(a6, a6, fmaf(a7, a7, d))));
     } else if constexpr (SD == 2) {
-        const float2 rv = *reinterpret_cast<const float2*>(r);
-        const float2 cv = __ldg(reinterpret_cast<const float2*>(c));
-        const float d0 = rv.x - cv.x, d1 = rv.y - cv.y;
+        const float d0 = r[0] - c[0], d1 = r[1] - c[1];
         return fmaf(d1, d1, fmaf(d0, d0, 0.0f));
     } else {
         float d = 0.0f;
 #pragma unroll
         for (int i = 0; i < SD; ++i) {
-            const float df = r[i] - __ldg(c + i);
+            const float df = r[i] - c[i];
             d = fmaf(df, df, d);
         }
         return d;
     }
+}
+
+// SD consecutive floats; GLOBAL reads through the read-only path.
+template <int SD, bool GLOBAL>
+__device__ __forceinline__ void load_sub(const float* p, float (&v)[SD]) {
+    if constexpr (SD % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < SD / 4; ++i) {
+            const float4 x = GLOBAL ? __ldg(reinterpret_cast<const float4*>(p) + i)
+                                    : reinterpret_cast<const float4*>(p)[i];
+            v[4 * i] = x.x;
+            v[4 * i + 1] = x.y;
+            v[4 * i + 2] = x.z;
+            v[4 * i + 3] = x.w;
+        }
+    } else if constexpr (SD == 2) {
+        const float2 x = GLOBAL ? __ldg(reinterpret_cast<const float2*>(p)) : *reinterpret_cast<const float2*>(p);
+        v[0] = x.x;
+        v[1] = x.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < SD; ++i) v[i] = GLOBAL ? __ldg(p + i) : p[i];
+    }
+}
+
+// r in shared memory, c in global memory.
+template <int SD>
+__device__ __forceinline__ float sub_dist(const float* r, const float* c) {
+    float rv[SD], cv[SD];
+    load_sub<SD, false>(r, rv);
+    load_sub<SD, true>(c, cv);
+    return sd_arith<SD>(rv, cv);
 }
 
 __device__ __forceinline__ float sub_dist_rt(const float* r, const float* c, int sd) {
@@ -438,6 +469,735 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
     }
 }
 
+// ---- team kernel: codebook resident in shared memory --------------------------
+//
+// The same per-query algorithm as ivfpq_batch_kernel, run by teams of NT
+// (64, 128 or 256) threads inside a persistent CTA of up to 1024 threads per SM.  The CTA
+// copies the PQ codebook into shared memory once; each team then takes
+// queries in turn and synchronises on its own named barrier, so up to eight
+// queries share an SM and one team's barrier waits are filled by the others'
+// work.  With LUT the
+// team builds each list's residual table from the resident codebook; without
+// it (short lists, where a table of M x 256 entries would outnumber the
+// lookups) every ADC term is computed on the fly from the codebook.  Both
+// produce the floats of the LUT path: one sd_arith expression per term, summed
+// over subspaces in order.
+
+constexpr int TEAM_THREADS = 1024;  // threads of a team CTA: TEAM_THREADS / NT teams of NT
+constexpr double TEAM_OTF_MAX_LEN = 400.0;  // mean list length up to which ADC terms are computed on the fly
+
+template <int NT>
+struct TeamMisc {
+    uint32_t hist[256];
+    int warp[NT / 32];
+    uint32_t b[2];
+    int carry[REF_BLOCK];
+    unsigned char passf[NT];
+    int buf_n, count, nb_list;
+    uint32_t prune_key;
+    float thr;
+};
+
+struct TeamLayout {
+    int lut, res, pid, cut, lkey, ckey, cid, sortb, misc, total;
+};
+
+template <int NT>
+__host__ __device__ inline TeamLayout team_layout(int M, int dim, int top_m, int p1, int lmax, int cap,
+                                                  int sort_n, bool lut) {
+    TeamLayout L;
+    int o = 0;
+    L.lut = lut ? take16(o, M * 256 * 4) : 0;
+    L.res = take16(o, dim * 4);
+    L.pid = take16(o, top_m * 4);
+    L.cut = take16(o, (p1 > 0 ? p1 : 1) * 4);
+    L.lkey = take16(o, (lmax > 0 ? lmax : 1) * 4);
+    const int prefix = o;  // dead once the final sort starts
+    L.ckey = take16(o, cap * 4);
+    L.cid = take16(o, cap * 4);
+    L.sortb = (sort_n * 8 <= prefix) ? 0 : take16(o, sort_n * 8);
+    L.misc = take16(o, (int)sizeof(TeamMisc<NT>));
+    L.total = o;
+    return L;
+}
+
+template <int NT>
+__device__ __forceinline__ void team_sync(int bar) {
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
+}
+
+// block_exclusive_scan over one team (thread tt of NT, barrier `bar`).
+template <int NT>
+__device__ __forceinline__ int team_exclusive_scan(int v, int tt, int bar, int* s_warp, int& total) {
+    const int lane = tt & 31, w = tt >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[w] = x;
+    team_sync<NT>(bar);
+    if (w == 0) {
+        int t = (lane < NT / 32) ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        if (lane < NT / 32) s_warp[lane] = t;
+    }
+    team_sync<NT>(bar);
+    const int wbase = w ? s_warp[w - 1] : 0;
+    total = s_warp[NT / 32 - 1];
+    team_sync<NT>(bar);
+    return wbase + x - v;
+}
+
+// block_radix_select over one team.
+template <int NT>
+__device__ void team_radix_select(const uint32_t* keys, int n, int k, int tt, int bar, uint32_t* s_hist,
+                                  uint32_t* s_b, uint32_t& kth, int& n_less) {
+    uint32_t prefix = 0, mask = 0, kk = (uint32_t)k, less = 0;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tt; i < 256; i += NT) s_hist[i] = 0;
+        team_sync<NT>(bar);
+        for (int i = tt; i < n; i += NT) {
+            const uint32_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+        }
+        team_sync<NT>(bar);
+        if (tt < 32) {
+            const int lane = tt;
+            uint32_t c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = s_hist[lane * 8 + j];
+                sum += c[j];
+            }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - sum;
+            if (excl < kk && kk <= incl) {
+                uint32_t run = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run + c[j] >= kk) {
+                        s_b[0] = (uint32_t)(lane * 8 + j);
+                        s_b[1] = run;
+                        break;
+                    }
+                    run += c[j];
+                }
+            }
+        }
+        team_sync<NT>(bar);
+        const uint32_t b = s_b[0], below = s_b[1];
+        prefix |= b << shift;
+        mask |= 255u << shift;
+        kk -= below;
+        less += below;
+        team_sync<NT>(bar);
+    }
+    kth = prefix;
+    n_less = (int)less;
+}
+
+// block_bitonic_sort over one team.
+template <int NT>
+__device__ void team_bitonic_sort(unsigned long long* sb, int n_pow2, int tt, int bar) {
+    for (int k = 2; k <= n_pow2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tt; i < n_pow2; i += NT) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = sb[i], y = sb[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((x > y) == up) {
+                        sb[i] = y;
+                        sb[ixj] = x;
+                    }
+                }
+            }
+            team_sync<NT>(bar);
+        }
+    }
+}
+
+template <int NT>
+struct TeamBufs {
+    uint32_t* ckey;
+    int32_t* cid;
+    TeamMisc<NT>* ms;
+};
+
+// reduce_buffer over one team.
+template <int NT>
+__device__ void team_reduce_buffer(int rsel, int tt, int bar, const TeamBufs<NT>& tb) {
+    TeamMisc<NT>* ms = tb.ms;
+    const int n = ms->buf_n;
+    uint32_t kth;
+    int n_less;
+    team_radix_select<NT>(tb.ckey, n, rsel, tt, bar, ms->hist, ms->b, kth, n_less);
+    const int need_eq = rsel - n_less;
+    int eq_base = 0, out_base = 0;
+    for (int r0 = 0; r0 < n; r0 += NT) {
+        const int i = r0 + tt;
+        const bool in = i < n;
+        const uint32_t key = in ? tb.ckey[i] : 0xffffffffu;
+        const int32_t idv = in ? tb.cid[i] : 0;
+        const int is_eq = (in && key == kth) ? 1 : 0;
+        int eq_tot, k_tot;
+        const int eq_pre = team_exclusive_scan<NT>(is_eq, tt, bar, ms->warp, eq_tot);
+        const bool keep = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
+        eq_base += eq_tot;
+        const int k_pre = team_exclusive_scan<NT>(keep ? 1 : 0, tt, bar, ms->warp, k_tot);
+        if (keep) {
+            tb.ckey[out_base + k_pre] = key;
+            tb.cid[out_base + k_pre] = idv;
+        }
+        out_base += k_tot;
+        team_sync<NT>(bar);
+    }
+    if (tt == 0) {
+        ms->buf_n = out_base;
+        ms->prune_key = kth;
+    }
+    team_sync<NT>(bar);
+}
+
+// append over one team.
+template <int NT>
+__device__ __forceinline__ void team_append(const ScanArgs& a, bool emit, uint32_t key, int32_t id, int tt, int bar,
+                                            const TeamBufs<NT>& tb) {
+    TeamMisc<NT>* ms = tb.ms;
+    int tot;
+    const int pre = team_exclusive_scan<NT>(emit ? 1 : 0, tt, bar, ms->warp, tot);
+    if (tot == 0) return;
+    if (ms->buf_n + tot > a.cap) team_reduce_buffer<NT>(a.rsel, tt, bar, tb);
+    const int base = ms->buf_n;
+    if (emit) {
+        tb.ckey[base + pre] = key;
+        tb.cid[base + pre] = id;
+    }
+    team_sync<NT>(bar);
+    if (tt == 0) ms->buf_n = base + tot;
+    team_sync<NT>(bar);
+}
+
+// k-th smallest (1-based) of n keys by one warp, as team_radix_select but
+// without team barriers: 8-bit MSD passes that start below the bytes every
+// key shares.
+__device__ void warp_select_keys(const uint32_t* keys, int n, int k, uint32_t* hist, uint32_t& kth, int& n_less) {
+    const int lane = threadIdx.x & 31;
+    uint32_t kand = 0xffffffffu, kor = 0u;
+    for (int i = lane; i < n; i += 32) {
+        const uint32_t x = keys[i];
+        kand &= x;
+        kor |= x;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        kand &= __shfl_xor_sync(0xffffffffu, kand, o);
+        kor |= __shfl_xor_sync(0xffffffffu, kor, o);
+    }
+    const uint32_t diff = kand ^ kor;
+    int top = 24;
+    while (top > 0 && ((diff >> top) & 255u) == 0u) top -= 8;
+    uint32_t mask = top == 24 ? 0u : (0xffffffffu << (top + 8));
+    uint32_t prefix = kand & mask, kk = (uint32_t)k, less = 0;
+#pragma unroll 1
+    for (int shift = top; shift >= 0; shift -= 8) {
+        for (int i = lane; i < 256; i += 32) hist[i] = 0;
+        __syncwarp();
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int i = i0 + lane;
+            const uint32_t key = i < n ? keys[i] : 0u;
+            const bool in = i < n && (key & mask) == prefix;
+            const uint32_t dg = (key >> shift) & 255u;
+            if (in) atomicAdd(&hist[dg], 1u);
+        }
+        __syncwarp();
+        uint32_t c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            c[j] = hist[lane * 8 + j];
+            sum += c[j];
+        }
+        uint32_t incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - sum;
+        const bool mine = excl < kk && kk <= incl;
+        uint32_t b = 0, below = 0;
+        if (mine) {
+            uint32_t run = excl;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (run + c[j] >= kk) {
+                    b = (uint32_t)(lane * 8 + j);
+                    below = run;
+                    break;
+                }
+                run += c[j];
+            }
+        }
+        const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        b = __shfl_sync(0xffffffffu, b, src);
+        below = __shfl_sync(0xffffffffu, below, src);
+        prefix |= b << shift;
+        mask |= 255u << shift;
+        kk -= below;
+        less += below;
+        __syncwarp();
+    }
+    kth = prefix;
+    n_less = (int)less;
+}
+
+constexpr int WARP_SELECT_MAX = 1024;  // lists up to this length are selected by one warp
+
+// ADC distance of one code row with every term computed from the resident
+// codebook `cb` ([M][256][SD]) and the list residual `res`.
+template <int M, int SD>
+__device__ __forceinline__ float adc_otf(const uint8_t* __restrict__ row, const float* cb, const float* res) {
+    float d = 0.0f;
+    if constexpr (M % 16 == 0) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+        for (int w = 0; w < M / 16; ++w) {
+            const uint4 v = __ldg(r4 + w);
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int b = 0; b < 16; ++b) {
+                const int m = 16 * w + b;
+                const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
+                float rv[SD], cv[SD];
+                load_sub<SD, false>(res + m * SD, rv);
+                load_sub<SD, false>(cb + ((size_t)m * 256 + code) * SD, cv);
+                d = __fadd_rn(d, sd_arith<SD>(rv, cv));
+            }
+        }
+    } else {
+        static_assert(M % 4 == 0, "pq_m must be a multiple of 4");
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(row);
+#pragma unroll
+        for (int w = 0; w < M / 4; ++w) {
+            const uint32_t v = __ldg(r1 + w);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int m = 4 * w + b;
+                const uint32_t code = (v >> (8 * b)) & 0xffu;
+                float rv[SD], cv[SD];
+                load_sub<SD, false>(res + m * SD, rv);
+                load_sub<SD, false>(cb + ((size_t)m * 256 + code) * SD, cv);
+                d = __fadd_rn(d, sd_arith<SD>(rv, cv));
+            }
+        }
+    }
+    return d;
+}
+
+// Whether the on-the-fly ADC of (M, SD) runs skewed: the resident codebook is
+// stored as [code][subspace][SD] and the lanes of one shared-memory phase
+// (Z = 32 / SD lanes: 128 bytes of 4*SD-byte terms) walk the subspaces offset
+// by lane % Z, so that at every step they read Z different subspaces.  With
+// M*SD a multiple of 32 the codebook entry (k, m) then lies in bank group
+// m % Z for every code k, and so does the residual of subspace m: both reads
+// are free of bank conflicts whatever the codes.
+template <int M, int SD>
+struct AdcSkew {
+    static constexpr int Z = (SD == 1 || SD == 2 || SD == 4 || SD == 8) ? 32 / SD : 0;
+    static constexpr bool value = Z > 0 && (M * SD) % 32 == 0 && M % Z == 0;
+};
+
+// Byte t of a code row held in registers (static t).
+template <int W>
+__device__ __forceinline__ uint32_t code_byte(const uint32_t (&w)[W], int t) {
+    return (w[t >> 2] >> (8 * (t & 3))) & 0xffu;
+}
+
+// ADC of one code row, skewed: lane offset j = lane % Z.  Step s (0 .. M+Z-2)
+// handles subspace s - j when that is in [0, M); the row's bytes are first
+// rotated by j so that the byte of step s sits at static position s mod M.
+// Each lane still adds its terms in subspace order, so the sum is the same
+// float as adc_otf's.
+template <int M, int SD>
+__device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, const float* cbT, const float* res) {
+    constexpr int Z = AdcSkew<M, SD>::Z;
+    constexpr int W = M / 4;
+    const int j = (threadIdx.x & 31) % Z;
+    uint32_t w[W];
+    if constexpr (M % 16 == 0) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+        for (int u = 0; u < M / 16; ++u) {
+            const uint4 v = __ldg(r4 + u);
+            w[4 * u] = v.x;
+            w[4 * u + 1] = v.y;
+            w[4 * u + 2] = v.z;
+            w[4 * u + 3] = v.w;
+        }
+    } else {
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(row);
+#pragma unroll
+        for (int u = 0; u < W; ++u) w[u] = __ldg(r1 + u);
+    }
+    // rotate the M bytes up by j: words by j / 4 (barrel), then bytes by j % 4
+    {
+        const int jw = j >> 2;
+#pragma unroll
+        for (int b = 1; b < (Z + 3) / 4; b <<= 1) {
+            if (jw & b) {
+                uint32_t t[W];
+#pragma unroll
+                for (int u = 0; u < W; ++u) t[u] = w[(u - b + W) % W];
+#pragma unroll
+                for (int u = 0; u < W; ++u) w[u] = t[u];
+            }
+        }
+        const int jb = 8 * (j & 3);
+        if (jb) {
+            uint32_t t[W];
+#pragma unroll
+            for (int u = 0; u < W; ++u) t[u] = __funnelshift_l(w[(u - 1 + W) % W], w[u], jb);
+#pragma unroll
+            for (int u = 0; u < W; ++u) w[u] = t[u];
+        }
+    }
+    const float* rl = res - j * SD;            // + s*SD: residual of subspace s - j
+    const float* cl = cbT - j * SD;            // + (k*M + s)*SD: codebook entry (k, s - j)
+    float d = 0.0f;
+#pragma unroll
+    for (int st = 0; st < M + Z - 1; ++st) {
+        const bool act = (st < Z - 1 || st >= M) ? (st >= j && st < j + M) : true;
+        if (act) {
+            const uint32_t k = code_byte<W>(w, st % M);
+            float rv[SD], cv[SD];
+            load_sub<SD, false>(rl + st * SD, rv);
+            load_sub<SD, false>(cl + ((size_t)k * M + st) * SD, cv);
+            d = __fadd_rn(d, sd_arith<SD>(rv, cv));
+        }
+    }
+    return d;
+}
+
+// Residual of list c for this query; with LUT also the list's table from the
+// resident codebook.  Ends on the team barrier.
+template <int M, int SD, bool LUT, int NT>
+__device__ __forceinline__ void team_prepare_list(const ScanArgs& a, const float* qv, uint32_t c, const float* cb,
+                                                  float* res, float* lut, int tt, int bar) {
+    const float* cv = a.centroids + (size_t)c * a.dim;
+    for (int t = tt; t < a.dim; t += NT) res[t] = qv[t] - cv[t];
+    team_sync<NT>(bar);
+    if constexpr (LUT) {
+        for (int e = tt; e < M * 256; e += NT) {
+            const int m = e >> 8;
+            float rv[SD], cv2[SD];
+            load_sub<SD, false>(res + m * SD, rv);
+            load_sub<SD, false>(cb + (size_t)e * SD, cv2);
+            lut[e] = sd_arith<SD>(rv, cv2);
+        }
+        team_sync<NT>(bar);
+    }
+}
+
+template <int M, int SD, bool LUT>
+__device__ __forceinline__ float team_adc(const ScanArgs& a, int start, int i, const float* cb, const float* res,
+                                          const float* lut) {
+    const uint8_t* row = a.codes + (size_t)(start + i) * M;
+    if constexpr (LUT)
+        return adc<M>(row, lut);
+    else if constexpr (AdcSkew<M, SD>::value)
+        return adc_otf_skew<M, SD>(row, cb, res);
+    else
+        return adc_otf<M, SD>(row, cb, res);
+}
+
+template <int M, int SD, bool LUT, int NT>
+__global__ void __launch_bounds__(TEAM_THREADS, 1)
+    ivfpq_team_kernel(const ScanArgs a, int nq, int nteams, int team_bytes) {
+    // the ref_compat phase-2 overflow ranks need whole 128-thread groups: the
+    // host launches teams of 64 threads only without ref_compat
+    static_assert(NT % REF_BLOCK == 0 || NT == 64, "team size");
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int CBF = M * 256 * SD;  // codebook floats
+    float* cb = reinterpret_cast<float*>(smem);
+    {
+        static_assert(CBF % 4 == 0, "the codebook copies as float4");
+        if constexpr (!LUT && AdcSkew<M, SD>::value) {
+            // [subspace][code][SD] -> [code][subspace][SD]
+            for (int e = threadIdx.x; e < M * 256; e += blockDim.x) {
+                const int m = e >> 8, k = e & 255;
+                float v[SD];
+                load_sub<SD, true>(a.codebook + (size_t)e * SD, v);
+#pragma unroll
+                for (int t = 0; t < SD; ++t) cb[((size_t)k * M + m) * SD + t] = v[t];
+            }
+        } else {
+            const float4* src = reinterpret_cast<const float4*>(a.codebook);
+            float4* dst = reinterpret_cast<float4*>(cb);
+            for (int i = threadIdx.x; i < CBF / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+        }
+    }
+    __syncthreads();
+    const int team = threadIdx.x / NT, tt = threadIdx.x % NT;
+    const int bar = 1 + team;
+    unsigned char* ts = smem + (size_t)(CBF * 4 + 15) / 16 * 16 + (size_t)team * team_bytes;
+    const TeamLayout L = team_layout<NT>(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n, LUT);
+    float* lut = reinterpret_cast<float*>(ts + L.lut);
+    float* res = reinterpret_cast<float*>(ts + L.res);
+    uint32_t* pid = reinterpret_cast<uint32_t*>(ts + L.pid);
+    float* cut = reinterpret_cast<float*>(ts + L.cut);
+    uint32_t* lkey = reinterpret_cast<uint32_t*>(ts + L.lkey);
+    unsigned long long* sortb = reinterpret_cast<unsigned long long*>(ts + L.sortb);
+    const TeamBufs<NT> tb{reinterpret_cast<uint32_t*>(ts + L.ckey), reinterpret_cast<int32_t*>(ts + L.cid),
+                          reinterpret_cast<TeamMisc<NT>*>(ts + L.misc)};
+    TeamMisc<NT>* ms = tb.ms;
+    const int P = a.top_m;
+
+    for (int q = blockIdx.x * nteams + team; q < nq; q += gridDim.x * nteams) {
+        const float* qv = a.queries + (size_t)q * a.dim;
+        // prune (gpu_global.cu:43-51); ids outside [0, nlist) are skipped
+        const float best = a.probe_dists[(size_t)q * P];
+        const float pthr = best * a.prune_ratio;
+        for (int j = tt; j < P; j += NT) {
+            const float d = a.probe_dists[(size_t)q * P + j];
+            const uint32_t id = a.probe_ids[(size_t)q * P + j];
+            pid[j] = (d > pthr || id >= (uint32_t)a.nlist) ? FG_INVALID_PROBE : id;
+        }
+        if (tt == 0) {
+            ms->buf_n = 0;
+            ms->count = 0;
+            ms->prune_key = 0xffffffffu;
+        }
+        team_sync<NT>(bar);
+
+        // ---- phase 1 ----------------------------------------------------------
+        for (int j = 0; j < a.p1; ++j) {
+            const uint32_t c = pid[j];
+            int start = 0, len = 0;
+            if (c != FG_INVALID_PROBE) {
+                start = a.offsets[c];
+                len = a.offsets[c + 1] - start;
+            }
+            if (len <= 0) {
+                if (tt == 0) cut[j] = 0.0f;
+                continue;
+            }
+            const int wc = len < a.limit_k ? len : a.limit_k;
+            const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
+            team_prepare_list<M, SD, LUT, NT>(a, qv, c, cb, res, lut, tt, bar);
+            for (int i = tt; i < scan; i += NT) lkey[i] = f2key(team_adc<M, SD, LUT>(a, start, i, cb, res, lut));
+            team_sync<NT>(bar);
+            if (a.small == 1 && scan <= WARP_SELECT_MAX) {
+                // one warp selects and emits (the buffer can never need a cut)
+                if (tt < 32) {
+                    uint32_t kth;
+                    int n_less;
+                    warp_select_keys(lkey, scan, wc, ms->hist, kth, n_less);
+                    const unsigned lt = lanemask_lt();
+                    const int need_eq = wc - n_less;
+                    const uint32_t pk = ms->prune_key;
+                    int eq_base = 0, bn = ms->buf_n;
+                    for (int i0 = 0; i0 < scan; i0 += 32) {
+                        const int i = i0 + tt;
+                        const bool in = i < scan;
+                        const uint32_t key = in ? lkey[i] : 0xffffffffu;
+                        const bool is_eq = in && key == kth;
+                        const unsigned eqb = __ballot_sync(0xffffffffu, is_eq);
+                        const bool sel = in && (key < kth || (is_eq && eq_base + __popc(eqb & lt) < need_eq));
+                        eq_base += __popc(eqb);
+                        const bool emit = sel && key < pk;
+                        const unsigned eb = __ballot_sync(0xffffffffu, emit);
+                        if (emit) {
+                            const int pos = bn + __popc(eb & lt);
+                            tb.ckey[pos] = key;
+                            tb.cid[pos] = start + i;
+                        }
+                        bn += __popc(eb);
+                    }
+                    if (tt == 0) {
+                        ms->buf_n = bn;
+                        cut[j] = key2f(kth);
+                        ms->count += wc;
+                    }
+                }
+                team_sync<NT>(bar);
+                continue;
+            }
+            uint32_t kth;
+            int n_less;
+            team_radix_select<NT>(lkey, scan, wc, tt, bar, ms->hist, ms->b, kth, n_less);
+            if (tt == 0) {
+                cut[j] = key2f(kth);
+                ms->count += wc;
+            }
+            const int need_eq = wc - n_less;
+            int eq_base = 0;
+            for (int r0 = 0; r0 < scan; r0 += NT) {
+                const int i = r0 + tt;
+                const bool in = i < scan;
+                const uint32_t key = in ? lkey[i] : 0xffffffffu;
+                const int is_eq = (in && key == kth) ? 1 : 0;
+                int eq_tot;
+                const int eq_pre = team_exclusive_scan<NT>(is_eq, tt, bar, ms->warp, eq_tot);
+                const bool sel = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
+                eq_base += eq_tot;
+                const bool emit = sel && key < ms->prune_key;
+                team_append<NT>(a, emit, key, emit ? start + i : 0, tt, bar, tb);
+            }
+        }
+
+        // ---- threshold (gpu_global.cu:394-426) ---------------------------------
+        team_sync<NT>(bar);
+        if (tt == 0) {
+            float mn = FLT_MAX;
+            for (int j = 0; j < a.p1; ++j)
+                if (cut[j] > 0.0f && cut[j] < mn) mn = cut[j];
+            ms->thr = (mn < FLT_MAX) ? mn * a.coeff : FLT_MAX;
+        }
+        team_sync<NT>(bar);
+        const float thr = ms->thr;
+
+        // ---- phase 2 ------------------------------------------------------------
+        for (int j = a.p1; j < P; ++j) {
+            const uint32_t c = pid[j];
+            int start = 0, len = 0;
+            if (c != FG_INVALID_PROBE) {
+                start = a.offsets[c];
+                len = a.offsets[c + 1] - start;
+            }
+            if (len <= 0) continue;
+            if (tt == 0) ms->nb_list = 0;
+            team_prepare_list<M, SD, LUT, NT>(a, qv, c, cb, res, lut, tt, bar);
+            for (int c0 = 0; c0 < len; c0 += NT) {
+                const int i = c0 + tt;
+                float d = 0.0f;
+                bool pass = false;
+                if (i < len) {
+                    d = team_adc<M, SD, LUT>(a, start, i, cb, res, lut);
+                    pass = d <= thr;
+                }
+                int p_tot;
+                const int p_pre = team_exclusive_scan<NT>(pass ? 1 : 0, tt, bar, ms->warp, p_tot);
+                const int rank = ms->nb_list + p_pre;
+                const uint32_t key = f2key(d);
+                const bool emit = pass && (!a.ref_compat || rank < REF_BLOCK) && key < ms->prune_key;
+                team_append<NT>(a, emit, key, emit ? start + i : 0, tt, bar, tb);
+                if (tt == 0) ms->nb_list += p_tot;
+                team_sync<NT>(bar);
+            }
+            const int s_count = ms->nb_list;
+            if (!a.ref_compat || s_count <= REF_BLOCK) {
+                if (tt == 0) ms->count += s_count;
+                team_sync<NT>(bar);
+                continue;
+            }
+            // overflow: each of the reference's 128 threads re-emits its first
+            // (s_count - 128) passing vectors (gpu_global.cu:508-526)
+            const int quota = s_count - REF_BLOCK;
+            if (tt < REF_BLOCK) ms->carry[tt] = 0;
+            if (tt == 0) ms->count += REF_BLOCK;
+            team_sync<NT>(bar);
+            for (int c0 = 0; c0 < len; c0 += NT) {
+                const int i = c0 + tt;
+                float d = 0.0f;
+                bool pass = false;
+                if (i < len) {
+                    d = team_adc<M, SD, LUT>(a, start, i, cb, res, lut);
+                    pass = d <= thr;
+                }
+                ms->passf[tt] = pass ? 1 : 0;
+                team_sync<NT>(bar);
+                // rank among the passing vectors of the same reference thread (i mod 128)
+                const int t = tt % REF_BLOCK;
+                int rank = ms->carry[t];
+                for (int u = t; u < tt; u += REF_BLOCK) rank += ms->passf[u];
+                const bool re = pass && rank < quota;
+                int r_tot;
+                (void)team_exclusive_scan<NT>(re ? 1 : 0, tt, bar, ms->warp, r_tot);
+                if (tt == 0) ms->count += r_tot;
+                const uint32_t key = f2key(d);
+                const bool emit = re && key < ms->prune_key;
+                team_append<NT>(a, emit, key, emit ? start + i : 0, tt, bar, tb);
+                if (tt < REF_BLOCK) {
+                    int add = 0;
+                    for (int u = tt; u < NT; u += REF_BLOCK) add += ms->passf[u];
+                    ms->carry[tt] += add;
+                }
+                team_sync<NT>(bar);
+            }
+        }
+
+        // ---- select, sort and gather (gpu_global.cu:838-871) -------------------
+        team_sync<NT>(bar);
+        if (ms->buf_n > a.rsel) team_reduce_buffer<NT>(a.rsel, tt, bar, tb);
+        const int n = ms->buf_n;
+        const int npow = next_pow2(n > 0 ? n : 1);
+        for (int i = tt; i < npow; i += NT)
+            sortb[i] = (i < n) ? ((unsigned long long)tb.ckey[i] << 32) | (unsigned)i : ~0ull;
+        team_sync<NT>(bar);
+        if (npow <= 256) {  // one warp: no team barriers between the stages
+            if (tt < 32) warp_bitonic_sort(sortb, npow);
+            team_sync<NT>(bar);
+        } else {
+            team_bitonic_sort<NT>(sortb, npow, tt, bar);
+        }
+        const int count = ms->count;
+        const int rm = a.rerank_m;
+        const int ak = count < rm ? count : rm;
+        const int pend = a.write_pad ? rm : (ak < rm ? ak : rm);
+        for (int p = tt; p < pend; p += NT) {
+            const size_t o = (size_t)q * rm + p;
+            if (a.ref_compat && p >= REF_BLOCK) {
+                a.top_ids[o] = 0;
+                a.top_dists[o] = 0.0f;
+            } else if (p < ak) {
+                const unsigned long long e = sortb[p];
+                a.top_ids[o] = __ldg(a.vids + tb.cid[(unsigned)(e & 0xffffffffu)]);
+                a.top_dists[o] = key2f((uint32_t)(e >> 32));
+            } else {
+                a.top_ids[o] = -1;
+                a.top_dists[o] = FLT_MAX;
+            }
+        }
+        if (tt == 0) {
+            a.top_counts[q] = ak;
+            if (a.cand_counts) a.cand_counts[q] = count;
+        }
+        team_sync<NT>(bar);  // the next query reuses every buffer
+    }
+}
+
+using TeamKernel = void (*)(const ScanArgs, int, int, int);
+
+template <bool LUT, int NT>
+static TeamKernel pick_team_kernel(int M, int SD) {
+#define FG_TEAM_CASE(m, sd) \
+    if (M == m && SD == sd) return ivfpq_team_kernel<m, sd, LUT, NT>;
+    FG_TEAM_CASE(4, 4)  // small test indexes
+    FG_TEAM_CASE(16, 4)
+    FG_TEAM_CASE(16, 8)
+    FG_TEAM_CASE(32, 2)
+    FG_TEAM_CASE(32, 3)
+    FG_TEAM_CASE(32, 4)
+    FG_TEAM_CASE(48, 2)
+    FG_TEAM_CASE(64, 2)
+    FG_TEAM_CASE(96, 8)
+    FG_TEAM_CASE(128, 1)
+#undef FG_TEAM_CASE
+    return nullptr;
+}
+
 using ScanKernel = void (*)(const ScanArgs);
 
 static ScanKernel pick_scan_kernel(int M, int SD) {
@@ -514,11 +1274,102 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.top_counts = top_counts;
     a.cand_counts = cand_counts;
     a.write_pad = write_pad ? 1 : 0;
+    a.small = 0;
 
     int dev = 0, smem_max = 0, smem_sm = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+
+    // The team kernel when the codebook and at least one team fit in shared
+    // memory (two teams for on-the-fly ADC).  FG_SCAN_KERNEL=block|team|team_lut|team_otf
+    // and FG_SCAN_TEAM_NT=64|128|256 override the choice (for tests and measurements).
+    const char* force = getenv("FG_SCAN_KERNEL");
+    const std::string mode = force ? force : "";
+    if (mode != "block") {
+        const double avg_len = (double)ix->total / ix->nlist;
+        const bool lut = mode == "team_lut" || (mode != "team_otf" && avg_len > TEAM_OTF_MAX_LEN);
+        // the most candidates one query can emit: phase-1 lists give at most
+        // limit_k each, phase-2 lists at most their length.  Below rsel the
+        // buffer is never cut and the final sort never holds more.
+        const long long p1n = std::min(a.top_m, a.p1);
+        const long long maxcand = std::max(1LL, p1n * std::min(a.limit_k, a.lmax) +
+                                                    (long long)(a.top_m - p1n) * std::max(ix->max_list_len, 1));
+        const bool small = maxcand < a.rsel;
+        const int sort_n = small ? next_pow2((int)maxcand) : a.sort_n;
+        const int cb_bytes = (M * 256 * SD * 4 + 15) / 16 * 16;
+        const int avail = smem_max - cb_bytes;
+        struct Pick {
+            TeamKernel k = nullptr;
+            int nt = 0, nteams = 0, cap = 0, bytes = 0;
+        } best;
+        const char* fnt = getenv("FG_SCAN_TEAM_NT");  // 64, 128 or 256: only that team size
+        // Small per-query work (few probed vectors) favours many small teams,
+        // more work per query teams of 128 (measured on C2: 64 at nprobe 2, 128
+        // at nprobe 8); when shared memory caps the team count, larger teams.
+        const double est = (double)a.top_m * avg_len;
+        const int pref_nt = (est <= 1024.0 && !a.ref_compat) ? 64 : 128;
+        const int only_nt = fnt ? atoi(fnt) : 0;
+        int pass_nt = only_nt;
+        Pick by_nt[3];  // teams of 64, 128, 256
+        auto consider = [&](TeamKernel k, int nt, int min_cap, int roomy_cap, int tbytes_min, int tbytes_roomy) {
+            // (a forced 64 yields to 128 under ref_compat, which needs whole 128-thread groups)
+            const int want_nt = (pass_nt == 64 && a.ref_compat) ? 128 : pass_nt;
+            if (!k || avail <= 0 || (want_nt && nt != want_nt)) return;
+            const int maxt = std::min(TEAM_THREADS / nt, 15);  // named barriers 1..15
+            int nteams = std::min(maxt, avail / tbytes_min);
+            if (nteams < (lut ? 1 : 2)) return;
+            int cap = min_cap, tbytes = tbytes_min;
+            if (std::min(maxt, avail / tbytes_roomy) == nteams) {
+                cap = roomy_cap;
+                tbytes = tbytes_roomy;
+            }
+            by_nt[nt == 64 ? 0 : nt == 128 ? 1 : 2] = Pick{k, nt, nteams, cap, tbytes};
+        };
+        auto consider_all = [&]() {
+            if (!a.ref_compat) {
+                const int c0 = small ? (int)maxcand + 64 : a.rsel + 64, c1 = small ? c0 : 2 * a.rsel + 64;
+                consider(lut ? pick_team_kernel<true, 64>(M, SD) : pick_team_kernel<false, 64>(M, SD), 64, c0, c1,
+                         team_layout<64>(M, a.dim, a.top_m, a.p1, a.lmax, c0, sort_n, lut).total,
+                         team_layout<64>(M, a.dim, a.top_m, a.p1, a.lmax, c1, sort_n, lut).total);
+            }
+            {
+                const int c0 = small ? (int)maxcand + 128 : a.rsel + 128, c1 = small ? c0 : 2 * a.rsel + 128;
+                consider(lut ? pick_team_kernel<true, 128>(M, SD) : pick_team_kernel<false, 128>(M, SD), 128, c0, c1,
+                         team_layout<128>(M, a.dim, a.top_m, a.p1, a.lmax, c0, sort_n, lut).total,
+                         team_layout<128>(M, a.dim, a.top_m, a.p1, a.lmax, c1, sort_n, lut).total);
+            }
+            {
+                const int c0 = small ? (int)maxcand + 256 : a.rsel + 256, c1 = small ? c0 : 2 * a.rsel + 256;
+                consider(lut ? pick_team_kernel<true, 256>(M, SD) : pick_team_kernel<false, 256>(M, SD), 256, c0, c1,
+                         team_layout<256>(M, a.dim, a.top_m, a.p1, a.lmax, c0, sort_n, lut).total,
+                         team_layout<256>(M, a.dim, a.top_m, a.p1, a.lmax, c1, sort_n, lut).total);
+            }
+        };
+        consider_all();
+        // the size with the most resident threads, unless the preferred size
+        // keeps at least 90 % of them
+        for (const Pick& p : by_nt)
+            if (p.k && p.nteams * p.nt > best.nteams * best.nt) best = p;
+        for (const Pick& p : by_nt)
+            if (p.k && p.nt == pref_nt && 10 * p.nteams * p.nt >= 9 * best.nteams * best.nt) best = p;
+        if (best.k) {
+            a.cap = best.cap;
+            a.sort_n = sort_n;
+            const char* fws = getenv("FG_SCAN_WARP_SELECT");  // 0: team-wide selection always
+            a.small = small ? ((fws && fws[0] == '0') ? 2 : 1) : 0;
+            int nsm = 0;
+            FG_CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+            const int grid = std::max(1, std::min(nsm, (nq + best.nteams - 1) / best.nteams));
+            const int bytes = cb_bytes + best.nteams * best.bytes;
+            FG_CUDA_TRY(cudaFuncSetAttribute(best.k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            best.k<<<grid, best.nteams * best.nt, bytes, stream>>>(a, nq, best.nteams, best.bytes);
+            return check_launch("ivfpq_team_kernel");
+        }
+        if (mode == "team" || mode == "team_lut" || mode == "team_otf")
+            return fail(FG_ERR_UNSUPPORTED, "FG_SCAN_KERNEL=%s: the team kernel does not fit (pq_m=%d sub_dim=%d)",
+                        mode.c_str(), M, SD);
+    }
     // a roomy buffer (fewer cuts) when it fits and costs no resident CTA, else
     // the minimum rsel + one round
     a.cap = 2 * a.rsel + SCAN_NT;

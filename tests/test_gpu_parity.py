@@ -27,6 +27,23 @@ def fg():
     return fgi
 
 
+SCAN_KERNELS = ["auto", "block", "team_otf/64", "team_otf/128", "team_otf/256", "team_lut/64", "team_lut/128",
+                "team_lut/256"]
+
+
+@pytest.fixture(params=SCAN_KERNELS)
+def scan_kernel(request, monkeypatch):
+    """Runs the test once per scan kernel: the per-query CTA kernel and the
+    team kernel with table or on-the-fly ADC, teams of 64, 128 or 256 threads
+    (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat)."""
+    if request.param != "auto":
+        kern, _, nt = request.param.partition("/")
+        monkeypatch.setenv("FG_SCAN_KERNEL", kern)
+        if nt:
+            monkeypatch.setenv("FG_SCAN_TEAM_NT", nt)
+    return request.param
+
+
 def _dataset(kind):
     from fusiongpu_b200 import datasets as ds
     if kind == "int128":
@@ -139,7 +156,7 @@ def test_coarse_tc_many_lists_two_stage(fg):
 @pytest.mark.parametrize("kind", ["int128", "int128m64", "unit96"])
 @pytest.mark.parametrize("pname", list(PARAMS))
 @pytest.mark.parametrize("ref_compat", [True, False])
-def test_batch_logic_and_rerank_match_oracle(fg, kind, pname, ref_compat):
+def test_batch_logic_and_rerank_match_oracle(fg, kind, pname, ref_compat, scan_kernel):
     index, base, q = dataset(kind)
     p = _params(fg, pname, ref_compat)
     if ref_compat and p.final_k > 128:
@@ -161,7 +178,7 @@ def test_batch_logic_and_rerank_match_oracle(fg, kind, pname, ref_compat):
 
 @pytest.mark.parametrize("kind", ["int128", "unit96"])
 @pytest.mark.parametrize("ref_compat", [True, False])
-def test_full_search_matches_oracle(fg, kind, ref_compat):
+def test_full_search_matches_oracle(fg, kind, ref_compat, scan_kernel):
     index, base, q = dataset(kind)
     p = _params(fg, "c1", ref_compat)
     idx = fg.IVFPQIndex.from_arrays(index, base)
@@ -173,7 +190,7 @@ def test_full_search_matches_oracle(fg, kind, ref_compat):
 
 @pytest.mark.parametrize("seed", [0, 1, 2])
 @pytest.mark.parametrize("ref_compat", [True, False])
-def test_toy_edge_cases(fg, seed, ref_compat):
+def test_toy_edge_cases(fg, seed, ref_compat, scan_kernel):
     """Empty lists, a 1100-vector list (phase-1 clamp), phase-2 overflow,
     heavy distance ties (integer codebooks)."""
     index, base = refpy.toy_index(seed)
