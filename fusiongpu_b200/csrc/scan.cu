@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
 // over subspaces in order.
 
 constexpr int TEAM_THREADS = 1024;  // threads of a team CTA: TEAM_THREADS / NT teams of NT
-constexpr double TEAM_OTF_MAX_LEN = 400.0;  // mean list length up to which ADC terms are computed on the fly
+constexpr double TEAM_OTF_MAX_LEN = 400.0;  // mean list length up to which the team kernel (on-the-fly terms) runs
 
 template <int NT>
 struct TeamMisc {
@@ -764,6 +764,7 @@ __device__ void warp_select_keys(const uint32_t* keys, int n, int k, uint32_t* h
 }
 
 constexpr int WARP_SELECT_MAX = 1024;  // lists up to this length are selected by one warp
+constexpr int RANK_SORT_MAX = 256;     // candidate sets up to this size are sorted by ranks
 
 // ADC distance of one code row with every term computed from the resident
 // codebook `cb` ([M][256][SD]) and the list residual `res`.
@@ -1143,13 +1144,31 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
         if (ms->buf_n > a.rsel) team_reduce_buffer<NT>(a.rsel, tt, bar, tb);
         const int n = ms->buf_n;
         const int npow = next_pow2(n > 0 ? n : 1);
-        for (int i = tt; i < npow; i += NT)
-            sortb[i] = (i < n) ? ((unsigned long long)tb.ckey[i] << 32) | (unsigned)i : ~0ull;
-        team_sync<NT>(bar);
-        if (npow <= 256) {  // one warp: no team barriers between the stages
-            if (tt < 32) warp_bitonic_sort(sortb, npow);
+        if (n <= RANK_SORT_MAX) {
+            // rank sort: entry i goes to the number of entries before it in
+            // (key, position) order; the keys are read as broadcasts
+            for (int i = tt; i < n; i += NT) {
+                const uint32_t key = tb.ckey[i];
+                int r = 0;
+                int u = 0;
+                for (; u + 4 <= n; u += 4) {
+                    const uint4 k4 = *reinterpret_cast<const uint4*>(tb.ckey + u);
+                    r += (k4.x < key) || (k4.x == key && u < i);
+                    r += (k4.y < key) || (k4.y == key && u + 1 < i);
+                    r += (k4.z < key) || (k4.z == key && u + 2 < i);
+                    r += (k4.w < key) || (k4.w == key && u + 3 < i);
+                }
+                for (; u < n; ++u) {
+                    const uint32_t ku = tb.ckey[u];
+                    r += (ku < key) || (ku == key && u < i);
+                }
+                sortb[r] = ((unsigned long long)key << 32) | (unsigned)i;
+            }
             team_sync<NT>(bar);
         } else {
+            for (int i = tt; i < npow; i += NT)
+                sortb[i] = (i < n) ? ((unsigned long long)tb.ckey[i] << 32) | (unsigned)i : ~0ull;
+            team_sync<NT>(bar);
             team_bitonic_sort<NT>(sortb, npow, tt, bar);
         }
         const int count = ms->count;
@@ -1286,9 +1305,13 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     // and FG_SCAN_TEAM_NT=64|128|256 override the choice (for tests and measurements).
     const char* force = getenv("FG_SCAN_KERNEL");
     const std::string mode = force ? force : "";
-    if (mode != "block") {
-        const double avg_len = (double)ix->total / ix->nlist;
-        const bool lut = mode == "team_lut" || (mode != "team_otf" && avg_len > TEAM_OTF_MAX_LEN);
+    const double avg_len = (double)ix->total / ix->nlist;
+    // measured: on long lists (C3: 680, C5: 1000 vectors per list at nprobe 64)
+    // the per-query CTA kernel is faster than any team configuration
+    if (mode != "block" && (!mode.empty() || avg_len <= TEAM_OTF_MAX_LEN)) {
+        bool lut = mode == "team_lut";
+        const bool forced = mode == "team_lut" || mode == "team_otf";
+        const int min_teams = forced ? 1 : 2;  // one team leaves an SM mostly idle
         // the most candidates one query can emit: phase-1 lists give at most
         // limit_k each, phase-2 lists at most their length.  Below rsel the
         // buffer is never cut and the final sort never holds more.
@@ -1318,7 +1341,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
             if (!k || avail <= 0 || (want_nt && nt != want_nt)) return;
             const int maxt = std::min(TEAM_THREADS / nt, 15);  // named barriers 1..15
             int nteams = std::min(maxt, avail / tbytes_min);
-            if (nteams < (lut ? 1 : 2)) return;
+            if (nteams < min_teams) return;
             int cap = min_cap, tbytes = tbytes_min;
             if (std::min(maxt, avail / tbytes_roomy) == nteams) {
                 cap = roomy_cap;
@@ -1347,6 +1370,10 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
             }
         };
         consider_all();
+        if (!forced && lut && !by_nt[0].k && !by_nt[1].k && !by_nt[2].k) {
+            lut = false;  // no two teams with tables fit: on-the-fly terms
+            consider_all();
+        }
         // the size with the most resident threads, unless the preferred size
         // keeps at least 90 % of them
         for (const Pick& p : by_nt)
