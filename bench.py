@@ -370,7 +370,9 @@ def roofline(idx, qd, nprobe, args, device, SearchParams, flush):
             traffic = tr["dram_bytes_per_launch"]
     except Exception:
         pass
-    return {"kernel": "ivfpq_batch_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+    # the library's scan dispatch: the team kernel on short lists (mean length <= 400), else one CTA per query
+    kernel = "ivfpq_team_kernel" if idx.total / max(idx.nlist, 1) <= 400 else "ivfpq_batch_kernel"
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
             "traffic": traffic, "algorithmic_bytes": alg, "ms_per_launch": ms, "nprobe": nprobe}
 

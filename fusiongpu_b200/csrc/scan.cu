@@ -935,13 +935,14 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
     {
         static_assert(CBF % 4 == 0, "the codebook copies as float4");
         if constexpr (!LUT && AdcSkew<M, SD>::value) {
-            // [subspace][code][SD] -> [code][subspace][SD]
+            // [subspace][code][SD] -> [code][subspace][SD], walking the
+            // destination in order (conflict-free stores; the reads hit L2)
             for (int e = threadIdx.x; e < M * 256; e += blockDim.x) {
-                const int m = e >> 8, k = e & 255;
+                const int k = e / M, m = e - k * M;
                 float v[SD];
-                load_sub<SD, true>(a.codebook + (size_t)e * SD, v);
+                load_sub<SD, true>(a.codebook + ((size_t)m * 256 + k) * SD, v);
 #pragma unroll
-                for (int t = 0; t < SD; ++t) cb[((size_t)k * M + m) * SD + t] = v[t];
+                for (int t = 0; t < SD; ++t) cb[(size_t)e * SD + t] = v[t];
             }
         } else {
             const float4* src = reinterpret_cast<const float4*>(a.codebook);
