@@ -5,10 +5,15 @@
 //    A = [q_hi | q_hi | q_lo], B = [c_hi | c_lo | c_hi] (K = 3*dim, zero padded to
 //    a multiple of 64), so one bf16 GEMM A.B^T = q_hi.c_hi + q_hi.c_lo + q_lo.c_hi
 //    approximates q.c to about 2^-16 relative.
-// 2. coarse_gemm_kernel: persistent, warp-specialised CTA per 128 queries x a run of
-//    64-centroid tiles; A resident in shared memory, B through a 2-stage TMA ring
-//    (128-byte swizzle, no multicast), tcgen05.mma issued by one thread into two
-//    TMEM accumulators; epilogue computes d~ = |q|^2 + |c|^2 - 2 q.c.
+// 2. coarse_gemm_kernel: persistent, warp-specialised CTA per SM over a balanced
+//    range of (128-query tile, 128-centroid tile) pairs; A resident in shared
+//    memory (reloaded where the range enters the next query tile), B through a
+//    6-stage TMA ring of 16 KB K blocks (128-byte swizzle, no multicast),
+//    tcgen05.mma issued by one thread into two TMEM accumulators; epilogue
+//    computes d~ = |q|^2 + |c|^2 - 2 q.c.
+//    top_m <= 4: a single pass in which every (query, range, column part) keeps
+//    its 4 or 8 smallest d~ in registers (coarse_topk_finish_kernel certifies).
+//    Larger top_m:
 //    Pass 0 writes d~ for a prefix of NS centroids; the S-th smallest of those (S =
 //    max(2P, P+32)) bounds the S-th smallest over all centroids.  Pass 1 covers every
 //    centroid and appends only (d~, id) within that bound to a per-query list, so
@@ -31,16 +36,17 @@
 namespace fg {
 
 
-constexpr int TC_M = 128;       // queries per CTA (UMMA M, TMEM lanes)
-constexpr int TC_N = 64;        // centroids per tile (UMMA N)
+constexpr int TC_M = 128;       // queries per tile (UMMA M, TMEM lanes)
+constexpr int TC_N = 128;       // centroids per tile (UMMA N)
 constexpr int TC_TILE = 128;    // row padding of both operands
 constexpr int TC_KB = 64;       // bf16 elements per K block (one 128-byte swizzle row)
-constexpr int TC_MAX_KB = 6;    // A resident + 2 B stages: 6*16 KB + 2*6*8 KB = 192 KB
+constexpr int TC_MAX_KB = 6;    // A resident (6 x 16 KB) + TC_NST B stages (16 KB each) = 224 KB
+constexpr int TC_NST = 8;       // B ring: one K block of one tile per stage
 constexpr int TC_PARTS = 4;              // column parts of a tile: one epilogue warp per (lane quarter, part)
-constexpr int TC_CPW = TC_N / TC_PARTS;  // 16 columns of each tile per epilogue thread
+constexpr int TC_CPW = TC_N / TC_PARTS;  // 32 columns of each tile per epilogue thread
 constexpr int TC_EPI_WARPS = 4 * TC_PARTS;
 constexpr int TC_NT = 64 + TC_EPI_WARPS * 32;
-constexpr int TC_MAX_TPC = 64;           // tiles per CTA; bounds the staged column norms (16 KB)
+constexpr int TC_NORM_STAGE = 0;  // centroid norms staged in shared memory when ncols <= this
 constexpr int RS_NT = 256;
 
 __host__ __device__ inline int tc_kpad(int dim) { return (3 * dim + TC_KB - 1) / TC_KB * TC_KB; }
@@ -73,48 +79,62 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, long long n, int 
     }
 }
 
-// Warp roles of the persistent GEMM CTA (576 threads):
-//   warp 0, lane 0: TMA producer (A once, then B tiles through a 2-stage ring)
+// Warp roles of the persistent GEMM CTA (576 threads, one CTA per SM):
+//   warp 0, lane 0: TMA producer (the query tile A, then B through a ring of
+//                   TC_NST stages, one 128 x 64 K block per stage)
 //   warp 1, lane 0: MMA issuer (and warp 1 owns the TMEM allocation)
 //   warps 2..17:    epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (its 32
-//                   queries) and columns 16*((w-2)/4) .. +15 of each tile
-// TMEM holds two 128 x 64 fp32 accumulators, so the epilogue of tile i runs
-// while the MMAs of tile i+1 fill the other one.  Four epilogue warps per SM
-// sub-partition hide one another's latency; the norms of the CTA's columns
-// are staged in shared memory once.
+//                   queries) and columns 32*((w-2)/4) .. +31 of each tile
+// The (query tile, centroid tile) pairs are numbered query-tile-major and every
+// CTA takes one contiguous range of L of them, so the work is balanced over the
+// SMs whatever the shape; where a range crosses into the next query tile the
+// producer reloads A once the MMAs on the old one have finished (a_empty).  A
+// range covers one "segment" of a query tile: segment = CTA index minus the
+// first CTA of that query tile, at most maxseg per query tile.  TMEM holds two
+// 128 x 128 fp32 accumulators, so the epilogue of tile i runs while the MMAs of
+// tile i+1 fill the other one.
 struct GemmArgs {
     int kt;              // 64-wide K blocks
     long long q0;        // first query row of this launch (row of the A tensor map)
     int nq;              // query rows of this launch
     int ncols;           // centroid columns [0, ncols)
-    int tiles_per_cta;   // 64-column tiles per CTA (blockIdx.y picks the run), <= TC_MAX_TPC
+    int ntiles;          // centroid tiles: ceil(ncols / TC_N)
+    long long total;     // (query tile, centroid tile) pairs
+    int per_cta;         // L: pairs per CTA
+    int maxseg;          // segments per query tile (lists per query = maxseg * TC_PARTS)
     const float* qn;     // |q|^2, indexed by q0 + row
     const float* cn;     // |c|^2
     uint32_t* out;       // GEMM_MATRIX: order key of d~ at out[row * ldo + col]
     long long ldo;
     const float* tq;     // GEMM_FILTER: per-query bound
-    int cap;             // GEMM_FILTER: capacity of each (query, column run, part) segment
-    int* cnt;            // GEMM_FILTER: [nq][gridDim.y * TC_PARTS] appended counts (may exceed cap)
-    uint32_t* list_k;    // [nq][gridDim.y * TC_PARTS][cap or TC_TOPT] keys of d~
+    int cap;             // GEMM_FILTER: capacity of each (query, segment, part) list
+    int* cnt;            // GEMM_FILTER: [nq][maxseg * TC_PARTS] appended counts (may exceed cap)
+    uint32_t* list_k;    // [nq][maxseg * TC_PARTS][cap or T] keys of d~
     int32_t* list_i;     // same shape: centroid ids
     int* err;
 };
 
 enum { GEMM_MATRIX = 0, GEMM_FILTER = 1, GEMM_TOPK = 2 };
-constexpr int TC_TOPT = 8;      // GEMM_TOPK: approximate candidates kept per (query, column run, part)
 constexpr int TC_TOPK_MAXP = 4;  // top_m up to which the single-pass GEMM_TOPK path runs
 
-// v[j] for a lane-varying j by a four-level select tree: every index is
+// Candidates kept per (query, segment, part) list in the single-pass path:
+// P + 2 or more, so that the list's largest kept value usually lies well above
+// the P-th distance and the certificate holds.
+__host__ __device__ constexpr int topk_len(int P) { return P <= 2 ? 4 : 8; }
+
+// v[j] for a lane-varying j by a five-level select tree: every index is
 // static, so v stays in registers.
-__device__ __forceinline__ float select16(const float (&v)[16], int j) {
-    float a[8], b[4], c[2];
+__device__ __forceinline__ float select32(const float (&v)[32], int j) {
+    float a[16], b[8], c[4], d[2];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) a[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
+    for (int t = 0; t < 16; ++t) a[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) b[t] = (j & 2) ? a[2 * t + 1] : a[2 * t];
+    for (int t = 0; t < 8; ++t) b[t] = (j & 2) ? a[2 * t + 1] : a[2 * t];
 #pragma unroll
-    for (int t = 0; t < 2; ++t) c[t] = (j & 4) ? b[2 * t + 1] : b[2 * t];
-    return (j & 8) ? c[1] : c[0];
+    for (int t = 0; t < 4; ++t) c[t] = (j & 4) ? b[2 * t + 1] : b[2 * t];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) d[t] = (j & 8) ? c[2 * t + 1] : c[2 * t];
+    return (j & 16) ? d[1] : d[0];
 }
 
 // Insert x into the ascending list bd (x < bd[T-1]); equal keys keep their
@@ -134,59 +154,64 @@ __device__ __forceinline__ void insert_sorted(float (&bd)[T], int32_t (&bi)[T], 
     bi[0] = lt[0] ? xi : bi[0];
 }
 
-// Ascending bitonic sorting network over 16 (value, column) pairs in registers.
-__device__ __forceinline__ void sort16(float (&v)[16], int32_t (&id)[16]) {
+// Minimum of 32 values by a tree.
+__device__ __forceinline__ float min32(const float (&v)[32]) {
+    float m[16];
 #pragma unroll
-    for (int k = 2; k <= 16; k <<= 1) {
+    for (int j = 0; j < 16; ++j) m[j] = fminf(v[j], v[j + 16]);
 #pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
+    for (int w = 8; w; w >>= 1)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int l = i ^ j;
-                if (l > i) {
-                    const bool up = (i & k) == 0;
-                    const bool sw = up ? (v[i] > v[l]) : (v[i] < v[l]);
-                    const float a = v[i], b = v[l];
-                    const int32_t ia = id[i], ib = id[l];
-                    v[i] = sw ? b : a;
-                    v[l] = sw ? a : b;
-                    id[i] = sw ? ib : ia;
-                    id[l] = sw ? ia : ib;
-                }
-            }
+        for (int j = 0; j < w; ++j) m[j] = fminf(m[j], m[j + w]);
+    return m[0];
+}
+
+// Norms of the 32 columns col0.. (0 past ncols), from shared or global memory.
+__device__ __forceinline__ void load_norms(const float* cn, int col0, int ncols, float (&c)[32]) {
+    if (col0 + 32 <= ncols) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(cn + col0 + j);
+            c[j] = c4.x;
+            c[j + 1] = c4.y;
+            c[j + 2] = c4.z;
+            c[j + 3] = c4.w;
         }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) c[j] = (col0 + j < ncols) ? cn[col0 + j] : 0.0f;
     }
 }
 
-template <int MODE>
+template <int MODE, int T>
 __global__ void __launch_bounds__(TC_NT, 1)
     coarse_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                        const GemmArgs g) {
     extern __shared__ __align__(1024) unsigned char dsmem[];
-    __shared__ __align__(8) uint64_t a_full, b_full[2], b_empty[2], acc_full[2], acc_empty[2];
+    __shared__ __align__(8) uint64_t a_full, a_empty, b_full[TC_NST], b_empty[TC_NST], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int s_fail;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ntiles = (g.ncols + TC_N - 1) / TC_N;
-    const int tile0 = blockIdx.y * g.tiles_per_cta;
-    const int nt = min(ntiles, tile0 + g.tiles_per_cta) - tile0;
-    if (nt <= 0) return;  // uniform for the whole CTA
+    const long long p0 = (long long)blockIdx.x * g.per_cta;
+    const long long p1 = p0 + g.per_cta < g.total ? p0 + g.per_cta : g.total;
+    if (p0 >= p1) return;  // uniform for the whole CTA
     constexpr int A_KB = TC_M * TC_KB * 2;  // 16 KB per K block
-    constexpr int B_KB = TC_N * TC_KB * 2;  // 8 KB per K block
+    constexpr int B_KB = TC_N * TC_KB * 2;  // 16 KB per K block
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
     unsigned char* sa = base;
     unsigned char* sb = base + g.kt * A_KB;
-    const int stage_bytes = g.kt * B_KB;
-    float* sn = reinterpret_cast<float*>(sb + 2 * stage_bytes);  // [nt * TC_N] column norms
-    const int m0 = blockIdx.x * TC_M;
+    float* sn = reinterpret_cast<float*>(sb + TC_NST * B_KB);  // [ncols] norms when staged
 
     if (tid == 0) {
         s_fail = 0;
         tc::mbar_init(&a_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        tc::mbar_init(&a_empty, 1);
+        for (int i = 0; i < TC_NST; ++i) {
             tc::mbar_init(&b_full[i], 1);
             tc::mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&acc_full[i], 1);
             tc::mbar_init(&acc_empty[i], TC_EPI_WARPS * 32);
         }
@@ -204,95 +229,141 @@ __global__ void __launch_bounds__(TC_NT, 1)
 
     if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
-            tc::mbar_arrive_expect_tx(&a_full, (uint32_t)(g.kt * A_KB));
-            for (int k = 0; k < g.kt; ++k)
-                tc::tma_load_2d(sa + k * A_KB, &ta, &a_full, k * TC_KB, (int)(g.q0 + m0));
-            for (int i = 0; i < nt; ++i) {
-                const int s = i & 1;
-                if (!tc::mbar_wait_or_fail(&b_empty[s], ((i >> 1) & 1) ^ 1, fail)) break;
-                tc::mbar_arrive_expect_tx(&b_full[s], (uint32_t)stage_bytes);
-                const int col0 = (tile0 + i) * TC_N;
-                for (int k = 0; k < g.kt; ++k)
-                    tc::tma_load_2d(sb + s * stage_bytes + k * B_KB, &tb, &b_full[s], k * TC_KB, col0);
+            long long cur = -1;
+            int na = 0;
+            long long kb = 0;
+            for (long long pi = p0; pi < p1; ++pi) {
+                const long long mt = pi / g.ntiles;
+                const int t = (int)(pi - mt * g.ntiles);
+                if (mt != cur) {
+                    if (na > 0 && !tc::mbar_wait_or_fail(&a_empty, (na - 1) & 1, fail)) break;
+                    tc::mbar_arrive_expect_tx(&a_full, (uint32_t)(g.kt * A_KB));
+                    for (int k = 0; k < g.kt; ++k)
+                        tc::tma_load_2d(sa + k * A_KB, &ta, &a_full, k * TC_KB, (int)(g.q0 + mt * TC_M));
+                    ++na;
+                    cur = mt;
+                }
+                bool ok = true;
+                for (int k = 0; k < g.kt; ++k, ++kb) {
+                    const int st = (int)(kb % TC_NST);
+                    if (!tc::mbar_wait_or_fail(&b_empty[st], (uint32_t)(((kb / TC_NST) & 1) ^ 1), fail)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&b_full[st], (uint32_t)B_KB);
+                    tc::tma_load_2d(sb + st * B_KB, &tb, &b_full[st], k * TC_KB, t * TC_N);
+                }
+                if (!ok) break;
             }
         }
     } else if (warp == 1) {
-        if (lane == 0 && tc::mbar_wait_or_fail(&a_full, 0, fail)) {  // ---- MMA issuer
+        if (lane == 0) {  // ---- MMA issuer
             constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_M, TC_N);
-            for (int i = 0; i < nt; ++i) {
-                const int s = i & 1, acc = i & 1, ph = (i >> 1) & 1;
-                if (!tc::mbar_wait_or_fail(&b_full[s], ph, fail)) break;
-                if (!tc::mbar_wait_or_fail(&acc_empty[acc], ph ^ 1, fail)) break;
+            long long cur = -1;
+            int na = 0;
+            long long kb = 0;
+            int li = 0;
+            for (long long pi = p0; pi < p1; ++pi, ++li) {
+                const long long mt = pi / g.ntiles;
+                if (mt != cur) {
+                    if (!tc::mbar_wait_or_fail(&a_full, na & 1, fail)) break;
+                    ++na;
+                    cur = mt;
+                }
+                const int acc = li & 1;
+                if (!tc::mbar_wait_or_fail(&acc_empty[acc], ((li >> 1) & 1) ^ 1, fail)) break;
                 tc::fence_after_sync();
-                for (int k = 0; k < g.kt; ++k) {
+                bool ok = true;
+                for (int k = 0; k < g.kt; ++k, ++kb) {
+                    const int st = (int)(kb % TC_NST);
+                    if (!tc::mbar_wait_or_fail(&b_full[st], (uint32_t)((kb / TC_NST) & 1), fail)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
                     const uint64_t da = tc::desc_kmajor_sw128(sa + k * A_KB);
-                    const uint64_t db = tc::desc_kmajor_sw128(sb + s * stage_bytes + k * B_KB);
+                    const uint64_t db = tc::desc_kmajor_sw128(sb + st * B_KB);
 #pragma unroll
                     for (int kk = 0; kk < TC_KB / 16; ++kk)
                         tc::umma_bf16(taddr + (uint32_t)(acc * TC_N), da + 2 * kk, db + 2 * kk, idesc,
                                       (k | kk) != 0);
+                    tc::umma_commit(&b_empty[st]);  // the stage may be refilled once these MMAs finish
                 }
-                tc::umma_commit(&b_empty[s]);    // the B stage may be refilled once these MMAs finish
-                tc::umma_commit(&acc_full[acc]);  // and the accumulator is ready for the epilogue
+                if (!ok) break;
+                tc::umma_commit(&acc_full[acc]);  // the accumulator is ready for the epilogue
+                if (pi + 1 == p1 || (pi + 1) / g.ntiles != mt) tc::umma_commit(&a_empty);  // last use of this A
             }
         }
     } else {  // ---- epilogue warps 2..17
-        {
-            const int c0 = tile0 * TC_N, ncn = nt * TC_N;
-            for (int t = tid - 64; t < ncn; t += TC_EPI_WARPS * 32)
-                sn[t] = (c0 + t < g.ncols) ? __ldg(g.cn + c0 + t) : 0.0f;
+        const int q4 = warp & 3;
+        const int part = (warp - 2) >> 2;  // which 32 columns of each tile
+        long long cur = -1;
+        int row = 0;
+        bool valid = false;
+        long long qg = 0, lidx = 0;
+        float qnr = 0.0f, bound = 0.0f;
+        int n = 0;
+        bool first = true;
+        // GEMM_TOPK: the T smallest u = cn - 2 dp of this thread's columns in the
+        // segment, ascending.  u orders the columns as d~ = qn + u does (qn is
+        // constant per thread and adding it is monotone); qn is added when written.
+        float bd[T];
+        int32_t bi[T];
+        auto flush = [&]() {
+            if (!valid) return;
+            if (MODE == GEMM_FILTER) g.cnt[lidx] = n;
+            if (MODE == GEMM_TOPK) {
+                const long long o = lidx * (long long)T;
+#pragma unroll
+                for (int t = 0; t < T; ++t) {
+                    g.list_k[o + t] = bi[t] >= 0 ? f2key(qnr + bd[t]) : 0xffffffffu;
+                    g.list_i[o + t] = bi[t];
+                }
+            }
+        };
+        // column norms: every one staged in shared memory once when they fit,
+        // else read per tile from global memory
+        const bool staged = g.ncols <= TC_NORM_STAGE;
+        if (staged) {
+            for (int i = tid - 64; i < g.ncols; i += TC_EPI_WARPS * 32) sn[i] = __ldg(g.cn + i);
             tc::named_bar_sync(1, TC_EPI_WARPS * 32);
         }
-        const int q4 = warp & 3;
-        const int part = (warp - 2) >> 2;  // which 16 columns of each tile
-        const int row = m0 + q4 * 32 + lane;
-        const bool valid = row < g.nq;
-        const long long qg = g.q0 + row;
-        const float qnr = valid ? g.qn[qg] : 0.0f;
-        const float bound = (MODE == GEMM_FILTER && valid) ? g.tq[qg] : 0.0f;
-        // each (query, column run, part) belongs to exactly one thread: its segment needs no atomics
-        const long long lidx = (qg * gridDim.y + blockIdx.y) * TC_PARTS + part;
-        const long long seg = lidx * (long long)g.cap;
-        int n = 0;
-        // GEMM_TOPK: the TC_TOPT smallest u = cn - 2 dp of this thread's columns,
-        // ascending.  u orders the columns as d~ = qn + u does (qn is constant
-        // per thread and adding it is monotone); qn is added when written out.
-        float bd[TC_TOPT];
-        int32_t bi[TC_TOPT];
-#pragma unroll
-        for (int t = 0; t < TC_TOPT; ++t) {
-            bd[t] = INFINITY;
-            bi[t] = -1;
-        }
-        for (int i = 0; i < nt; ++i) {
-            const int acc = i & 1, ph = (i >> 1) & 1;
+        const float* cnp = staged ? sn : g.cn;
+        int li = 0;
+        for (long long pi = p0; pi < p1; ++pi, ++li) {
+            const long long mt = pi / g.ntiles;
+            const int t = (int)(pi - mt * g.ntiles);
+            if (mt != cur) {
+                flush();
+                cur = mt;
+                row = (int)(mt * TC_M) + q4 * 32 + lane;
+                valid = row < g.nq;
+                qg = g.q0 + row;
+                qnr = valid ? g.qn[qg] : 0.0f;
+                bound = (MODE == GEMM_FILTER && valid) ? g.tq[qg] : 0.0f;
+                const long long first_cta = (mt * g.ntiles) / g.per_cta;
+                lidx = (qg * g.maxseg + ((long long)blockIdx.x - first_cta)) * TC_PARTS + part;
+                n = 0;
+                first = true;
+            }
+            const int acc = li & 1, ph = (li >> 1) & 1;
             if (!__all_sync(0xffffffffu, tc::mbar_wait_or_fail(&acc_full[acc], ph, fail))) break;
             tc::fence_after_sync();
-            float v[TC_CPW];
-            tc::tmem_ld_32x16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + part * TC_CPW), v);
+            float v[32];
+            tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + part * TC_CPW), v);
             tc::fence_before_sync();
             tc::mbar_arrive(&acc_empty[acc]);
             // GEMM_TOPK keeps every lane in the loop: its candidate rounds are warp-collective
             if (!valid && MODE != GEMM_TOPK) continue;
-            const int col0 = (tile0 + i) * TC_N + part * TC_CPW;
+            const int col0 = t * TC_N + part * TC_CPW;
             const int ncol = min(TC_CPW, g.ncols - col0);
-            float c[TC_CPW];
-            {
-                const float4* s4 = reinterpret_cast<const float4*>(sn + i * TC_N + part * TC_CPW);
-#pragma unroll
-                for (int j = 0; j < TC_CPW / 4; ++j) {
-                    const float4 x = s4[j];
-                    c[4 * j] = x.x;
-                    c[4 * j + 1] = x.y;
-                    c[4 * j + 2] = x.z;
-                    c[4 * j + 3] = x.w;
-                }
-            }
+            float c[32];
+            load_norms(cnp, col0, g.ncols, c);
             if (MODE == GEMM_MATRIX) {
                 uint32_t* o = g.out + (long long)row * g.ldo + col0;
                 if (ncol == TC_CPW && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
 #pragma unroll
-                    for (int j = 0; j < TC_CPW; j += 4) {
+                    for (int j = 0; j < 32; j += 4) {
                         uint4 k4;
                         k4.x = f2key(qnr + c[j] - 2.0f * v[j]);
                         k4.y = f2key(qnr + c[j + 1] - 2.0f * v[j + 1]);
@@ -302,36 +373,34 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < TC_CPW; ++j)
+                    for (int j = 0; j < 32; ++j)
                         if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
                 }
             } else if (MODE == GEMM_TOPK) {
 #pragma unroll
-                for (int j = 0; j < TC_CPW; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
-                if (i == 0) {
-                    // the first chunk fills the list through a sorting network
-                    int32_t id[TC_CPW];
+                for (int j = 0; j < 32; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
+                if (first) {
+                    // fill the list from the segment's first chunk: T rounds of
+                    // taking out the minimum (lowest column first on equal values)
 #pragma unroll
-                    for (int j = 0; j < TC_CPW; ++j) id[j] = col0 + j;
-                    sort16(v, id);
+                    for (int r = 0; r < T; ++r) {
+                        const float mn = min32(v);
+                        unsigned em = 0;
 #pragma unroll
-                    for (int t = 0; t < TC_TOPT; ++t) {
-                        bd[t] = v[t];
-                        bi[t] = v[t] < INFINITY ? id[t] : -1;
+                        for (int j = 0; j < 32; ++j) em |= (v[j] == mn) ? (1u << j) : 0u;
+                        const int jm = __ffs(em) - 1;
+                        bd[r] = mn;
+                        bi[r] = (mn < INFINITY) ? col0 + jm : -1;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = (j == jm) ? INFINITY : v[j];
                     }
+                    first = false;
                     continue;
                 }
-                float m[TC_CPW / 2];
-#pragma unroll
-                for (int j = 0; j < TC_CPW / 2; ++j) m[j] = fminf(v[2 * j], v[2 * j + 1]);
-#pragma unroll
-                for (int w = TC_CPW / 4; w; w >>= 1)
-#pragma unroll
-                    for (int j = 0; j < w; ++j) m[j] = fminf(m[j], m[j + w]);
                 unsigned cand = 0;
-                if (valid && m[0] < bd[TC_TOPT - 1]) {
+                if (valid && min32(v) < bd[T - 1]) {
 #pragma unroll
-                    for (int j = 0; j < TC_CPW; ++j) cand |= (v[j] < bd[TC_TOPT - 1]) ? (1u << j) : 0u;
+                    for (int j = 0; j < 32; ++j) cand |= (v[j] < bd[T - 1]) ? (1u << j) : 0u;
                 }
                 // one candidate per lane per round: the warp runs as many rounds as
                 // its busiest lane has candidates (one or two once the lists fill)
@@ -339,24 +408,24 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     if (cand) {
                         const int j = __ffs(cand) - 1;
                         cand &= cand - 1u;
-                        const float x = select16(v, j);
-                        if (x < bd[TC_TOPT - 1]) insert_sorted(bd, bi, x, col0 + j);
+                        const float x = select32(v, j);
+                        if (x < bd[T - 1]) insert_sorted<T>(bd, bi, x, col0 + j);
                     }
                 }
             } else {
                 unsigned pass = 0;
 #pragma unroll
-                for (int j = 0; j < TC_CPW; ++j) {
+                for (int j = 0; j < 32; ++j) {
                     v[j] = qnr + c[j] - 2.0f * v[j];
                     pass |= (j < ncol && v[j] <= bound) ? (1u << j) : 0u;
                 }
                 if (pass) {
 #pragma unroll
-                    for (int j = 0; j < TC_CPW; ++j) {
+                    for (int j = 0; j < 32; ++j) {
                         if (pass & (1u << j)) {
                             if (n < g.cap) {
-                                g.list_k[seg + n] = f2key(v[j]);
-                                g.list_i[seg + n] = col0 + j;
+                                g.list_k[lidx * g.cap + n] = f2key(v[j]);
+                                g.list_i[lidx * g.cap + n] = col0 + j;
                             }
                             ++n;
                         }
@@ -364,15 +433,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 }
             }
         }
-        if (MODE == GEMM_FILTER && valid) g.cnt[lidx] = n;
-        if (MODE == GEMM_TOPK && valid) {
-            const long long o = lidx * (long long)TC_TOPT;
-#pragma unroll
-            for (int t = 0; t < TC_TOPT; ++t) {
-                g.list_k[o + t] = bi[t] >= 0 ? f2key(qnr + bd[t]) : 0xffffffffu;
-                g.list_i[o + t] = bi[t];
-            }
-        }
+        flush();
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -560,22 +621,23 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
     }
 }
 
-// Warp per query, single-pass path: the TC_TOPT smallest d~ of every (column
-// run, half) list are rescored exactly and sorted by (distance, id).  Every
+// Warp per query, single-pass path: the topt smallest d~ of every (segment,
+// part) list are rescored exactly and sorted by (distance, id).  Every
 // centroid outside a full list has d~ >= that list's largest kept d~, so with
 // B = the smallest such value over the full lists, the first P are the exact
 // top-P when their P-th distance is below B - E.  Otherwise every centroid is
 // rescored through the warp's scratch row.
 __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_topk_finish_kernel(
     const float* __restrict__ centroids, int nlist, int dim, const float* __restrict__ queries, int nq, int nlists,
-    const uint32_t* __restrict__ list_k, const int32_t* __restrict__ list_i, int P, const float* __restrict__ qn,
+    int topt, const uint32_t* __restrict__ list_k, const int32_t* __restrict__ list_i, int P,
+    const float* __restrict__ qn,
     const unsigned* __restrict__ max_cn_bits, const int* __restrict__ err, uint32_t* __restrict__ fb,
     uint32_t* __restrict__ out_ids, float* __restrict__ out_d, int* __restrict__ n_fallback) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * FIN_WARPS + w;
     if (q >= nq) return;
-    const int ncand = nlists * TC_TOPT;
+    const int ncand = nlists * topt;
     const int cpow = next_pow2(ncand);
     const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(P)};
     // per warp: query, histogram (fallback select), candidate keys [cpow]
@@ -589,7 +651,7 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_topk_finish_kernel(
     // every centroid of its columns)
     float B = INFINITY;
     for (int l = lane; l < nlists; l += 32) {
-        const size_t o = ((size_t)q * nlists + l) * TC_TOPT + (TC_TOPT - 1);
+        const size_t o = ((size_t)q * nlists + l) * topt + (topt - 1);
         if (list_i[o] >= 0) B = fminf(B, key2f(list_k[o]));
     }
 #pragma unroll
@@ -711,36 +773,41 @@ bool coarse_tc_supported(int dim, int P) {
 }
 
 namespace {
+// Persistent GEMM grid: the (query tile, centroid tile) pairs split into
+// contiguous ranges of `per_cta`, one per CTA, at most one CTA per SM.
+struct GemmGrid {
+    int ntiles;       // centroid tiles
+    long long total;  // pairs
+    int per_cta, ctas, maxseg;
+};
+
+GemmGrid gemm_grid(long long nq, int ncols) {
+    GemmGrid gg;
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) !=
+                                                      cudaSuccess || nsm <= 0)
+            nsm = 148;
+    }
+    const long long mtiles = (std::max(nq, 1ll) + TC_M - 1) / TC_M;
+    gg.ntiles = (ncols + TC_N - 1) / TC_N;
+    gg.total = mtiles * gg.ntiles;
+    gg.per_cta = (int)((gg.total + nsm - 1) / nsm);
+    gg.ctas = (int)((gg.total + gg.per_cta - 1) / gg.per_cta);
+    // a query tile's ntiles pairs touch at most ceil(ntiles / L) + 1 ranges
+    gg.maxseg = std::min(gg.ctas, (gg.ntiles + gg.per_cta - 1) / gg.per_cta + 1);
+    return gg;
+}
+
 struct CoarsePlan {
     int S;       // exactly rescored superset
     int NS;      // prefix of centroids whose S-th smallest d~ bounds the S-th over all
-    int cap;     // capacity of one (query, column run) segment
-    int gy1;     // column runs of pass 1
-    int tpc1;    // 64-column tiles per run
+    int cap;     // capacity of one (query, segment, part) list
+    GemmGrid g1;  // the pass over every centroid
+    int nlists;   // lists per query: g1.maxseg * TC_PARTS
     int fin_cta;
 };
-
-// Column runs per query tile.  One CTA fills an SM (its shared memory holds the
-// whole query tile and two centroid stages), so the grid runs in waves of 148
-// CTAs; the split minimises waves x (tiles per CTA + a fixed per-CTA cost of
-// about two tiles for the query-tile load and the pipeline fill).
-void col_split(int mtiles, int ntiles, int& gy, int& tpc) {
-    constexpr int kSMs = 148, kCtaCost = 2;
-    long long best = -1;
-    gy = (ntiles + TC_MAX_TPC - 1) / TC_MAX_TPC;
-    tpc = (ntiles + gy - 1) / gy;
-    for (int want = (ntiles + TC_MAX_TPC - 1) / TC_MAX_TPC; want <= std::min(ntiles, 1024); ++want) {
-        const int t = (ntiles + want - 1) / want;
-        const int runs = (ntiles + t - 1) / t;
-        const long long waves = ((long long)mtiles * runs + kSMs - 1) / kSMs;
-        const long long cost = waves * (t + kCtaCost);
-        if (best < 0 || cost < best) {
-            best = cost;
-            gy = runs;
-            tpc = t;
-        }
-    }
-}
 
 CoarsePlan coarse_plan(long long nq, int nlist, int P) {
     CoarsePlan c;
@@ -749,10 +816,10 @@ CoarsePlan coarse_plan(long long nq, int nlist, int P) {
     ns = (ns + TC_N - 1) / TC_N * TC_N;
     c.NS = std::min(nlist, std::min(ns, 8192));
     const long long expect = (long long)c.S * nlist / c.NS;
-    const int mtiles = (int)((std::max(nq, 1ll) + TC_M - 1) / TC_M);
-    col_split(mtiles, (nlist + TC_N - 1) / TC_N, c.gy1, c.tpc1);
+    c.g1 = gemm_grid(nq, nlist);
+    c.nlists = c.g1.maxseg * TC_PARTS;
     c.cap = (int)std::min<long long>(FIN_TOT, std::max<long long>(4 * expect, c.S + 256));
-    c.cap = std::min(c.cap, c.tpc1 * TC_CPW);
+    c.cap = std::min(c.cap, std::max(topk_len(TC_TOPK_MAXP), std::min(c.g1.per_cta, c.g1.ntiles) * TC_CPW));
     c.fin_cta = (int)((std::max(nq, 1ll) + FIN_WARPS - 1) / FIN_WARPS);
     return c;
 }
@@ -765,8 +832,8 @@ size_t coarse_tc_workspace(long long nq, int nlist, int dim, int P) {
     b += round_up(round_up((size_t)nq, TC_TILE) * kpad * 2, 256) + round_up(round_up((size_t)nlist, TC_TILE) * kpad * 2, 256);
     b += round_up((size_t)nq * 4, 256) * 2 + round_up((size_t)nlist * 4, 256) + 256 * 3;
     b += round_up((size_t)nq * round_up(c.NS, 4) * 4, 256);     // prefix keys
-    b += round_up((size_t)nq * c.gy1 * TC_PARTS * 4, 256);             // segment counts
-    b += round_up((size_t)nq * c.gy1 * TC_PARTS * c.cap * 4, 256) * 2; // segments
+    b += round_up((size_t)nq * c.nlists * 4, 256);              // list counts
+    b += round_up((size_t)nq * c.nlists * c.cap * 4, 256) * 2;  // lists
     b += round_up((size_t)c.fin_cta * FIN_WARPS * nlist * 4, 256);  // fallback rows
     return b + 4096;
 }
@@ -792,9 +859,9 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     int* nfb = cv.take<int>(4);
     const long long ldm = (long long)round_up((size_t)c.NS, 4);
     uint32_t* M0 = cv.take<uint32_t>((size_t)nq * ldm);
-    int* cnt = cv.take<int>((size_t)nq * c.gy1 * TC_PARTS);
-    uint32_t* lk = cv.take<uint32_t>((size_t)nq * c.gy1 * TC_PARTS * c.cap);
-    int32_t* li = cv.take<int32_t>((size_t)nq * c.gy1 * TC_PARTS * c.cap);
+    int* cnt = cv.take<int>((size_t)nq * c.nlists);
+    uint32_t* lk = cv.take<uint32_t>((size_t)nq * c.nlists * c.cap);
+    int32_t* li = cv.take<int32_t>((size_t)nq * c.nlists * c.cap);
     uint32_t* fb = cv.take<uint32_t>((size_t)c.fin_cta * FIN_WARPS * nlist);
     if (!cv.ok()) return fail(FG_ERR_WORKSPACE, "coarse workspace too small (%zu < %zu)", ws_bytes,
                               coarse_tc_workspace(nq, nlist, dim, P));
@@ -812,38 +879,49 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     CUtensorMap ta, tb;
     if ((rc = make_map(&ta, A, nq_pad, kpad, TC_M))) return rc;
     if ((rc = make_map(&tb, B, nl_pad, kpad, TC_N))) return rc;
-    const int smem = 1024 + kt * TC_M * TC_KB * 2 + 2 * kt * TC_N * TC_KB * 2 + TC_MAX_TPC * TC_N * 4;
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_MATRIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
-    const int mtiles = (int)((nq + TC_M - 1) / TC_M);
+    const int smem_base = 1024 + kt * TC_M * TC_KB * 2 + TC_NST * TC_N * TC_KB * 2;
+    // the staged norms of the pass over every centroid (pass 0 covers a prefix)
+    const int smem = smem_base + (nlist <= TC_NORM_STAGE ? nlist * 4 : 0);
 
-    const int topk_fsm = FIN_WARPS * ((dim + 3) / 4 * 4 * 4 + 256 * 4 + next_pow2(c.gy1 * TC_PARTS * TC_TOPT) * 8);
+    GemmArgs g{};
+    g.kt = kt;
+    g.q0 = 0;
+    g.nq = (int)nq;
+    g.qn = qn;
+    g.cn = cn;
+    g.err = err;
+    auto set_grid = [&](const GemmGrid& gg, int ncols) {
+        g.ncols = ncols;
+        g.ntiles = gg.ntiles;
+        g.total = gg.total;
+        g.per_cta = gg.per_cta;
+        g.maxseg = gg.maxseg;
+    };
+
+    const int T = topk_len(P);
+    const int topk_fsm = FIN_WARPS * ((dim + 3) / 4 * 4 * 4 + 256 * 4 + next_pow2(c.nlists * T) * 8);
     if (P <= TC_TOPK_MAXP && topk_fsm <= 227 * 1024) {
-        // single pass: each (query, column run, half) keeps its TC_TOPT smallest
-        // d~ in registers; a warp per query rescores and certifies them
-        FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem));
-        GemmArgs g{};
-        g.kt = kt;
-        g.q0 = 0;
-        g.nq = (int)nq;
-        g.qn = qn;
-        g.cn = cn;
-        g.err = err;
-        g.ncols = nlist;
-        g.tiles_per_cta = c.tpc1;
+        // single pass: each (query, segment, part) keeps its T smallest d~ in
+        // registers; a warp per query rescores and certifies them.  Lists of
+        // segments that no CTA covers stay empty (ids -1).
+        FG_CUDA_TRY(cudaMemsetAsync(li, 0xff, (size_t)nq * c.nlists * T * sizeof(int32_t), s));
+        set_grid(c.g1, nlist);
         g.list_k = lk;
         g.list_i = li;
-        coarse_gemm_kernel<GEMM_TOPK><<<dim3(mtiles, c.gy1), TC_NT, smem, s>>>(ta, tb, g);
+        if (T == 4) {
+            FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK, 4>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            coarse_gemm_kernel<GEMM_TOPK, 4><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
+        } else {
+            FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK, 8>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            coarse_gemm_kernel<GEMM_TOPK, 8><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
+        }
         if ((rc = check_launch("coarse_gemm_kernel(top-k)"))) return rc;
-        const int nlists = c.gy1 * TC_PARTS;
-        const int fsm = topk_fsm;
-        FG_CUDA_TRY(cudaFuncSetAttribute(coarse_topk_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fsm));
-        coarse_topk_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fsm, s>>>(centroids, nlist, dim, queries, (int)nq,
-                                                                        nlists, lk, li, P, qn, maxc, err, fb,
-                                                                        out_ids, out_d, nfb);
+        FG_CUDA_TRY(
+            cudaFuncSetAttribute(coarse_topk_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, topk_fsm));
+        coarse_topk_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, topk_fsm, s>>>(
+            centroids, nlist, dim, queries, (int)nq, c.nlists, T, lk, li, P, qn, maxc, err, fb, out_ids, out_d, nfb);
         if ((rc = check_launch("coarse_topk_finish_kernel"))) return rc;
         if (n_fallback_host) {
             FG_CUDA_TRY(cudaMemcpyAsync(n_fallback_host, nfb, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -853,34 +931,31 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     }
 
     // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
-    GemmArgs g{};
-    g.kt = kt;
-    g.q0 = 0;
-    g.nq = (int)nq;
-    g.qn = qn;
-    g.cn = cn;
-    g.err = err;
-    g.ncols = c.NS;
-    int gy0, tpc0;
-    col_split(mtiles, (c.NS + TC_N - 1) / TC_N, gy0, tpc0);
-    g.tiles_per_cta = tpc0;
+    const int smem0 = smem_base + (c.NS <= TC_NORM_STAGE ? c.NS * 4 : 0);
+    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_MATRIX, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem0));
+    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+    const GemmGrid g0 = gemm_grid(nq, c.NS);
+    set_grid(g0, c.NS);
     g.out = M0;
     g.ldo = ldm;
-    coarse_gemm_kernel<GEMM_MATRIX><<<dim3(mtiles, gy0), TC_NT, smem, s>>>(ta, tb, g);
+    coarse_gemm_kernel<GEMM_MATRIX, 1><<<g0.ctas, TC_NT, smem0, s>>>(ta, tb, g);
     if ((rc = check_launch("coarse_gemm_kernel(prefix)"))) return rc;
     coarse_bound_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(M0, c.NS, ldm, (int)nq, c.S, tq);
     if ((rc = check_launch("coarse_bound_kernel"))) return rc;
 
     // pass 1: every centroid; each query row appends those within its bound
-    g.ncols = nlist;
-    g.tiles_per_cta = c.tpc1;
+    // (counts of segments that no CTA covers stay 0)
+    FG_CUDA_TRY(cudaMemsetAsync(cnt, 0, (size_t)nq * c.nlists * sizeof(int), s));
+    set_grid(c.g1, nlist);
     g.out = nullptr;
     g.tq = tq;
     g.cap = c.cap;
     g.cnt = cnt;
     g.list_k = lk;
     g.list_i = li;
-    coarse_gemm_kernel<GEMM_FILTER><<<dim3(mtiles, c.gy1), TC_NT, smem, s>>>(ta, tb, g);
+    coarse_gemm_kernel<GEMM_FILTER, 1><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
     if ((rc = check_launch("coarse_gemm_kernel(filter)"))) return rc;
 
     // pass 2: select, rescore exactly, certify (or fall back)
@@ -888,8 +963,8 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     const int fin_smem = FIN_WARPS * FL.per_warp_bytes();
     FG_CUDA_TRY(cudaFuncSetAttribute(coarse_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem));
     coarse_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fin_smem, s>>>(centroids, nlist, dim, queries, (int)nq, cnt,
-                                                                     c.gy1 * TC_PARTS, lk, li, c.cap, c.S, P, qn, maxc, err, fb,
-                                                                     out_ids, out_d, nfb);
+                                                                     c.nlists, lk, li, c.cap, c.S, P, qn, maxc, err,
+                                                                     fb, out_ids, out_d, nfb);
     if ((rc = check_launch("coarse_finish_kernel"))) return rc;
     if (n_fallback_host) {
         FG_CUDA_TRY(cudaMemcpyAsync(n_fallback_host, nfb, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -141,6 +141,21 @@ def test_coarse_tc_odd_shapes(fg):
         np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
 
 
+def test_coarse_tc_ranges_cross_query_tiles(fg):
+    """40 query tiles x 8 centroid tiles = 320 (query tile, centroid tile)
+    pairs over at most 148 CTAs: ranges of 3 pairs start and end inside query
+    tiles, so CTAs reload the query tile and lists come from several segments."""
+    rng = np.random.default_rng(21)
+    cen = rng.normal(size=(1000, 64)).astype(np.float32)
+    q = rng.normal(size=(5000, 64)).astype(np.float32)
+    for top_m in (1, 2, 3, 16):
+        ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
+        eids, ed = oracle.coarse(cen, q, top_m)
+        np.testing.assert_array_equal(_np(d), ed)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+        assert nfb <= q.shape[0] // 20
+
+
 def test_coarse_tc_many_lists_two_stage(fg):
     """nlist above one select segment (8192): stage-2 merge in the superset select."""
     rng = np.random.default_rng(10)
