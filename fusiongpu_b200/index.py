@@ -316,6 +316,61 @@ class IVFPQIndex:
                   _p(ids), _p(dist), _p(ws), ws.numel(), _stream(stream))
         return ids, dist
 
+    def search_host(self, queries, params: SearchParams | None = None, out=None, chunks: int = 2):
+        """Search host-resident queries into host-resident results with the
+        copies overlapped: the batch is cut into `chunks` pieces on two
+        streams, each stream with its own device buffers and workspace, so one
+        piece's upload and download run on the copy engines while another
+        piece's kernels run.  Pinned host buffers keep the copies asynchronous;
+        `out` = (ids, dists) host tensors [nq][final_k].  Returns them once the
+        current stream has been made to wait for every piece (synchronise
+        before reading them on the host)."""
+        params = params or SearchParams()
+        if self.base is None:
+            raise ValueError("search needs the raw base vectors (build with keep_base=True)")
+        hq = torch.as_tensor(queries, dtype=torch.float32)
+        if hq.device.type != "cpu":
+            raise ValueError("search_host takes host queries")
+        nq = hq.shape[0]
+        if out is None:
+            out = (torch.empty((nq, params.final_k), dtype=torch.int32).pin_memory(),
+                   torch.empty((nq, params.final_k), dtype=torch.float32).pin_memory())
+        hid, hdd = out
+        chunks = max(1, min(int(chunks), nq)) if nq else 1
+        per = (nq + chunks - 1) // chunks if nq else 0
+        dev = self.device
+        key = (per, params.final_k, self.workspace_bytes(max(per, 1), params))
+        if getattr(self, "_host_state", None) is None or self._host_state[0] != key:
+            state = []
+            for _ in range(2):
+                state.append(dict(stream=torch.cuda.Stream(device=dev),
+                                  q=torch.empty((max(per, 1), self.dim), dtype=torch.float32, device=dev),
+                                  ids=torch.empty((max(per, 1), params.final_k), dtype=torch.int32, device=dev),
+                                  dd=torch.empty((max(per, 1), params.final_k), dtype=torch.float32, device=dev),
+                                  ws=_workspace(key[2], dev)))
+            self._host_state = (key, state)
+        state = self._host_state[1]
+        cur = torch.cuda.current_stream(dev)
+        for st in state:
+            st["stream"].wait_stream(cur)
+        cp = params.c()
+        fn = "fg_search_u8" if self.base.dtype == torch.uint8 else "fg_search"
+        for c in range(chunks):
+            lo, hi = c * per, min(nq, (c + 1) * per)
+            if lo >= hi:
+                break
+            n = hi - lo
+            st = state[c % 2]
+            with torch.cuda.stream(st["stream"]):
+                st["q"][:n].copy_(hq[lo:hi], non_blocking=True)
+                _lib.call(fn, C.byref(self._view), _p(self.base), self.base.shape[0], _p(st["q"]), n, C.byref(cp),
+                          _p(st["ids"]), _p(st["dd"]), _p(st["ws"]), st["ws"].numel(), _stream(st["stream"]))
+                hid[lo:hi].copy_(st["ids"][:n], non_blocking=True)
+                hdd[lo:hi].copy_(st["dd"][:n], non_blocking=True)
+        for st in state:
+            cur.wait_stream(st["stream"])
+        return hid, hdd
+
     def capture(self, nq: int, params: SearchParams | None = None) -> "SearchGraph":
         """A CUDA graph of one search of `nq` queries with these parameters,
         for replay in launch-bound (small-batch) serving: the search needs no

@@ -427,6 +427,21 @@ def test_sampled_kmeans_build_bit_exact(fg):
         np.testing.assert_array_equal(got[k], eidx[k])
 
 
+@pytest.mark.parametrize("chunks", [1, 2, 3])
+def test_search_host_matches_device_search(fg, chunks):
+    """The pipelined host-buffer search (pieces on two streams) returns the
+    device search's results."""
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    p = _params(fg, "c1", False)
+    ids, d = idx.search(q, p)
+    hq = torch.from_numpy(np.ascontiguousarray(q)).pin_memory()
+    hi, hd = idx.search_host(hq, p, chunks=chunks)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(hi.numpy(), _np(ids))
+    np.testing.assert_array_equal(hd.numpy(), _np(d))
+
+
 def test_search_graph_replay_matches_eager(fg):
     index, base, q = dataset("int128")
     idx = fg.IVFPQIndex.from_arrays(index, base)
