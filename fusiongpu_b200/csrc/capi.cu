@@ -36,7 +36,7 @@ int check_launch(const char* what) {
 
 // implemented in the kernel files
 int batch_logic(const fg_ivfpq_view*, const float*, int, const uint32_t*, const float*, const fg_search_params*,
-                int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad);
+                int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad, int* work_counter = nullptr);
 int rerank(const float*, int, int, const int32_t*, const int32_t*, const void*, int, long long,
            const fg_search_params*, int32_t*, float*, cudaStream_t);
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
@@ -111,7 +111,7 @@ struct SearchWs {
 static size_t search_fixed_bytes(int nq, const fg_search_params* p) {
     const size_t P = (size_t)p->top_m, R = (size_t)p->rerank_m;
     return round_up((size_t)nq * P * 4, 256) * 2 + round_up((size_t)nq * R * 4, 256) * 2 +
-           round_up((size_t)nq * 4, 256);
+           round_up((size_t)nq * 4, 256) + 256;  // + the scan's query counter
 }
 
 }  // namespace fg
@@ -241,13 +241,15 @@ static int search_any(const fg_ivfpq_view* index, const void* base, int base_u8,
     int32_t* tid = cv.take<int32_t>((size_t)nq * R);
     float* td = cv.take<float>((size_t)nq * R);
     int32_t* tc = cv.take<int32_t>((size_t)nq);
+    int* qctr = cv.take<int>(4);
     const size_t used = round_up(cv.used, 256);
     if (!cv.ok() || used >= ws_bytes) return fail(FG_ERR_WORKSPACE, "search workspace too small");
     rc = coarse(index->centroids, index->nlist, index->dim, queries, nq, params->top_m, pids, pd,
                 static_cast<char*>(ws) + used, ws_bytes - used, s);
     if (rc) return rc;
     // the rerank reads only the first top_counts[q] entries: skip the padding
-    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false);
+    FG_CUDA_TRY(cudaMemsetAsync(qctr, 0, sizeof(int), s));
+    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false, qctr);
     if (rc) return rc;
     return rerank(queries, nq, index->dim, tid, tc, base, base_u8, nbase, params, out_ids, out_dists, s);
 }

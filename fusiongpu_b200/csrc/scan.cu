@@ -45,6 +45,7 @@ struct ScanArgs {
     int top_m, p1, limit_k;
     float coeff, prune_ratio;
     int rerank_m, rsel, ref_compat, lmax, cap, sort_n;
+    int* work_counter;  // team kernel: zeroed counter for dynamic query fetching (null: static round robin)
     int small;      // team kernel: 1 when no query can emit more than rsel candidates (the buffer is never
                     // cut) and one warp selects each list; 2 the same with team-wide selection
     int write_pad;  // write (-1, FLT_MAX) / ref_compat zeros past each query's count
@@ -493,7 +494,7 @@ struct TeamMisc {
     uint32_t b[2];
     int carry[REF_BLOCK];
     unsigned char passf[NT];
-    int buf_n, count, nb_list;
+    int buf_n, count, nb_list, next_q;
     uint32_t prune_key;
     float thr;
 };
@@ -966,7 +967,9 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
     TeamMisc<NT>* ms = tb.ms;
     const int P = a.top_m;
 
-    for (int q = blockIdx.x * nteams + team; q < nq; q += gridDim.x * nteams) {
+    // first query by position, then (with a counter) whichever is next, so
+    // teams that drew cheap queries take more and the launch ends together
+    for (int q = blockIdx.x * nteams + team; q < nq;) {
         const float* qv = a.queries + (size_t)q * a.dim;
         // prune (gpu_global.cu:43-51); ids outside [0, nlist) are skipped
         const float best = a.probe_dists[(size_t)q * P];
@@ -1193,8 +1196,10 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
         if (tt == 0) {
             a.top_counts[q] = ak;
             if (a.cand_counts) a.cand_counts[q] = count;
+            ms->next_q = a.work_counter ? gridDim.x * nteams + atomicAdd(a.work_counter, 1) : q + gridDim.x * nteams;
         }
         team_sync<NT>(bar);  // the next query reuses every buffer
+        q = ms->next_q;
     }
 }
 
@@ -1240,7 +1245,7 @@ static ScanKernel pick_scan_kernel(int M, int SD) {
 int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uint32_t* probe_ids,
                 const float* probe_dists, const fg_search_params* p, int32_t* top_ids,
                 float* top_dists, int32_t* top_counts, int32_t* cand_counts, cudaStream_t stream,
-                bool write_pad) {
+                bool write_pad, int* work_counter) {
     FG_REQUIRE(ix && p, "null index or params");
     FG_REQUIRE(nq >= 0, "nq < 0");
     FG_REQUIRE(ix->dim > 0 && ix->pq_m > 0 && ix->dim % ix->pq_m == 0, "dim %d not divisible by pq_m %d",
@@ -1295,6 +1300,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.cand_counts = cand_counts;
     a.write_pad = write_pad ? 1 : 0;
     a.small = 0;
+    a.work_counter = work_counter;
 
     int dev = 0, smem_max = 0, smem_sm = 0;
     FG_CUDA_TRY(cudaGetDevice(&dev));
