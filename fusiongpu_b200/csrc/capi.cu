@@ -1,6 +1,8 @@
 // capi.cu -- the extern "C" entry points declared in include/fusiongpu.h.
 #include <algorithm>
 #include <cstdarg>
+#include <map>
+#include <mutex>
 #include <string>
 
 #include "fg_common.cuh"
@@ -32,6 +34,37 @@ int check_launch(const char* what) {
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
     return FG_OK;
+}
+
+namespace {
+std::mutex g_attr_mu;
+std::map<std::pair<int, int>, int> g_attr;           // (device, attribute) -> value
+std::map<std::pair<int, const void*>, int> g_smem;   // (device, function) -> granted bytes
+}  // namespace
+
+int device_attr(cudaDeviceAttr attr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    const auto key = std::make_pair(dev, (int)attr);
+    auto it = g_attr.find(key);
+    if (it != g_attr.end()) return it->second;
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, attr, dev) != cudaSuccess) return 0;
+    g_attr[key] = v;
+    return v;
+}
+
+cudaError_t ensure_smem(const void* func, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    int& granted = g_smem[std::make_pair(dev, func)];
+    if (bytes <= granted) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) granted = bytes;
+    return e;
 }
 
 // implemented in the kernel files

@@ -232,7 +232,7 @@ int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, i
     auto smem_for = [&](int len, int kk) { return round_up_dev(len * 4) + next_pow2(kk) * 8; };
     if (nseg == 1) {
         const int sm = smem_for(seg_len, k);
-        FG_CUDA_TRY(cudaFuncSetAttribute(topk_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&topk_segment_kernel), sm));
         topk_segment_kernel<<<dim3((unsigned)rows, 1), TK_NT, sm, s>>>(v, ldv, ncols, seg_len, nullptr, k,
                                                                       out_i, out_v, out_ld);
         return check_launch("topk_segment_kernel");
@@ -244,8 +244,7 @@ int rows_topk(const float* v, long long ldv, long long rows, int ncols, int k, i
     FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     if (sm > smem_max || sld > TK_STAGE_MAX)
         return fail(FG_ERR_UNSUPPORTED, "top-%d of %d columns per row is beyond the two-stage select", k, ncols);
-    FG_CUDA_TRY(cudaFuncSetAttribute(topk_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     std::max(sm, smem_for((int)sld, k))));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&topk_segment_kernel), std::max(sm, smem_for((int)sld, k))));
     topk_segment_kernel<<<dim3((unsigned)rows, nseg), TK_NT, sm, s>>>(v, ldv, ncols, seg_len, nullptr, k,
                                                                      stage_i, stage_v, sld);
     int rc = check_launch("topk_segment_kernel(stage 1)");

@@ -47,7 +47,6 @@ constexpr int TC_CPW = TC_N / TC_PARTS;  // 32 columns of each tile per epilogue
 constexpr int TC_EPI_WARPS = 4 * TC_PARTS;
 constexpr int TC_NT = 64 + TC_EPI_WARPS * 32;
 constexpr int TC_NORM_STAGE = 0;  // centroid norms staged in shared memory when ncols <= this
-constexpr int RS_NT = 256;
 
 __host__ __device__ inline int tc_kpad(int dim) { return (3 * dim + TC_KB - 1) / TC_KB * TC_KB; }
 
@@ -783,13 +782,8 @@ struct GemmGrid {
 
 GemmGrid gemm_grid(long long nq, int ncols) {
     GemmGrid gg;
-    static int nsm = 0;
-    if (!nsm) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) !=
-                                                      cudaSuccess || nsm <= 0)
-            nsm = 148;
-    }
+    int nsm = device_attr(cudaDevAttrMultiProcessorCount);
+    if (nsm <= 0) nsm = 148;
     const long long mtiles = (std::max(nq, 1ll) + TC_M - 1) / TC_M;
     gg.ntiles = (ncols + TC_N - 1) / TC_N;
     gg.total = mtiles * gg.ntiles;
@@ -909,17 +903,15 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
         g.list_k = lk;
         g.list_i = li;
         if (T == 4) {
-            FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK, 4>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 4>), smem));
             coarse_gemm_kernel<GEMM_TOPK, 4><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
         } else {
-            FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_TOPK, 8>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 8>), smem));
             coarse_gemm_kernel<GEMM_TOPK, 8><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
         }
         if ((rc = check_launch("coarse_gemm_kernel(top-k)"))) return rc;
         FG_CUDA_TRY(
-            cudaFuncSetAttribute(coarse_topk_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, topk_fsm));
+            ensure_smem(reinterpret_cast<const void*>(&coarse_topk_finish_kernel), topk_fsm));
         coarse_topk_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, topk_fsm, s>>>(
             centroids, nlist, dim, queries, (int)nq, c.nlists, T, lk, li, P, qn, maxc, err, fb, out_ids, out_d, nfb);
         if ((rc = check_launch("coarse_topk_finish_kernel"))) return rc;
@@ -932,10 +924,8 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
 
     // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
     const int smem0 = smem_base + (c.NS <= TC_NORM_STAGE ? c.NS * 4 : 0);
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_MATRIX, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem0));
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_gemm_kernel<GEMM_FILTER, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_MATRIX, 1>), smem0));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_FILTER, 1>), smem));
     const GemmGrid g0 = gemm_grid(nq, c.NS);
     set_grid(g0, c.NS);
     g.out = M0;
@@ -961,7 +951,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     // pass 2: select, rescore exactly, certify (or fall back)
     const FinishSmem FL{(dim + 3) / 4 * 4, next_pow2(std::max(c.S, P))};
     const int fin_smem = FIN_WARPS * FL.per_warp_bytes();
-    FG_CUDA_TRY(cudaFuncSetAttribute(coarse_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fin_smem));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_finish_kernel), fin_smem));
     coarse_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fin_smem, s>>>(centroids, nlist, dim, queries, (int)nq, cnt,
                                                                      c.nlists, lk, li, c.cap, c.S, P, qn, maxc, err,
                                                                      fb, out_ids, out_d, nfb);

@@ -15,6 +15,13 @@ void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int check_launch(const char* what);
 
+// A device attribute of the current device, read once per device and cached
+// (launch paths ask for shared-memory limits and SM counts on every call).
+int device_attr(cudaDeviceAttr attr);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) only when `bytes` exceeds
+// what was last granted to `func` (the attribute is per function, not per launch).
+cudaError_t ensure_smem(const void* func, int bytes);
+
 #define FG_REQUIRE(cond, ...)                                          \
     do {                                                               \
         if (!(cond)) return ::fg::fail(FG_ERR_INVALID_ARG, __VA_ARGS__); \

@@ -338,7 +338,7 @@ int graph_build(const void* data, int dtype, long long n, int dim, const fg_grap
     {
         const int nt = (I + 31) / 32 * 32;
         const size_t sm = (size_t)I * 8 + (size_t)next_pow2(I) * 4;
-        FG_CUDA_TRY(cudaFuncSetAttribute(prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&prune_kernel), (int)sm));
         prune_kernel<<<(unsigned)n, nt, sm, s>>>(g0.as<int32_t>(), order.as<int32_t>(), n, I, D, pr.as<int32_t>());
         if ((rc = check_launch("prune_kernel"))) return rc;
     }
@@ -882,7 +882,7 @@ int graph_search(const void* data, int dtype, long long n, int dim, const int32_
         k = p->metric == FG_METRIC_IP ? graph_search_kernel<__half, FG_METRIC_IP> : graph_search_kernel<__half, FG_METRIC_L2>;
     else
         k = p->metric == FG_METRIC_IP ? graph_search_kernel<float, FG_METRIC_IP> : graph_search_kernel<float, FG_METRIC_L2>;
-    FG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k), (int)sm));
     k<<<nq, GS_NT, sm, s>>>(a);
     return check_launch("graph_search_kernel");
 }

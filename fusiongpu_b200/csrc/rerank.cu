@@ -347,18 +347,15 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
     a.rch = std::max(8, std::min(mmax, 34816 / stride));
     if (const char* e = getenv("FG_RERANK_CHUNK")) a.rch = std::max(8, std::min(mmax, atoi(e)));  // tuning override
     const size_t smem = (size_t)rerank_layout(dim, a.k, a.mb).fixed + (size_t)a.rch * stride;
-    int dev = 0, smem_max = 0;
-    FG_CUDA_TRY(cudaGetDevice(&dev));
-    FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    int smem_max = 0;
+    smem_max = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin);
     if (smem > (size_t)smem_max - 1024)
         return fail(FG_ERR_UNSUPPORTED, "rerank needs %zu bytes of shared memory", smem);
     if (base_u8) {
-        FG_CUDA_TRY(cudaFuncSetAttribute(rerank_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem));
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&rerank_kernel<uint8_t>), (int)smem));
         rerank_kernel<uint8_t><<<nq, RR_NT, smem, stream>>>(a);
     } else {
-        FG_CUDA_TRY(cudaFuncSetAttribute(rerank_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem));
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&rerank_kernel<float>), (int)smem));
         rerank_kernel<float><<<nq, RR_NT, smem, stream>>>(a);
     }
     return check_launch("rerank_kernel");

@@ -1302,10 +1302,10 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.small = 0;
     a.work_counter = work_counter;
 
-    int dev = 0, smem_max = 0, smem_sm = 0;
-    FG_CUDA_TRY(cudaGetDevice(&dev));
-    FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    FG_CUDA_TRY(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    int smem_max = 0, smem_sm = 0;
+    smem_max = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin);
+    smem_sm = device_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor);
+    if (smem_max <= 0 || smem_sm <= 0) return fail(FG_ERR_CUDA, "cannot read the device's shared-memory limits");
 
     // The team kernel when the codebook and at least one team fit in shared
     // memory (two teams for on-the-fly ADC).  FG_SCAN_KERNEL=block|team|team_lut|team_otf
@@ -1393,10 +1393,10 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
             const char* fws = getenv("FG_SCAN_WARP_SELECT");  // 0: team-wide selection always
             a.small = small ? ((fws && fws[0] == '0') ? 2 : 1) : 0;
             int nsm = 0;
-            FG_CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+            nsm = std::max(1, device_attr(cudaDevAttrMultiProcessorCount));
             const int grid = std::max(1, std::min(nsm, (nq + best.nteams - 1) / best.nteams));
             const int bytes = cb_bytes + best.nteams * best.bytes;
-            FG_CUDA_TRY(cudaFuncSetAttribute(best.k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(best.k), bytes));
             best.k<<<grid, best.nteams * best.nt, bytes, stream>>>(a, nq, best.nteams, best.bytes);
             return check_launch("ivfpq_team_kernel");
         }
@@ -1417,7 +1417,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     if (L.total > smem_max)
         return fail(FG_ERR_UNSUPPORTED, "scan needs %d bytes of shared memory (max %d): rerank_m=%d "
                     "max_list_len=%d", L.total, smem_max, a.rerank_m, a.lmax);
-    FG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k), L.total));
     k<<<nq, SCAN_NT, L.total, stream>>>(a);
     return check_launch("ivfpq_batch_kernel");
 }

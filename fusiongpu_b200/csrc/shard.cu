@@ -57,7 +57,7 @@ int merge_topk(const float* dists, const int32_t* ids, int nshards, int nq, int 
     const int npow = next_pow2(nshards * k);
     FG_REQUIRE(npow <= 4096, "nshards * k = %d exceeds 4096", nshards * k);
     const size_t smem = (size_t)MG_WARPS * npow * 8;
-    FG_CUDA_TRY(cudaFuncSetAttribute(merge_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&merge_topk_kernel), (int)smem));
     merge_topk_kernel<<<(nq + MG_WARPS - 1) / MG_WARPS, MG_WARPS * 32, smem, s>>>(dists, ids, nshards, nq, k, npow,
                                                                                 out_ids, out_d);
     return check_launch("merge_topk_kernel");
