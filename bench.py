@@ -192,7 +192,10 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > 126 MB L2
     stream = torch.cuda.current_stream(device)
     sweep = []
-    launches_per_step = 4 if idx.nlist <= 8192 else 5  # coarse tile + top-k (+stage 2) + scan + rerank
+    def launches_per_step(nprobe):
+        # two bf16 splits + coarse GEMM + finish (top_m <= 4), or splits + prefix GEMM
+        # + bound + filter GEMM + finish; then the scan and the rerank
+        return (4 if nprobe <= 4 else 6) + 2
     clocks = ClockSampler(local)
     with clocks:
         for nprobe in (SWEEP if not args.nprobe else (args.nprobe,)):
@@ -277,8 +280,8 @@ def main():
         "sweep": sweep,
         "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
-        "gpu_launches": launches_per_step * args.steps * len(sweep),
-        "gpu_launches_per_step": launches_per_step,
+        "gpu_launches": sum(launches_per_step(s["nprobe"]) for s in sweep) * args.steps,
+        "gpu_launches_per_step": launches_per_step(op["nprobe"]),
         "roofline": roof,
         "clocks": clocks.summary(),
         "setup_s": W["setup_s"],
