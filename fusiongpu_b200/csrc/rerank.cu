@@ -24,7 +24,7 @@
 
 namespace fg {
 
-constexpr int RR_NT = 256;
+constexpr int RR_NT = 128;
 
 struct RerankArgs {
     const float* queries;
@@ -142,8 +142,10 @@ __device__ __forceinline__ void stage_rows(const RerankArgs& a, const int32_t* w
     if ((row_bytes & 15) == 0) {
         const int per_row = row_bytes >> 4;
         const int total = nr * per_row;
+        const bool pow2 = (per_row & (per_row - 1)) == 0;
+        const int sh = pow2 ? __ffs(per_row) - 1 : 0;
         for (int e = threadIdx.x; e < total; e += RR_NT) {
-            const int r = e / per_row, c = e - r * per_row;
+            const int r = pow2 ? e >> sh : e / per_row, c = e - r * per_row;
             const int32_t vid = wi[c0 + r];
             if (vid >= 0 && (long long)vid < a.nbase) {
                 const unsigned char* src = static_cast<const unsigned char*>(a.base) + (size_t)vid * row_bytes + 16 * c;
@@ -167,7 +169,7 @@ __device__ __forceinline__ void stage_rows(const RerankArgs& a, const int32_t* w
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <class T>
-__global__ void __launch_bounds__(RR_NT, 4) rerank_kernel(const RerankArgs a) {
+__global__ void __launch_bounds__(RR_NT, 8) rerank_kernel(const RerankArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp[RR_NT / 32];
     __shared__ int s_stab;
@@ -228,9 +230,19 @@ __global__ void __launch_bounds__(RR_NT, 4) rerank_kernel(const RerankArgs a) {
         if (tid < m4 - m) wd[m + tid] = INFINITY;
         __syncthreads();
         // stable ranks, old and new entries at once: old entries come before
-        // new ones on equal distance, new ones keep their order
+        // new ones on equal distance, new ones keep their order.  In the first
+        // mini-batch every old entry is (FLT_MAX, -1): the merged list is those
+        // placeholders with each finite new entry at its rank among the new ones.
         const float4* w4 = reinterpret_cast<const float4*>(wd);
-        for (int t = tid; t < k + m; t += RR_NT) {
+        const bool first_batch = off == 0;
+        if (first_batch) {
+            for (int t = tid; t < k; t += RR_NT) {
+                nd[t] = FLT_MAX;
+                ni[t] = -1;
+            }
+            __syncthreads();
+        }
+        for (int t = first_batch ? k + tid : tid; t < k + m; t += RR_NT) {
             if (t < k) {  // old entry t (the top-k is sorted)
                 const float d = fd[t];
                 int r = t;
@@ -247,9 +259,13 @@ __global__ void __launch_bounds__(RR_NT, 4) rerank_kernel(const RerankArgs a) {
                 const int i = t - k;
                 const float d = wd[i];
                 int lo = 0, hi = k;  // old entries with distance <= d
-                while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    if (fd[mid] <= d) lo = mid + 1; else hi = mid;
+                if (first_batch) {
+                    lo = d < FLT_MAX ? 0 : k;
+                } else {
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (fd[mid] <= d) lo = mid + 1; else hi = mid;
+                    }
                 }
                 int r = lo;
 #pragma unroll 4
@@ -342,9 +358,10 @@ int rerank(const float* queries, int nq, int dim, const int32_t* top_ids, const 
     a.out_dists = out_dists;
     const int stride = base_u8 ? row_stride_bytes<uint8_t>(dim) : row_stride_bytes<float>(dim);
     const int mmax = std::max(1, std::min(a.mb, a.nw - a.k));  // new entries per mini-batch
-    // about 34 KB of staged rows: six CTAs per SM (measured on C2 against 128
-    // rows at once: 0.114 against 0.137 ms at nprobe 1, 0.84 against 0.95 at 8)
-    a.rch = std::max(8, std::min(mmax, 34816 / stride));
+    // about 24 KB of staged rows: eight 128-thread CTAs per SM (measured on C2
+    // against 64 and 96 rows: 0.130 / 0.134 / 0.167 ms at nprobe 2, 0.61 / 0.66 /
+    // 0.86 ms at nprobe 8)
+    a.rch = std::max(8, std::min(mmax, 24576 / stride));
     if (const char* e = getenv("FG_RERANK_CHUNK")) a.rch = std::max(8, std::min(mmax, atoi(e)));  // tuning override
     const size_t smem = (size_t)rerank_layout(dim, a.k, a.mb).fixed + (size_t)a.rch * stride;
     int smem_max = 0;
