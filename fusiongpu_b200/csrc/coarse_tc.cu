@@ -46,7 +46,6 @@ constexpr int TC_PARTS = 4;              // column parts of a tile: one epilogue
 constexpr int TC_CPW = TC_N / TC_PARTS;  // 32 columns of each tile per epilogue thread
 constexpr int TC_EPI_WARPS = 4 * TC_PARTS;
 constexpr int TC_NT = 64 + TC_EPI_WARPS * 32;
-constexpr int TC_NORM_STAGE = 0;  // centroid norms staged in shared memory when ncols <= this
 
 __host__ __device__ inline int tc_kpad(int dim) { return (3 * dim + TC_KB - 1) / TC_KB * TC_KB; }
 
@@ -200,7 +199,6 @@ __global__ void __launch_bounds__(TC_NT, 1)
         (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
     unsigned char* sa = base;
     unsigned char* sb = base + g.kt * A_KB;
-    float* sn = reinterpret_cast<float*>(sb + TC_NST * B_KB);  // [ncols] norms when staged
 
     if (tid == 0) {
         s_fail = 0;
@@ -320,14 +318,9 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 }
             }
         };
-        // column norms: every one staged in shared memory once when they fit,
-        // else read per tile from global memory
-        const bool staged = g.ncols <= TC_NORM_STAGE;
-        if (staged) {
-            for (int i = tid - 64; i < g.ncols; i += TC_EPI_WARPS * 32) sn[i] = __ldg(g.cn + i);
-            tc::named_bar_sync(1, TC_EPI_WARPS * 32);
-        }
-        const float* cnp = staged ? sn : g.cn;
+        // column norms come from global memory per tile (16 KB for 4K
+        // centroids: they stay in L1; the shared memory holds the B ring)
+        const float* cnp = g.cn;
         int li = 0;
         for (long long pi = p0; pi < p1; ++pi, ++li) {
             const long long mt = pi / g.ntiles;
@@ -873,9 +866,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     CUtensorMap ta, tb;
     if ((rc = make_map(&ta, A, nq_pad, kpad, TC_M))) return rc;
     if ((rc = make_map(&tb, B, nl_pad, kpad, TC_N))) return rc;
-    const int smem_base = 1024 + kt * TC_M * TC_KB * 2 + TC_NST * TC_N * TC_KB * 2;
-    // the staged norms of the pass over every centroid (pass 0 covers a prefix)
-    const int smem = smem_base + (nlist <= TC_NORM_STAGE ? nlist * 4 : 0);
+    const int smem = 1024 + kt * TC_M * TC_KB * 2 + TC_NST * TC_N * TC_KB * 2;
 
     GemmArgs g{};
     g.kt = kt;
@@ -923,7 +914,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     }
 
     // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
-    const int smem0 = smem_base + (c.NS <= TC_NORM_STAGE ? c.NS * 4 : 0);
+    const int smem0 = smem;
     FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_MATRIX, 1>), smem0));
     FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_FILTER, 1>), smem));
     const GemmGrid g0 = gemm_grid(nq, c.NS);
