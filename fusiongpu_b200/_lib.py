@@ -8,7 +8,8 @@ import ctypes as C
 import os
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libfusiongpu_b200.so")
+# FG_LIBRARY names another build of the same library (a variant under test)
+LIB_PATH = os.environ.get("FG_LIBRARY") or os.path.join(PKG, "libfusiongpu_b200.so")
 
 FG_OK = 0
 STATUS = {0: "FG_OK", 1: "FG_ERR_INVALID_ARG", 2: "FG_ERR_CUDA", 3: "FG_ERR_WORKSPACE",
