@@ -520,7 +520,7 @@ struct FinishSmem {
     }
 };
 
-// Warp per query: gather the appended (key, id) of every column run, keep the
+// Warp per query: gather the appended (key, id) of every list segment, keep the
 // S smallest keys, rescore them exactly, sort by (distance, id), certify;
 // otherwise rescore all centroids exactly through the warp's scratch row.
 __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
     unsigned long long* ex = sx + L.spow;
     for (int t = lane; t < dim; t += 32) sq[t] = queries[(size_t)q * dim + t];
 
-    // gather the column runs' segments
+    // gather the segments
     int total = 0;
     bool over = false;
     for (int y = 0; y < gy; ++y) {

@@ -123,12 +123,17 @@ int fg_coarse_search_noalloc(const float* centroids, int32_t nlist, int32_t dim,
                              void* stream);
 
 /* ---- candidate generation: replaces run_gpu_batch_logic (gpu_global.cu:679-874)
- * Prune, per-(query, list) LUT in shared memory, phase-1 ADC scan with
- * per-list top-limit_k, threshold, phase-2 ADC scan, and the sorted top
- * rerank_m candidates per query.  probe_ids/probe_dists: [nq][top_m] as
- * fg_coarse_search writes them (FG_INVALID_PROBE entries are skipped).
- * top_ids/top_dists: [nq][rerank_m]; top_counts: [nq] = min(#candidates, rerank_m).
- * Needs no workspace.  The probe list is not modified. */
+ * Prune, phase-1 ADC scan with per-list top-limit_k, threshold, phase-2 ADC
+ * scan, and the sorted top rerank_m candidates per query.  Short lists (mean
+ * length <= 400) run in a persistent kernel that keeps the PQ codebook in
+ * shared memory and computes each ADC term on the fly; long lists in one CTA
+ * per query with a per-(query, list) LUT in shared memory.  Both produce the
+ * reference's floats bit for bit.  FG_SCAN_KERNEL=block|team|team_lut|team_otf
+ * and FG_SCAN_TEAM_NT=64|128|256 in the environment override the choice.
+ * probe_ids/probe_dists: [nq][top_m] as fg_coarse_search writes them
+ * (FG_INVALID_PROBE entries are skipped).  top_ids/top_dists: [nq][rerank_m];
+ * top_counts: [nq] = min(#candidates, rerank_m).  Needs no workspace.  The
+ * probe list is not modified. */
 int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                    const uint32_t* probe_ids, const float* probe_dists,
                    const fg_search_params* params, int32_t* top_ids, float* top_dists,
@@ -161,7 +166,9 @@ int fg_rerank_u8(const float* queries, int32_t nq, int32_t dim, const int32_t* t
 
 /* ---- full search: coarse + candidate generation + rerank on one stream.
  * Replaces one SearchPipeline::submit_batch (search_pipeline.cu:311-377)
- * minus the host copies. */
+ * minus the host copies.  Allocation- and synchronisation-free (capturable
+ * into a CUDA graph); one workspace per concurrently running call.  The scan
+ * hands out queries through a counter in the workspace. */
 int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params,
                              int32_t nq, size_t* bytes);
 int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, const float* queries,
