@@ -28,19 +28,23 @@ def fg():
 
 
 SCAN_KERNELS = ["auto", "block", "team_otf/64", "team_otf/128", "team_otf/256", "team_lut/64", "team_lut/128",
-                "team_lut/256"]
+                "team_lut/256", "team_otf/64/teamselect"]
 
 
 @pytest.fixture(params=SCAN_KERNELS)
 def scan_kernel(request, monkeypatch):
     """Runs the test once per scan kernel: the per-query CTA kernel and the
     team kernel with table or on-the-fly ADC, teams of 64, 128 or 256 threads
-    (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat)."""
+    (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat), and
+    the team-wide list selection (FG_SCAN_WARP_SELECT=0)."""
     if request.param != "auto":
-        kern, _, nt = request.param.partition("/")
+        kern, _, rest = request.param.partition("/")
+        nt, _, sel = rest.partition("/")
         monkeypatch.setenv("FG_SCAN_KERNEL", kern)
         if nt:
             monkeypatch.setenv("FG_SCAN_TEAM_NT", nt)
+        if sel == "teamselect":  # team-wide selection where one warp would do it
+            monkeypatch.setenv("FG_SCAN_WARP_SELECT", "0")
     return request.param
 
 
