@@ -8,9 +8,11 @@
 // 2. coarse_gemm_kernel: persistent, warp-specialised CTA per SM over a balanced
 //    range of (128-query tile, 128-centroid tile) pairs; A resident in shared
 //    memory (reloaded where the range enters the next query tile), B through a
-//    6-stage TMA ring of 16 KB K blocks (128-byte swizzle, no multicast),
-//    tcgen05.mma issued by one thread into two TMEM accumulators; epilogue
-//    computes d~ = |q|^2 + |c|^2 - 2 q.c.
+//    3-stage TMA ring of 32 KB K blocks (two centroid tiles, 128-byte swizzle,
+//    no multicast), one tcgen05.mma of N = 256 per K step for two consecutive
+//    centroid tiles, issued by one thread into two TMEM accumulators; the
+//    epilogue computes d~ = |q|^2 + |c|^2 - 2 q.c with |c|^2 read from shared
+//    memory.
 //    top_m <= 4: a single pass in which every (query, range, column part) keeps
 //    its 4 or 8 smallest d~ in registers (coarse_topk_finish_kernel certifies).
 //    Larger top_m:
@@ -40,8 +42,10 @@ constexpr int TC_M = 128;       // queries per tile (UMMA M, TMEM lanes)
 constexpr int TC_N = 128;       // centroids per tile (UMMA N)
 constexpr int TC_TILE = 128;    // row padding of both operands
 constexpr int TC_KB = 64;       // bf16 elements per K block (one 128-byte swizzle row)
-constexpr int TC_MAX_KB = 6;    // A resident (6 x 16 KB) + TC_NST B stages (16 KB each) = 224 KB
-constexpr int TC_NST = 8;       // B ring: one K block of one tile per stage
+constexpr int TC_MAX_KB = 6;    // A resident (6 x 16 KB) + TC_NST B stages (32 KB each) = 192 KB
+constexpr int TC_GRP = 2;       // centroid tiles per MMA group (UMMA N = 256)
+constexpr int TC_NST = 3;       // B ring: one K block of a group's TC_GRP tiles per stage
+constexpr int TC_SMEM_MAX = 227 * 1024;  // dynamic shared memory per CTA; the rest holds column norms
 constexpr int TC_PARTS = 4;              // column parts of a tile: one epilogue warp per (lane quarter, part)
 constexpr int TC_CPW = TC_N / TC_PARTS;  // 32 columns of each tile per epilogue thread
 constexpr int TC_EPI_WARPS = 4 * TC_PARTS;
@@ -79,7 +83,7 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, long long n, int 
 
 // Warp roles of the persistent GEMM CTA (576 threads, one CTA per SM):
 //   warp 0, lane 0: TMA producer (the query tile A, then B through a ring of
-//                   TC_NST stages, one 128 x 64 K block per stage)
+//                   TC_NST stages, one 256 x 64 K block per stage)
 //   warp 1, lane 0: MMA issuer (and warp 1 owns the TMEM allocation)
 //   warps 2..17:    epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (its 32
 //                   queries) and columns 32*((w-2)/4) .. +31 of each tile
@@ -88,9 +92,14 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, long long n, int 
 // SMs whatever the shape; where a range crosses into the next query tile the
 // producer reloads A once the MMAs on the old one have finished (a_empty).  A
 // range covers one "segment" of a query tile: segment = CTA index minus the
-// first CTA of that query tile, at most maxseg per query tile.  TMEM holds two
-// 128 x 128 fp32 accumulators, so the epilogue of tile i runs while the MMAs of
-// tile i+1 fill the other one.
+// first CTA of that query tile, at most maxseg per query tile.
+// Within a range, two consecutive tiles of one query tile form a group whose
+// MMAs run as one UMMA of N = 256 (half the tcgen05.mma instructions, waits
+// and commits per flop of 128-wide tiles, which bound the MMA issuer); a tile
+// left over at the end of a range or of a query tile is a group of one (N =
+// 128).  Producer, issuer and epilogue walk the same groups.  TMEM holds two
+// 128 x 256 fp32 accumulators (all 512 columns), so the epilogue of group i
+// runs while the MMAs of group i+1 fill the other one.
 struct GemmArgs {
     int kt;              // 64-wide K blocks
     long long q0;        // first query row of this launch (row of the A tensor map)
@@ -110,6 +119,7 @@ struct GemmArgs {
     uint32_t* list_k;    // [nq][maxseg * TC_PARTS][cap or T] keys of d~
     int32_t* list_i;     // same shape: centroid ids
     int* err;
+    int norm_smem;       // column norms staged in shared memory (+inf past ncols)
 };
 
 enum { GEMM_MATRIX = 0, GEMM_FILTER = 1, GEMM_TOPK = 2 };
@@ -195,10 +205,12 @@ __global__ void __launch_bounds__(TC_NT, 1)
     if (p0 >= p1) return;  // uniform for the whole CTA
     constexpr int A_KB = TC_M * TC_KB * 2;  // 16 KB per K block
     constexpr int B_KB = TC_N * TC_KB * 2;  // 16 KB per K block
+    constexpr int B_ST = TC_GRP * B_KB;     // one stage
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
     unsigned char* sa = base;
     unsigned char* sb = base + g.kt * A_KB;
+    float* sn = reinterpret_cast<float*>(sb + TC_NST * B_ST);
 
     if (tid == 0) {
         s_fail = 0;
@@ -215,7 +227,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
         tc::fence_mbar_init();
     }
     if (warp == 1) {
-        tc::tmem_alloc(&tmem_slot, 2 * TC_N);
+        tc::tmem_alloc(&tmem_slot, 2 * TC_GRP * TC_N);
         tc::tmem_relinquish();
     }
     tc::fence_before_sync();
@@ -229,9 +241,10 @@ __global__ void __launch_bounds__(TC_NT, 1)
             long long cur = -1;
             int na = 0;
             long long kb = 0;
-            for (long long pi = p0; pi < p1; ++pi) {
+            for (long long pi = p0, gs = 1; pi < p1; pi += gs) {
                 const long long mt = pi / g.ntiles;
                 const int t = (int)(pi - mt * g.ntiles);
+                gs = (pi + 1 < p1 && t + 1 < g.ntiles) ? 2 : 1;
                 if (mt != cur) {
                     if (na > 0 && !tc::mbar_wait_or_fail(&a_empty, (na - 1) & 1, fail)) break;
                     tc::mbar_arrive_expect_tx(&a_full, (uint32_t)(g.kt * A_KB));
@@ -247,21 +260,25 @@ __global__ void __launch_bounds__(TC_NT, 1)
                         ok = false;
                         break;
                     }
-                    tc::mbar_arrive_expect_tx(&b_full[st], (uint32_t)B_KB);
-                    tc::tma_load_2d(sb + st * B_KB, &tb, &b_full[st], k * TC_KB, t * TC_N);
+                    tc::mbar_arrive_expect_tx(&b_full[st], (uint32_t)(gs * B_KB));
+                    tc::tma_load_2d(sb + st * B_ST, &tb, &b_full[st], k * TC_KB, t * TC_N);
+                    if (gs == 2) tc::tma_load_2d(sb + st * B_ST + B_KB, &tb, &b_full[st], k * TC_KB, (t + 1) * TC_N);
                 }
                 if (!ok) break;
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
-            constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_M, TC_N);
+            constexpr uint32_t idesc1 = tc::idesc_bf16_f32(TC_M, TC_N);
+            constexpr uint32_t idesc2 = tc::idesc_bf16_f32(TC_M, 2 * TC_N);
             long long cur = -1;
             int na = 0;
             long long kb = 0;
             int li = 0;
-            for (long long pi = p0; pi < p1; ++pi, ++li) {
+            for (long long pi = p0, gs = 1; pi < p1; pi += gs, ++li) {
                 const long long mt = pi / g.ntiles;
+                gs = (pi + 1 < p1 && (int)(pi - mt * g.ntiles) + 1 < g.ntiles) ? 2 : 1;
+                const uint32_t idesc = gs == 2 ? idesc2 : idesc1;
                 if (mt != cur) {
                     if (!tc::mbar_wait_or_fail(&a_full, na & 1, fail)) break;
                     ++na;
@@ -279,16 +296,16 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     }
                     tc::fence_after_sync();
                     const uint64_t da = tc::desc_kmajor_sw128(sa + k * A_KB);
-                    const uint64_t db = tc::desc_kmajor_sw128(sb + st * B_KB);
+                    const uint64_t db = tc::desc_kmajor_sw128(sb + st * B_ST);
 #pragma unroll
                     for (int kk = 0; kk < TC_KB / 16; ++kk)
-                        tc::umma_bf16(taddr + (uint32_t)(acc * TC_N), da + 2 * kk, db + 2 * kk, idesc,
+                        tc::umma_bf16(taddr + (uint32_t)(acc * TC_GRP * TC_N), da + 2 * kk, db + 2 * kk, idesc,
                                       (k | kk) != 0);
                     tc::umma_commit(&b_empty[st]);  // the stage may be refilled once these MMAs finish
                 }
                 if (!ok) break;
                 tc::umma_commit(&acc_full[acc]);  // the accumulator is ready for the epilogue
-                if (pi + 1 == p1 || (pi + 1) / g.ntiles != mt) tc::umma_commit(&a_empty);  // last use of this A
+                if (pi + gs == p1 || (pi + gs) / g.ntiles != mt) tc::umma_commit(&a_empty);  // last use of this A
             }
         }
     } else {  // ---- epilogue warps 2..17
@@ -318,13 +335,19 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 }
             }
         };
-        // column norms come from global memory per tile (16 KB for 4K
-        // centroids: they stay in L1; the shared memory holds the B ring)
+        // column norms: staged in shared memory once per CTA (+inf past ncols,
+        // so padded columns never enter a list), else read per tile from global
         const float* cnp = g.cn;
+        if (g.norm_smem) {
+            const int nfl = g.ntiles * TC_N;
+            for (int i = tid - 64; i < nfl; i += TC_EPI_WARPS * 32) sn[i] = i < g.ncols ? g.cn[i] : INFINITY;
+            asm volatile("bar.sync 1, %0;" ::"r"(TC_EPI_WARPS * 32) : "memory");
+        }
         int li = 0;
-        for (long long pi = p0; pi < p1; ++pi, ++li) {
+        for (long long pi = p0, gs = 1; pi < p1; pi += gs, ++li) {
             const long long mt = pi / g.ntiles;
-            const int t = (int)(pi - mt * g.ntiles);
+            const int t0 = (int)(pi - mt * g.ntiles);
+            gs = (pi + 1 < p1 && t0 + 1 < g.ntiles) ? 2 : 1;
             if (mt != cur) {
                 flush();
                 cur = mt;
@@ -341,85 +364,109 @@ __global__ void __launch_bounds__(TC_NT, 1)
             const int acc = li & 1, ph = (li >> 1) & 1;
             if (!__all_sync(0xffffffffu, tc::mbar_wait_or_fail(&acc_full[acc], ph, fail))) break;
             tc::fence_after_sync();
-            float v[32];
-            tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * TC_N + part * TC_CPW), v);
-            tc::fence_before_sync();
-            tc::mbar_arrive(&acc_empty[acc]);
-            // GEMM_TOPK keeps every lane in the loop: its candidate rounds are warp-collective
-            if (!valid && MODE != GEMM_TOPK) continue;
-            const int col0 = t * TC_N + part * TC_CPW;
-            const int ncol = min(TC_CPW, g.ncols - col0);
-            float c[32];
-            load_norms(cnp, col0, g.ncols, c);
-            if (MODE == GEMM_MATRIX) {
-                uint32_t* o = g.out + (long long)row * g.ldo + col0;
-                if (ncol == TC_CPW && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
+#pragma unroll 1
+            for (int sub = 0; sub < (int)gs; ++sub) {
+                const int t = t0 + sub;
+                float v[32];
+                tc::tmem_ld_32x32(taddr + ((uint32_t)(q4 * 32) << 16) +
+                                      (uint32_t)(acc * TC_GRP * TC_N + sub * TC_N + part * TC_CPW),
+                                  v);
+                if (sub + 1 == (int)gs) {
+                    tc::fence_before_sync();
+                    tc::mbar_arrive(&acc_empty[acc]);
+                }
+                // GEMM_TOPK keeps every lane in the loop: its candidate rounds are warp-collective
+                if (!valid && MODE != GEMM_TOPK) continue;
+                const int col0 = t * TC_N + part * TC_CPW;
+                const int ncol = min(TC_CPW, g.ncols - col0);
+                float c[32];
+                if (g.norm_smem) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
-                        uint4 k4;
-                        k4.x = f2key(qnr + c[j] - 2.0f * v[j]);
-                        k4.y = f2key(qnr + c[j + 1] - 2.0f * v[j + 1]);
-                        k4.z = f2key(qnr + c[j + 2] - 2.0f * v[j + 2]);
-                        k4.w = f2key(qnr + c[j + 3] - 2.0f * v[j + 3]);
-                        *reinterpret_cast<uint4*>(o + j) = k4;
+                        const float4 c4 = *reinterpret_cast<const float4*>(sn + col0 + j);
+                        c[j] = c4.x;
+                        c[j + 1] = c4.y;
+                        c[j + 2] = c4.z;
+                        c[j + 3] = c4.w;
                     }
                 } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
+                    load_norms(cnp, col0, g.ncols, c);
                 }
-            } else if (MODE == GEMM_TOPK) {
+                if (MODE == GEMM_MATRIX) {
+                    uint32_t* o = g.out + (long long)row * g.ldo + col0;
+                    if (ncol == TC_CPW && (g.ldo & 3) == 0) {  // 16-byte aligned row chunks
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
-                if (first) {
-                    // fill the list from the segment's first chunk: T rounds of
-                    // taking out the minimum (lowest column first on equal values)
+                        for (int j = 0; j < 32; j += 4) {
+                            uint4 k4;
+                            k4.x = f2key(qnr + c[j] - 2.0f * v[j]);
+                            k4.y = f2key(qnr + c[j + 1] - 2.0f * v[j + 1]);
+                            k4.z = f2key(qnr + c[j + 2] - 2.0f * v[j + 2]);
+                            k4.w = f2key(qnr + c[j + 3] - 2.0f * v[j + 3]);
+                            *reinterpret_cast<uint4*>(o + j) = k4;
+                        }
+                    } else {
 #pragma unroll
-                    for (int r = 0; r < T; ++r) {
-                        const float mn = min32(v);
-                        unsigned em = 0;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) em |= (v[j] == mn) ? (1u << j) : 0u;
-                        const int jm = __ffs(em) - 1;
-                        bd[r] = mn;
-                        bi[r] = (mn < INFINITY) ? col0 + jm : -1;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = (j == jm) ? INFINITY : v[j];
+                        for (int j = 0; j < 32; ++j)
+                            if (j < ncol) o[j] = f2key(qnr + c[j] - 2.0f * v[j]);
                     }
-                    first = false;
-                    continue;
-                }
-                unsigned cand = 0;
-                if (valid && min32(v) < bd[T - 1]) {
+                } else if (MODE == GEMM_TOPK) {
+                    if (g.norm_smem) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) cand |= (v[j] < bd[T - 1]) ? (1u << j) : 0u;
-                }
-                // one candidate per lane per round: the warp runs as many rounds as
-                // its busiest lane has candidates (one or two once the lists fill)
-                while (__any_sync(0xffffffffu, cand != 0u)) {
-                    if (cand) {
-                        const int j = __ffs(cand) - 1;
-                        cand &= cand - 1u;
-                        const float x = select32(v, j);
-                        if (x < bd[T - 1]) insert_sorted<T>(bd, bi, x, col0 + j);
+                        for (int j = 0; j < 32; ++j) v[j] = fmaf(-2.0f, v[j], c[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = (j < ncol) ? fmaf(-2.0f, v[j], c[j]) : INFINITY;
                     }
-                }
-            } else {
-                unsigned pass = 0;
+                    if (first) {
+                        // fill the list from the segment's first chunk: T rounds of
+                        // taking out the minimum (lowest column first on equal values)
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    v[j] = qnr + c[j] - 2.0f * v[j];
-                    pass |= (j < ncol && v[j] <= bound) ? (1u << j) : 0u;
-                }
-                if (pass) {
+                        for (int r = 0; r < T; ++r) {
+                            const float mn = min32(v);
+                            unsigned em = 0;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) em |= (v[j] == mn) ? (1u << j) : 0u;
+                            const int jm = __ffs(em) - 1;
+                            bd[r] = mn;
+                            bi[r] = (mn < INFINITY) ? col0 + jm : -1;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = (j == jm) ? INFINITY : v[j];
+                        }
+                        first = false;
+                        continue;
+                    }
+                    unsigned cand = 0;
+                    if (valid && min32(v) < bd[T - 1]) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) cand |= (v[j] < bd[T - 1]) ? (1u << j) : 0u;
+                    }
+                    // one candidate per lane per round: the warp runs as many rounds as
+                    // its busiest lane has candidates (one or two once the lists fill)
+                    while (__any_sync(0xffffffffu, cand != 0u)) {
+                        if (cand) {
+                            const int j = __ffs(cand) - 1;
+                            cand &= cand - 1u;
+                            const float x = select32(v, j);
+                            if (x < bd[T - 1]) insert_sorted<T>(bd, bi, x, col0 + j);
+                        }
+                    }
+                } else {
+                    unsigned pass = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        if (pass & (1u << j)) {
-                            if (n < g.cap) {
-                                g.list_k[lidx * g.cap + n] = f2key(v[j]);
-                                g.list_i[lidx * g.cap + n] = col0 + j;
+                        v[j] = qnr + c[j] - 2.0f * v[j];
+                        pass |= (j < ncol && v[j] <= bound) ? (1u << j) : 0u;
+                    }
+                    if (pass) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (pass & (1u << j)) {
+                                if (n < g.cap) {
+                                    g.list_k[lidx * g.cap + n] = f2key(v[j]);
+                                    g.list_i[lidx * g.cap + n] = col0 + j;
+                                }
+                                ++n;
                             }
-                            ++n;
                         }
                     }
                 }
@@ -429,7 +476,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 1) tc::tmem_dealloc(taddr, 2 * TC_N);
+    if (warp == 1) tc::tmem_dealloc(taddr, 2 * TC_GRP * TC_N);
     if (tid == 0 && s_fail) atomicExch(g.err, 1);
 }
 
@@ -866,7 +913,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     CUtensorMap ta, tb;
     if ((rc = make_map(&ta, A, nq_pad, kpad, TC_M))) return rc;
     if ((rc = make_map(&tb, B, nl_pad, kpad, TC_N))) return rc;
-    const int smem = 1024 + kt * TC_M * TC_KB * 2 + TC_NST * TC_N * TC_KB * 2;
+    const int smem_base = 1024 + kt * TC_M * TC_KB * 2 + TC_NST * TC_GRP * TC_N * TC_KB * 2;
 
     GemmArgs g{};
     g.kt = kt;
@@ -875,12 +922,17 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     g.qn = qn;
     g.cn = cn;
     g.err = err;
+    // Sets the launch's columns and range split; returns its dynamic shared
+    // memory, which holds the column norms too where they fit.
     auto set_grid = [&](const GemmGrid& gg, int ncols) {
         g.ncols = ncols;
         g.ntiles = gg.ntiles;
         g.total = gg.total;
         g.per_cta = gg.per_cta;
         g.maxseg = gg.maxseg;
+        const int norm_bytes = gg.ntiles * TC_N * (int)sizeof(float);
+        g.norm_smem = smem_base + norm_bytes <= TC_SMEM_MAX;
+        return g.norm_smem ? smem_base + norm_bytes : smem_base;
     };
 
     const int T = topk_len(P);
@@ -890,15 +942,15 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
         // registers; a warp per query rescores and certifies them.  Lists of
         // segments that no CTA covers stay empty (ids -1).
         FG_CUDA_TRY(cudaMemsetAsync(li, 0xff, (size_t)nq * c.nlists * T * sizeof(int32_t), s));
-        set_grid(c.g1, nlist);
+        const int smem1 = set_grid(c.g1, nlist);
         g.list_k = lk;
         g.list_i = li;
         if (T == 4) {
-            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 4>), smem));
-            coarse_gemm_kernel<GEMM_TOPK, 4><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
+            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 4>), smem1));
+            coarse_gemm_kernel<GEMM_TOPK, 4><<<c.g1.ctas, TC_NT, smem1, s>>>(ta, tb, g);
         } else {
-            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 8>), smem));
-            coarse_gemm_kernel<GEMM_TOPK, 8><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
+            FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_TOPK, 8>), smem1));
+            coarse_gemm_kernel<GEMM_TOPK, 8><<<c.g1.ctas, TC_NT, smem1, s>>>(ta, tb, g);
         }
         if ((rc = check_launch("coarse_gemm_kernel(top-k)"))) return rc;
         FG_CUDA_TRY(
@@ -914,11 +966,9 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     }
 
     // pass 0: keys of d~ to the first NS centroids, then the S-th smallest per query
-    const int smem0 = smem;
-    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_MATRIX, 1>), smem0));
-    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_FILTER, 1>), smem));
     const GemmGrid g0 = gemm_grid(nq, c.NS);
-    set_grid(g0, c.NS);
+    const int smem0 = set_grid(g0, c.NS);
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_MATRIX, 1>), smem0));
     g.out = M0;
     g.ldo = ldm;
     coarse_gemm_kernel<GEMM_MATRIX, 1><<<g0.ctas, TC_NT, smem0, s>>>(ta, tb, g);
@@ -929,14 +979,15 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     // pass 1: every centroid; each query row appends those within its bound
     // (counts of segments that no CTA covers stay 0)
     FG_CUDA_TRY(cudaMemsetAsync(cnt, 0, (size_t)nq * c.nlists * sizeof(int), s));
-    set_grid(c.g1, nlist);
+    const int smem1 = set_grid(c.g1, nlist);
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_gemm_kernel<GEMM_FILTER, 1>), smem1));
     g.out = nullptr;
     g.tq = tq;
     g.cap = c.cap;
     g.cnt = cnt;
     g.list_k = lk;
     g.list_i = li;
-    coarse_gemm_kernel<GEMM_FILTER, 1><<<c.g1.ctas, TC_NT, smem, s>>>(ta, tb, g);
+    coarse_gemm_kernel<GEMM_FILTER, 1><<<c.g1.ctas, TC_NT, smem1, s>>>(ta, tb, g);
     if ((rc = check_launch("coarse_gemm_kernel(filter)"))) return rc;
 
     // pass 2: select, rescore exactly, certify (or fall back)
