@@ -832,12 +832,11 @@ __device__ __forceinline__ uint32_t code_byte(const uint32_t (&w)[W], int t) {
 // rotated by j so that the byte of step s sits at static position s mod M.
 // Each lane still adds its terms in subspace order, so the sum is the same
 // float as adc_otf's.
-template <int M, int SD>
-__device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, const float* cbT, const float* res) {
-    constexpr int Z = AdcSkew<M, SD>::Z;
+// The M code bytes of one row, rotated up by j (0 <= j < Z): byte p of the
+// result is byte (p - j) mod M of the row.
+template <int M, int Z>
+__device__ __forceinline__ void load_rotated(const uint8_t* __restrict__ row, int j, uint32_t (&w)[M / 4]) {
     constexpr int W = M / 4;
-    const int j = (threadIdx.x & 31) % Z;
-    uint32_t w[W];
     if constexpr (M % 16 == 0) {
         const uint4* r4 = reinterpret_cast<const uint4*>(row);
 #pragma unroll
@@ -875,6 +874,15 @@ __device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, c
             for (int u = 0; u < W; ++u) w[u] = t[u];
         }
     }
+}
+
+template <int M, int SD>
+__device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, const float* cbT, const float* res) {
+    constexpr int Z = AdcSkew<M, SD>::Z;
+    constexpr int W = M / 4;
+    const int j = (threadIdx.x & 31) % Z;
+    uint32_t w[W];
+    load_rotated<M, Z>(row, j, w);
     const float* rl = res - j * SD;            // + s*SD: residual of subspace s - j
     const float* cl = cbT - j * SD;            // + (k*M + s)*SD: codebook entry (k, s - j)
     float d = 0.0f;
@@ -890,6 +898,91 @@ __device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, c
         }
     }
     return d;
+}
+
+// Skewed ADC of every row of a list, the rows of one lane streamed back to
+// back: lane tt takes rows tt, tt + NT, ...  Period r (M steps) finishes the
+// previous row's subspaces M-j .. M-1 in its first j steps and starts row r in
+// the rest, so a lane idles only in the Z - 1 drain steps after its last row
+// (adc_otf_skew idles Z - 1 steps per row).  Shared-memory reads keep the
+// bank pattern of adc_otf_skew (lane j reads subspaces s with s mod Z = (step
+// - j) mod Z), and each row's terms are still added in subspace order from
+// 0.0f, so every key equals f2key(adc_otf_skew(row)).  Writes lkey[i] for i <
+// n; the caller syncs the team.
+template <int M, int SD, int NT>
+__device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows, int n, int tt, const float* cbT,
+                                                const float* res, uint32_t* lkey) {
+    constexpr int Z = AdcSkew<M, SD>::Z;
+    constexpr int W = M / 4;
+    constexpr int HW = (Z - 1 + 3) / 4;  // words holding byte positions < Z - 1
+    const int j = (threadIdx.x & 31) % Z;
+    const int nr = n > tt ? (n - tt + NT - 1) / NT : 0;  // rows of this lane
+    const int tw = tt & ~31;
+    const int nw = n > tw ? (n - tw + NT - 1) / NT : 0;  // rows of the warp's first lane: the most
+    // byte masks: position p < j takes the previous row
+    uint32_t pm[HW];
+#pragma unroll
+    for (int u = 0; u < HW; ++u) {
+        const int e = j - 4 * u;
+        pm[u] = e >= 4 ? 0xffffffffu : (e <= 0 ? 0u : (1u << (8 * e)) - 1u);
+    }
+    const float* rl = res - j * SD;  // + s*SD: residual of subspace s - j
+    const float* cl = cbT - j * SD;  // + (k*M + s)*SD: codebook entry (k, s - j)
+    uint32_t prev[HW];
+#pragma unroll
+    for (int u = 0; u < HW; ++u) prev[u] = 0u;
+    float dprev = 0.0f;
+    for (int r = 0; r < nw; ++r) {
+        uint32_t w[W];
+        if (r < nr) {
+            load_rotated<M, Z>(rows + (size_t)(tt + r * NT) * M, j, w);
+        } else {
+#pragma unroll
+            for (int u = 0; u < W; ++u) w[u] = 0u;
+        }
+        uint32_t h[HW];
+#pragma unroll
+        for (int u = 0; u < HW; ++u) h[u] = (prev[u] & pm[u]) | (w[u] & ~pm[u]);
+        float dcur = 0.0f;
+#pragma unroll
+        for (int st = 0; st < M; ++st) {
+            if (st < Z - 1) {
+                const bool tail = st < j;  // previous row, subspace st - j + M
+                const int sp = tail ? st + M : st;
+                const uint32_t k = code_byte<HW>(h, st);
+                float rv[SD], cv[SD];
+                load_sub<SD, false>(rl + sp * SD, rv);
+                load_sub<SD, false>(cl + ((size_t)k * M + sp) * SD, cv);
+                const float t = sd_arith<SD>(rv, cv);
+                if (tail)
+                    dprev = __fadd_rn(dprev, t);
+                else
+                    dcur = __fadd_rn(dcur, t);
+            } else {
+                const uint32_t k = code_byte<W>(w, st);
+                float rv[SD], cv[SD];
+                load_sub<SD, false>(rl + st * SD, rv);
+                load_sub<SD, false>(cl + ((size_t)k * M + st) * SD, cv);
+                dcur = __fadd_rn(dcur, sd_arith<SD>(rv, cv));
+            }
+        }
+        if (r > 0 && r - 1 < nr) lkey[tt + (r - 1) * NT] = f2key(dprev);
+        dprev = dcur;
+#pragma unroll
+        for (int u = 0; u < HW; ++u) prev[u] = w[u];
+    }
+    // drain: the last row's subspaces M-j .. M-1
+#pragma unroll
+    for (int st = 0; st < Z - 1; ++st) {
+        if (st < j) {
+            const uint32_t k = code_byte<HW>(prev, st);
+            float rv[SD], cv[SD];
+            load_sub<SD, false>(rl + (st + M) * SD, rv);
+            load_sub<SD, false>(cl + ((size_t)k * M + st + M) * SD, cv);
+            dprev = __fadd_rn(dprev, sd_arith<SD>(rv, cv));
+        }
+    }
+    if (nw > 0 && nw - 1 < nr) lkey[tt + (nw - 1) * NT] = f2key(dprev);
 }
 
 // Residual of list c for this query; with LUT also the list's table from the
@@ -1001,7 +1094,10 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
             const int wc = len < a.limit_k ? len : a.limit_k;
             const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
             team_prepare_list<M, SD, LUT, NT>(a, qv, c, cb, res, lut, tt, bar);
-            for (int i = tt; i < scan; i += NT) lkey[i] = f2key(team_adc<M, SD, LUT>(a, start, i, cb, res, lut));
+            if constexpr (!LUT && AdcSkew<M, SD>::value)
+                adc_skew_stream<M, SD, NT>(a.codes + (size_t)start * M, scan, tt, cb, res, lkey);
+            else
+                for (int i = tt; i < scan; i += NT) lkey[i] = f2key(team_adc<M, SD, LUT>(a, start, i, cb, res, lut));
             team_sync<NT>(bar);
             if (a.small == 1 && scan <= WARP_SELECT_MAX) {
                 // one warp selects and emits (the buffer can never need a cut)
