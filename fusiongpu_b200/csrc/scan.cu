@@ -148,6 +148,23 @@ __device__ __forceinline__ void load_sub(const float* p, float (&v)[SD]) {
     }
 }
 
+// SD consecutive floats at a 32-bit shared-memory address.
+template <int SD>
+__device__ __forceinline__ void lds_sub(uint32_t addr, float (&v)[SD]) {
+    if constexpr (SD % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < SD / 4; ++i)
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(v[4 * i]), "=f"(v[4 * i + 1]), "=f"(v[4 * i + 2]), "=f"(v[4 * i + 3])
+                         : "r"(addr + 16 * i));
+    } else if constexpr (SD == 2) {
+        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v[0]), "=f"(v[1]) : "r"(addr));
+    } else {
+#pragma unroll
+        for (int i = 0; i < SD; ++i) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v[i]) : "r"(addr + 4 * i));
+    }
+}
+
 // r in shared memory, c in global memory.
 template <int SD>
 __device__ __forceinline__ float sub_dist(const float* r, const float* c) {
@@ -883,8 +900,10 @@ __device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, c
     const int j = (threadIdx.x & 31) % Z;
     uint32_t w[W];
     load_rotated<M, Z>(row, j, w);
-    const float* rl = res - j * SD;            // + s*SD: residual of subspace s - j
-    const float* cl = cbT - j * SD;            // + (k*M + s)*SD: codebook entry (k, s - j)
+    // 32-bit shared addresses: + 4*SD*s is the residual of subspace s - j, + 4*SD*(k*M + s)
+    // the codebook entry (k, s - j)
+    const uint32_t rl = static_cast<uint32_t>(__cvta_generic_to_shared(res)) - 4u * SD * j;
+    const uint32_t cl = static_cast<uint32_t>(__cvta_generic_to_shared(cbT)) - 4u * SD * j;
     float d = 0.0f;
 #pragma unroll
     for (int st = 0; st < M + Z - 1; ++st) {
@@ -892,8 +911,8 @@ __device__ __forceinline__ float adc_otf_skew(const uint8_t* __restrict__ row, c
         if (act) {
             const uint32_t k = code_byte<W>(w, st % M);
             float rv[SD], cv[SD];
-            load_sub<SD, false>(rl + st * SD, rv);
-            load_sub<SD, false>(cl + ((size_t)k * M + st) * SD, cv);
+            lds_sub<SD>(rl + 4u * SD * st, rv);
+            lds_sub<SD>(cl + 4u * SD * (k * M + st), cv);
             d = __fadd_rn(d, sd_arith<SD>(rv, cv));
         }
     }
@@ -926,8 +945,10 @@ __device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows
         const int e = j - 4 * u;
         pm[u] = e >= 4 ? 0xffffffffu : (e <= 0 ? 0u : (1u << (8 * e)) - 1u);
     }
-    const float* rl = res - j * SD;  // + s*SD: residual of subspace s - j
-    const float* cl = cbT - j * SD;  // + (k*M + s)*SD: codebook entry (k, s - j)
+    // 32-bit shared addresses: + 4*SD*s is the residual of subspace s - j, + 4*SD*(k*M + s)
+    // the codebook entry (k, s - j)
+    const uint32_t rl = static_cast<uint32_t>(__cvta_generic_to_shared(res)) - 4u * SD * j;
+    const uint32_t cl = static_cast<uint32_t>(__cvta_generic_to_shared(cbT)) - 4u * SD * j;
     uint32_t prev[HW];
 #pragma unroll
     for (int u = 0; u < HW; ++u) prev[u] = 0u;
@@ -951,8 +972,8 @@ __device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows
                 const int sp = tail ? st + M : st;
                 const uint32_t k = code_byte<HW>(h, st);
                 float rv[SD], cv[SD];
-                load_sub<SD, false>(rl + sp * SD, rv);
-                load_sub<SD, false>(cl + ((size_t)k * M + sp) * SD, cv);
+                lds_sub<SD>(rl + 4u * SD * sp, rv);
+                lds_sub<SD>(cl + 4u * SD * (k * M + sp), cv);
                 const float t = sd_arith<SD>(rv, cv);
                 if (tail)
                     dprev = __fadd_rn(dprev, t);
@@ -961,8 +982,8 @@ __device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows
             } else {
                 const uint32_t k = code_byte<W>(w, st);
                 float rv[SD], cv[SD];
-                load_sub<SD, false>(rl + st * SD, rv);
-                load_sub<SD, false>(cl + ((size_t)k * M + st) * SD, cv);
+                lds_sub<SD>(rl + 4u * SD * st, rv);
+                lds_sub<SD>(cl + 4u * SD * (k * M + st), cv);
                 dcur = __fadd_rn(dcur, sd_arith<SD>(rv, cv));
             }
         }
@@ -977,8 +998,8 @@ __device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows
         if (st < j) {
             const uint32_t k = code_byte<HW>(prev, st);
             float rv[SD], cv[SD];
-            load_sub<SD, false>(rl + (st + M) * SD, rv);
-            load_sub<SD, false>(cl + ((size_t)k * M + st + M) * SD, cv);
+            lds_sub<SD>(rl + 4u * SD * (st + M), rv);
+            lds_sub<SD>(cl + 4u * SD * (k * M + st + M), cv);
             dprev = __fadd_rn(dprev, sd_arith<SD>(rv, cv));
         }
     }
