@@ -755,7 +755,7 @@ __device__ void warp_select_keys(const uint32_t* keys, int n, int k, uint32_t* h
         }
         const uint32_t excl = incl - sum;
         const bool mine = excl < kk && kk <= incl;
-        uint32_t b = 0, below = 0;
+        uint32_t b = 0, below = 0, cb = 0;
         if (mine) {
             uint32_t run = excl;
 #pragma unroll
@@ -763,6 +763,7 @@ __device__ void warp_select_keys(const uint32_t* keys, int n, int k, uint32_t* h
                 if (run + c[j] >= kk) {
                     b = (uint32_t)(lane * 8 + j);
                     below = run;
+                    cb = c[j];
                     break;
                 }
                 run += c[j];
@@ -771,11 +772,26 @@ __device__ void warp_select_keys(const uint32_t* keys, int n, int k, uint32_t* h
         const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
         b = __shfl_sync(0xffffffffu, b, src);
         below = __shfl_sync(0xffffffffu, below, src);
+        cb = __shfl_sync(0xffffffffu, cb, src);
         prefix |= b << shift;
         mask |= 255u << shift;
         kk -= below;
         less += below;
         __syncwarp();
+        if (cb == 1u && shift > 0) {
+            // one key left under the prefix: it is the k-th, and no key
+            // below it shares the prefix
+            for (int i0 = 0; i0 < n; i0 += 32) {
+                const int i = i0 + lane;
+                const uint32_t key = i < n ? keys[i] : 0u;
+                const unsigned m = __ballot_sync(0xffffffffu, i < n && (key & mask) == prefix);
+                if (m) {
+                    prefix = __shfl_sync(0xffffffffu, key, __ffs(m) - 1);
+                    break;
+                }
+            }
+            break;
+        }
     }
     kth = prefix;
     n_less = (int)less;
