@@ -66,6 +66,7 @@ _SIGS = {
     "fg_search_u8": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, C.POINTER(SearchParams), _P, _P, _P, _SZ, _P],
     "fg_search_workspace_size": [C.POINTER(IvfpqView), C.POINTER(SearchParams), _I32, C.POINTER(_SZ)],
     "fg_search": [C.POINTER(IvfpqView), _P, _I64, _P, _I32, C.POINTER(SearchParams), _P, _P, _P, _SZ, _P],
+    "fg_host_memory_mapped": [_P, C.POINTER(C.c_int32)],
     "fg_map_ids": [_P, _I64, _P, _I64, _P, _P],
     "fg_merge_topk": [_P, _P, _I32, _I32, _I32, _P, _P, _P],
     "fg_kmeans_init": [_P, _I64, _I32, _I32, _U32, _P, _P, _SZ, _P],

@@ -299,6 +299,19 @@ int fg_search_u8(const fg_ivfpq_view* index, const uint8_t* base, int64_t nbase,
     return search_any(index, base, 1, nbase, queries, nq, params, out_ids, out_dists, ws, ws_bytes, stream);
 }
 
+int fg_host_memory_mapped(const void* p, int32_t* mapped) {
+    FG_REQUIRE(mapped, "null output");
+    *mapped = 0;
+    if (!p) return FG_OK;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        (void)cudaGetLastError();  // an unknown pointer is not mapped
+        return FG_OK;
+    }
+    *mapped = (at.type == cudaMemoryTypeHost && at.devicePointer == p) ? 1 : 0;
+    return FG_OK;
+}
+
 int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_t seed, float* centroids,
                    void* ws, size_t ws_bytes, void* stream) {
     FG_REQUIRE(data && centroids && n >= 1 && dim >= 1 && k >= 1, "bad k-means init arguments");

@@ -316,15 +316,20 @@ class IVFPQIndex:
                   _p(ids), _p(dist), _p(ws), ws.numel(), _stream(stream))
         return ids, dist
 
-    def search_host(self, queries, params: SearchParams | None = None, out=None, chunks: int = 2):
+    def search_host(self, queries, params: SearchParams | None = None, out=None, chunks: int = 2,
+                    zero_copy: bool | None = None):
         """Search host-resident queries into host-resident results with the
         copies overlapped: the batch is cut into `chunks` pieces on two
         streams, each stream with its own device buffers and workspace, so one
         piece's upload and download run on the copy engines while another
         piece's kernels run.  Pinned host buffers keep the copies asynchronous;
-        `out` = (ids, dists) host tensors [nq][final_k].  Returns them once the
-        current stream has been made to wait for every piece (synchronise
-        before reading them on the host)."""
+        `out` = (ids, dists) host tensors [nq][final_k].  When both are
+        page-locked, contiguous and mapped into the device's address space
+        (fg_host_memory_mapped), the rerank kernel writes the results into
+        them directly and no download follows the search (zero_copy=None
+        decides by that check, True requires it, False always copies).
+        Returns them once the current stream has been made to wait for every
+        piece (synchronise before reading them on the host)."""
         params = params or SearchParams()
         if self.base is None:
             raise ValueError("search needs the raw base vectors (build with keep_base=True)")
@@ -336,6 +341,10 @@ class IVFPQIndex:
             out = (torch.empty((nq, params.final_k), dtype=torch.int32).pin_memory(),
                    torch.empty((nq, params.final_k), dtype=torch.float32).pin_memory())
         hid, hdd = out
+        mapped = _host_mapped(hid) and _host_mapped(hdd)
+        if zero_copy and not mapped:
+            raise ValueError("zero_copy needs contiguous, page-locked, device-mapped result tensors")
+        zc = mapped if zero_copy is None else bool(zero_copy)
         chunks = max(1, min(int(chunks), nq)) if nq else 1
         per = (nq + chunks - 1) // chunks if nq else 0
         dev = self.device
@@ -363,10 +372,12 @@ class IVFPQIndex:
             st = state[c % 2]
             with torch.cuda.stream(st["stream"]):
                 st["q"][:n].copy_(hq[lo:hi], non_blocking=True)
+                oi, od = (hid[lo:hi], hdd[lo:hi]) if zc else (st["ids"], st["dd"])
                 _lib.call(fn, C.byref(self._view), _p(self.base), self.base.shape[0], _p(st["q"]), n, C.byref(cp),
-                          _p(st["ids"]), _p(st["dd"]), _p(st["ws"]), st["ws"].numel(), _stream(st["stream"]))
-                hid[lo:hi].copy_(st["ids"][:n], non_blocking=True)
-                hdd[lo:hi].copy_(st["dd"][:n], non_blocking=True)
+                          _p(oi), _p(od), _p(st["ws"]), st["ws"].numel(), _stream(st["stream"]))
+                if not zc:
+                    hid[lo:hi].copy_(st["ids"][:n], non_blocking=True)
+                    hdd[lo:hi].copy_(st["dd"][:n], non_blocking=True)
         for st in state:
             cur.wait_stream(st["stream"])
         return hid, hdd
@@ -385,6 +396,16 @@ class IVFPQIndex:
 
     def rerank(self, queries, top_ids, top_counts, params: SearchParams):
         return run_gpu_rerank(queries, top_ids, top_counts, self.base, params, self.device)
+
+
+def _host_mapped(t) -> bool:
+    """Whether kernels can write host tensor t in place: contiguous,
+    page-locked and mapped at its own address (fg_host_memory_mapped)."""
+    if t.device.type != "cpu" or not t.is_contiguous() or not t.is_pinned() or t.numel() == 0:
+        return False
+    m = C.c_int32(0)
+    _lib.call("fg_host_memory_mapped", C.c_void_p(t.data_ptr()), C.byref(m))
+    return m.value == 1
 
 
 class SearchGraph:

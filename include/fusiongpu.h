@@ -178,6 +178,14 @@ int fg_search(const fg_ivfpq_view* index, const float* base, int64_t nbase, cons
 int fg_search_u8(const fg_ivfpq_view* index, const uint8_t* base, int64_t nbase, const float* queries,
                  int32_t nq, const fg_search_params* params, int32_t* out_ids, float* out_dists,
                  void* workspace, size_t workspace_bytes, void* stream);
+/* *mapped = 1 when kernels on the current device can read and write the host
+ * memory at p through the address p itself (page-locked memory under unified
+ * addressing), else 0.  Such memory may be passed as out_ids / out_dists of
+ * fg_search: the rerank kernel then writes the results straight into host
+ * memory, so no device-to-host copy follows the search.  No counterpart in the
+ * reference, which copies results back after each batch
+ * (search_pipeline.cu:311-377). */
+int fg_host_memory_mapped(const void* p, int32_t* mapped);
 
 /* ---- sharded search: the exchange step (no counterpart in the single-GPU
  * reference, whose search runs on device 0 only, search_pipeline.cu:560).

@@ -431,19 +431,56 @@ def test_sampled_kmeans_build_bit_exact(fg):
         np.testing.assert_array_equal(got[k], eidx[k])
 
 
+@pytest.mark.parametrize("zero_copy", [True, False])
 @pytest.mark.parametrize("chunks", [1, 2, 3])
-def test_search_host_matches_device_search(fg, chunks):
+def test_search_host_matches_device_search(fg, chunks, zero_copy):
     """The pipelined host-buffer search (pieces on two streams) returns the
-    device search's results."""
+    device search's results, whether the rerank writes the pinned result
+    tensors in place or the results are copied back; a second call into the
+    same buffers overwrites every entry."""
     index, base, q = dataset("int128")
     idx = fg.IVFPQIndex.from_arrays(index, base)
     p = _params(fg, "c1", False)
     ids, d = idx.search(q, p)
     hq = torch.from_numpy(np.ascontiguousarray(q)).pin_memory()
-    hi, hd = idx.search_host(hq, p, chunks=chunks)
-    torch.cuda.synchronize()
-    np.testing.assert_array_equal(hi.numpy(), _np(ids))
-    np.testing.assert_array_equal(hd.numpy(), _np(d))
+    out = (torch.full((q.shape[0], p.final_k), -7, dtype=torch.int32).pin_memory(),
+           torch.full((q.shape[0], p.final_k), -7.0, dtype=torch.float32).pin_memory())
+    for _ in range(2):
+        hi, hd = idx.search_host(hq, p, out=out, chunks=chunks, zero_copy=zero_copy)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(hi.numpy(), _np(ids))
+        np.testing.assert_array_equal(hd.numpy(), _np(d))
+        out[0].fill_(-7)
+        out[1].fill_(-7.0)
+
+
+def test_host_memory_mapped_query(fg):
+    """Pinned host memory is reported mapped, pageable host memory and device
+    memory are not, so the zero-copy result path never hands a kernel memory
+    it cannot reach."""
+    import ctypes as C
+    from fusiongpu_b200 import _lib
+
+    def mapped(ptr):
+        m = C.c_int32(-1)
+        _lib.call("fg_host_memory_mapped", C.c_void_p(ptr), C.byref(m))
+        return m.value
+
+    pinned = torch.zeros(1024, dtype=torch.int32).pin_memory()
+    pageable = np.zeros(1024, dtype=np.int32)
+    dev = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    assert mapped(pinned.data_ptr()) == 1
+    assert mapped(pinned.data_ptr() + 64) == 1
+    assert mapped(pageable.ctypes.data) == 0
+    assert mapped(dev.data_ptr()) == 0
+    assert mapped(0) == 0
+    with pytest.raises(ValueError):
+        index, base, q = dataset("int128")
+        idx = fg.IVFPQIndex.from_arrays(index, base)
+        p = _params(fg, "c1", False)
+        out = (torch.empty((q.shape[0], p.final_k), dtype=torch.int32),
+               torch.empty((q.shape[0], p.final_k), dtype=torch.float32))
+        idx.search_host(torch.from_numpy(np.ascontiguousarray(q)), p, out=out, zero_copy=True)
 
 
 def test_search_graph_replay_matches_eager(fg):
