@@ -333,10 +333,38 @@ class IVFPQIndex:
         params = params or SearchParams()
         if self.base is None:
             raise ValueError("search needs the raw base vectors (build with keep_base=True)")
-        hq = torch.as_tensor(queries, dtype=torch.float32)
+        hq = queries if isinstance(queries, torch.Tensor) and queries.dtype == torch.float32 else \
+            torch.as_tensor(queries, dtype=torch.float32)
         if hq.device.type != "cpu":
             raise ValueError("search_host takes host queries")
         nq = hq.shape[0]
+        chunks = max(1, min(int(chunks), nq)) if nq else 1
+        per = (nq + chunks - 1) // chunks if nq else 0
+        dev = self.device
+        # streams, device buffers, workspaces and the C parameter block are
+        # kept for the next call with the same piece size and parameters
+        key = (per, *vars(params).values())
+        hs = getattr(self, "_host_state", None)
+        if hs is None or hs[0] != key:
+            ws_bytes = self.workspace_bytes(max(per, 1), params)
+            state = []
+            for _ in range(2):
+                state.append(dict(stream=torch.cuda.Stream(device=dev),
+                                  q=torch.empty((max(per, 1), self.dim), dtype=torch.float32, device=dev),
+                                  ids=torch.empty((max(per, 1), params.final_k), dtype=torch.int32, device=dev),
+                                  dd=torch.empty((max(per, 1), params.final_k), dtype=torch.float32, device=dev),
+                                  ws=_workspace(ws_bytes, dev)))
+            self._host_state = hs = (key, state, params.c())
+        state, cp = hs[1], hs[2]
+        cur = torch.cuda.current_stream(dev)
+        for st in state:
+            st["stream"].wait_stream(cur)
+        pieces = [(lo, min(nq, lo + per)) for lo in range(0, nq, max(per, 1))]
+        # each stream's first upload goes out before the per-call checks below
+        for c, (lo, hi) in enumerate(pieces[:2]):
+            st = state[c % 2]
+            with torch.cuda.stream(st["stream"]):
+                st["q"][:hi - lo].copy_(hq[lo:hi], non_blocking=True)
         if out is None:
             out = (torch.empty((nq, params.final_k), dtype=torch.int32).pin_memory(),
                    torch.empty((nq, params.final_k), dtype=torch.float32).pin_memory())
@@ -345,33 +373,13 @@ class IVFPQIndex:
         if zero_copy and not mapped:
             raise ValueError("zero_copy needs contiguous, page-locked, device-mapped result tensors")
         zc = mapped if zero_copy is None else bool(zero_copy)
-        chunks = max(1, min(int(chunks), nq)) if nq else 1
-        per = (nq + chunks - 1) // chunks if nq else 0
-        dev = self.device
-        key = (per, params.final_k, self.workspace_bytes(max(per, 1), params))
-        if getattr(self, "_host_state", None) is None or self._host_state[0] != key:
-            state = []
-            for _ in range(2):
-                state.append(dict(stream=torch.cuda.Stream(device=dev),
-                                  q=torch.empty((max(per, 1), self.dim), dtype=torch.float32, device=dev),
-                                  ids=torch.empty((max(per, 1), params.final_k), dtype=torch.int32, device=dev),
-                                  dd=torch.empty((max(per, 1), params.final_k), dtype=torch.float32, device=dev),
-                                  ws=_workspace(key[2], dev)))
-            self._host_state = (key, state)
-        state = self._host_state[1]
-        cur = torch.cuda.current_stream(dev)
-        for st in state:
-            st["stream"].wait_stream(cur)
-        cp = params.c()
         fn = "fg_search_u8" if self.base.dtype == torch.uint8 else "fg_search"
-        for c in range(chunks):
-            lo, hi = c * per, min(nq, (c + 1) * per)
-            if lo >= hi:
-                break
+        for c, (lo, hi) in enumerate(pieces):
             n = hi - lo
             st = state[c % 2]
             with torch.cuda.stream(st["stream"]):
-                st["q"][:n].copy_(hq[lo:hi], non_blocking=True)
+                if c >= 2:
+                    st["q"][:n].copy_(hq[lo:hi], non_blocking=True)
                 oi, od = (hid[lo:hi], hdd[lo:hi]) if zc else (st["ids"], st["dd"])
                 _lib.call(fn, C.byref(self._view), _p(self.base), self.base.shape[0], _p(st["q"]), n, C.byref(cp),
                           _p(oi), _p(od), _p(st["ws"]), st["ws"].numel(), _stream(st["stream"]))
