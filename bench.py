@@ -227,6 +227,7 @@ def main():
 
     # ---- end to end through the public API: pinned host queries in, host results out
     E2E_CHUNKS = int(os.environ.get("FG_E2E_CHUNKS", "2"))
+    E2E_GRAPH = os.environ.get("FG_E2E_GRAPH", "1") != "0"  # one graph launch per step
     e2e_pts = []
     hq = torch.from_numpy(queries).pin_memory()
     for s in sweep:
@@ -235,8 +236,9 @@ def main():
         hdd = torch.empty((nq, p.final_k), dtype=torch.float32).pin_memory()
 
         def one():
-            # the public host-buffer call: uploads and downloads overlap the kernels
-            idx.search_host(hq, p, out=(hid, hdd), chunks=E2E_CHUNKS)
+            # the public host-buffer call: uploads, kernels and result writes replayed
+            # as one CUDA graph (captured in the first warm-up call)
+            idx.search_host(hq, p, out=(hid, hdd), chunks=E2E_CHUNKS, graph=E2E_GRAPH)
 
         for _ in range(max(1, args.warmup)):
             one()

@@ -317,7 +317,7 @@ class IVFPQIndex:
         return ids, dist
 
     def search_host(self, queries, params: SearchParams | None = None, out=None, chunks: int = 2,
-                    zero_copy: bool | None = None):
+                    zero_copy: bool | None = None, graph: bool = False, _mapped: bool | None = None):
         """Search host-resident queries into host-resident results with the
         copies overlapped: the batch is cut into `chunks` pieces on two
         streams, each stream with its own device buffers and workspace, so one
@@ -329,8 +329,18 @@ class IVFPQIndex:
         them directly and no download follows the search (zero_copy=None
         decides by that check, True requires it, False always copies).
         Returns them once the current stream has been made to wait for every
-        piece (synchronise before reading them on the host)."""
+        piece (synchronise before reading them on the host).
+
+        graph=True replays the whole step -- uploads, kernels and result
+        writes -- as one CUDA graph, captured on the first call for these
+        host buffers and parameters (the graph holds their addresses: keep
+        the same pinned query and result tensors between calls and overwrite
+        their contents; other buffers capture another graph).  One launch per
+        call then replaces about a dozen, so host delays no longer stall the
+        GPU between them."""
         params = params or SearchParams()
+        if graph:
+            return self._search_host_graph(queries, params, out, chunks, zero_copy)
         if self.base is None:
             raise ValueError("search needs the raw base vectors (build with keep_base=True)")
         hq = queries if isinstance(queries, torch.Tensor) and queries.dtype == torch.float32 else \
@@ -369,7 +379,7 @@ class IVFPQIndex:
             out = (torch.empty((nq, params.final_k), dtype=torch.int32).pin_memory(),
                    torch.empty((nq, params.final_k), dtype=torch.float32).pin_memory())
         hid, hdd = out
-        mapped = _host_mapped(hid) and _host_mapped(hdd)
+        mapped = _mapped if _mapped is not None else (_host_mapped(hid) and _host_mapped(hdd))
         if zero_copy and not mapped:
             raise ValueError("zero_copy needs contiguous, page-locked, device-mapped result tensors")
         zc = mapped if zero_copy is None else bool(zero_copy)
@@ -388,6 +398,35 @@ class IVFPQIndex:
                     hdd[lo:hi].copy_(st["dd"][:n], non_blocking=True)
         for st in state:
             cur.wait_stream(st["stream"])
+        return hid, hdd
+
+    def _search_host_graph(self, queries, params: SearchParams, out, chunks: int, zero_copy: bool | None):
+        hq = queries if isinstance(queries, torch.Tensor) and queries.dtype == torch.float32 else None
+        if hq is None or hq.device.type != "cpu" or not hq.is_pinned() or not hq.is_contiguous():
+            raise ValueError("search_host(graph=True) takes a contiguous pinned float32 query tensor")
+        nq = hq.shape[0]
+        if out is None:
+            raise ValueError("search_host(graph=True) needs the result tensors (out=) it is captured for")
+        hid, hdd = out
+        if not (hid.is_pinned() and hdd.is_pinned()):
+            raise ValueError("search_host(graph=True) needs pinned result tensors")
+        key = (hq.data_ptr(), nq, hid.data_ptr(), hdd.data_ptr(), tuple(hid.shape), int(chunks), zero_copy,
+               *vars(params).values())
+        graphs = self.__dict__.setdefault("_host_graphs", {})
+        g = graphs.get(key)
+        if g is None:
+            mapped = _host_mapped(hid) and _host_mapped(hdd)
+            # an eager call first: it sets up the streams, buffers and workspace
+            # the graph will use, and the kernels' shared-memory attributes
+            self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped)
+            if len(graphs) >= 8:
+                graphs.pop(next(iter(graphs)))
+            graphs[key] = g
+        g.replay()
         return hid, hdd
 
     def capture(self, nq: int, params: SearchParams | None = None) -> "SearchGraph":

@@ -454,6 +454,29 @@ def test_search_host_matches_device_search(fg, chunks, zero_copy):
         out[1].fill_(-7.0)
 
 
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_search_host_graph_replays_new_queries(fg, chunks):
+    """search_host(graph=True): the first call captures, later calls replay
+    the graph on whatever the pinned query tensor holds by then, and each
+    replay's results equal the device search of those queries."""
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    p = _params(fg, "c1", False)
+    n = q.shape[0] // 2
+    hq = torch.empty((n, q.shape[1]), dtype=torch.float32).pin_memory()
+    out = (torch.empty((n, p.final_k), dtype=torch.int32).pin_memory(),
+           torch.empty((n, p.final_k), dtype=torch.float32).pin_memory())
+    for rows in (slice(0, n), slice(n, 2 * n), slice(0, n)):
+        qs = np.ascontiguousarray(q[rows])
+        hq.copy_(torch.from_numpy(qs))
+        out[0].fill_(-7)
+        hi, hd = idx.search_host(hq, p, out=out, chunks=chunks, graph=True)
+        torch.cuda.synchronize()
+        ids, d = idx.search(qs, p)
+        np.testing.assert_array_equal(hi.numpy(), _np(ids))
+        np.testing.assert_array_equal(hd.numpy(), _np(d))
+
+
 def test_host_memory_mapped_query(fg):
     """Pinned host memory is reported mapped, pageable host memory and device
     memory are not, so the zero-copy result path never hands a kernel memory
