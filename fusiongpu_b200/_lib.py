@@ -70,7 +70,8 @@ _SIGS = {
     "fg_map_ids": [_P, _I64, _P, _I64, _P, _P],
     "fg_merge_topk": [_P, _P, _I32, _I32, _I32, _P, _P, _P],
     "fg_kmeans_init": [_P, _I64, _I32, _I32, _U32, _P, _P, _SZ, _P],
-    "fg_assign": [_P, _I64, _I32, _P, _I32, _P, _P],
+    "fg_assign_workspace_size": [_I64, _I32, _I32, _P],
+    "fg_assign": [_P, _I64, _I32, _P, _I32, _P, _P, _SZ, _P],
     "fg_sort_by_list_workspace_size": [_I64, _I32, C.POINTER(_SZ)],
     "fg_sort_by_list": [_P, _I64, _I32, _P, _P, _P, _SZ, _P],
     "fg_kmeans_update": [_P, _I32, _P, _P, _I32, _P, _P],

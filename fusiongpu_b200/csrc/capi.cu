@@ -321,20 +321,23 @@ int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_
     return rc;
 }
 
+int fg_assign_workspace_size(int64_t n, int32_t dim, int32_t k, size_t* bytes) {
+    FG_REQUIRE(bytes && n >= 0 && dim >= 1 && k >= 1, "bad arguments");
+    *bytes = assign_workspace(n, k, dim);
+    return FG_OK;
+}
+
 int fg_assign(const float* data, int64_t n, int32_t dim, const float* centroids, int32_t k, int32_t* out_assign,
-              void* stream) {
+              void* ws, size_t ws_bytes, void* stream) {
     FG_REQUIRE(n >= 0 && dim >= 1 && k >= 1, "bad assign shape");
     if (n == 0) return FG_OK;
     FG_REQUIRE(data && centroids && out_assign, "null buffer");
     cudaStream_t s = as_stream(stream);
     const size_t wb = assign_workspace(n, k, dim);
     if (!wb) return l2_argmin(data, n, centroids, k, dim, out_assign, s);
-    // tensor-core path: stream-ordered scratch, released after the last use
-    void* ws = nullptr;
-    FG_CUDA_TRY(cudaMallocAsync(&ws, wb, s));
-    const int rc = assign_auto(data, n, dim, centroids, k, out_assign, ws, wb, s);
-    FG_CUDA_TRY(cudaFreeAsync(ws, s));
-    return rc;
+    int rc = need_ws(ws, ws_bytes, wb);
+    if (rc) return rc;
+    return assign_auto(data, n, dim, centroids, k, out_assign, ws, ws_bytes, s);
 }
 
 int fg_sort_by_list_workspace_size(int64_t n, int32_t k, size_t* bytes) {

@@ -1,8 +1,6 @@
 // noalloc.cu -- a coarse search that allocates nothing and takes no workspace.
 //
 // Some callers cannot hand this library device memory at call time:
-//   * code that runs while a CUDA stream is being captured into a graph
-//     (cudaMalloc is not allowed during capture and would break it);
 //   * plugins hosted inside another runtime that owns every device pool and
 //     forbids its plugins from calling the CUDA allocator;
 //   * latency-critical serving loops that must never hit cudaMalloc/cudaFree,
@@ -14,8 +12,11 @@
 //
 // The array's name is only a host-side handle: host code must never pass it
 // to a kernel.  Its device address is resolved with cudaGetSymbolAddress once
-// per device, the first time the entry point runs with that device current;
-// make that first call outside stream capture.
+// per device, the first time the entry point runs with that device current,
+// and cached for the life of the process; make that first call before any
+// stream capture.  cudaDeviceReset unloads the library's device image, so a
+// process that resets a device must not call this entry point there again:
+// the cached address would point at the old image.
 //
 // All calls on one device share the array.  Calls whose GPU work overlaps
 // (different streams, or different host threads) race on it and may return

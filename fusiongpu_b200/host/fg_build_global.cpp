@@ -67,7 +67,10 @@ int main(int argc, char** argv) {
 
     std::cout << "Training " << k << " initial centroids (GPU)..." << std::endl;
     stage("k-means", [&] { check(fg_kmeans(x.p, n, dim, k, km_iters, seed, cen.p, ws.p, wsb, nullptr), "fg_kmeans"); });
-    stage("assign", [&] { check(fg_assign(x.p, n, dim, cen.p, k, as.p, nullptr), "fg_assign"); });
+    size_t awb = 0;
+    check(fg_assign_workspace_size(n, dim, k, &awb), "fg_assign_workspace_size");
+    DevBuf<uint8_t> aws(awb ? awb : 256);
+    stage("assign", [&] { check(fg_assign(x.p, n, dim, cen.p, k, as.p, aws.p, awb, nullptr), "fg_assign"); });
 
     int nlist = k;
     DevBuf<float> fcen;

@@ -94,7 +94,10 @@ def gpu_assign_to_centroids(data, centroids, device="cuda") -> torch.Tensor:
     x = _dev(data, torch.float32, device)
     c = _dev(centroids, torch.float32, device)
     out = torch.empty(x.shape[0], dtype=torch.int32, device=device)
-    _lib.call("fg_assign", _p(x), x.shape[0], x.shape[1], _p(c), c.shape[0], _p(out), _stream())
+    wb = _lib.size_query("fg_assign_workspace_size", x.shape[0], x.shape[1], c.shape[0])
+    ws = _workspace(wb, device)
+    _lib.call("fg_assign", _p(x), x.shape[0], x.shape[1], _p(c), c.shape[0], _p(out), _p(ws), ws.numel(),
+              _stream())
     return out
 
 
@@ -296,9 +299,12 @@ class IVFPQIndex:
             self._ws = _workspace(need, self.device)
         return self._ws
 
-    def search(self, queries, params: SearchParams | None = None, out=None, stream=None):
+    def search(self, queries, params: SearchParams | None = None, out=None, stream=None, ws=None):
         """Full search: exact coarse -> candidate generation -> rerank.
-        Returns (ids [nq][final_k] int32, dists [nq][final_k] float32)."""
+        Returns (ids [nq][final_k] int32, dists [nq][final_k] float32).
+        `ws` is a caller-owned uint8 device workspace of at least
+        workspace_bytes(nq, params); without it the index's shared one is used
+        (grown on demand, so a captured graph must pass its own)."""
         params = params or SearchParams()
         if self.base is None:
             raise ValueError("search needs the raw base vectors (build with keep_base=True)")
@@ -309,7 +315,8 @@ class IVFPQIndex:
             dist = torch.empty((nq, params.final_k), dtype=torch.float32, device=self.device)
         else:
             ids, dist = out
-        ws = self.workspace(nq, params)
+        if ws is None:
+            ws = self.workspace(nq, params)
         cp = params.c()
         fn = "fg_search_u8" if self.base.dtype == torch.uint8 else "fg_search"
         _lib.call(fn, C.byref(self._view), _p(self.base), self.base.shape[0], _p(q), nq, C.byref(cp),
@@ -317,7 +324,8 @@ class IVFPQIndex:
         return ids, dist
 
     def search_host(self, queries, params: SearchParams | None = None, out=None, chunks: int = 2,
-                    zero_copy: bool | None = None, graph: bool = False, _mapped: bool | None = None):
+                    zero_copy: bool | None = None, graph: bool = False, _mapped: bool | None = None,
+                    _state=None):
         """Search host-resident queries into host-resident results with the
         copies overlapped: the batch is cut into `chunks` pieces on two
         streams, each stream with its own device buffers and workspace, so one
@@ -353,18 +361,12 @@ class IVFPQIndex:
         dev = self.device
         # streams, device buffers, workspaces and the C parameter block are
         # kept for the next call with the same piece size and parameters
-        key = (per, *vars(params).values())
-        hs = getattr(self, "_host_state", None)
-        if hs is None or hs[0] != key:
-            ws_bytes = self.workspace_bytes(max(per, 1), params)
-            state = []
-            for _ in range(2):
-                state.append(dict(stream=torch.cuda.Stream(device=dev),
-                                  q=torch.empty((max(per, 1), self.dim), dtype=torch.float32, device=dev),
-                                  ids=torch.empty((max(per, 1), params.final_k), dtype=torch.int32, device=dev),
-                                  dd=torch.empty((max(per, 1), params.final_k), dtype=torch.float32, device=dev),
-                                  ws=_workspace(ws_bytes, dev)))
-            self._host_state = hs = (key, state, params.c())
+        # (a captured graph passes the state it owns instead)
+        hs = _state
+        if hs is None:
+            hs = getattr(self, "_host_state", None)
+            if hs is None or hs[0] != self._host_key(per, params):
+                self._host_state = hs = self._new_host_state(per, params)
         state, cp = hs[1], hs[2]
         cur = torch.cuda.current_stream(dev)
         for st in state:
@@ -400,6 +402,24 @@ class IVFPQIndex:
             cur.wait_stream(st["stream"])
         return hid, hdd
 
+    @staticmethod
+    def _host_key(per: int, params: SearchParams):
+        return (per, *vars(params).values())
+
+    def _new_host_state(self, per: int, params: SearchParams):
+        """Two streams, each with its own device query/result buffers and
+        workspace for pieces of `per` queries, plus the C parameter block."""
+        dev = self.device
+        ws_bytes = self.workspace_bytes(max(per, 1), params)
+        state = []
+        for _ in range(2):
+            state.append(dict(stream=torch.cuda.Stream(device=dev),
+                              q=torch.empty((max(per, 1), self.dim), dtype=torch.float32, device=dev),
+                              ids=torch.empty((max(per, 1), params.final_k), dtype=torch.int32, device=dev),
+                              dd=torch.empty((max(per, 1), params.final_k), dtype=torch.float32, device=dev),
+                              ws=_workspace(ws_bytes, dev)))
+        return (self._host_key(per, params), state, params.c())
+
     def _search_host_graph(self, queries, params: SearchParams, out, chunks: int, zero_copy: bool | None):
         hq = queries if isinstance(queries, torch.Tensor) and queries.dtype == torch.float32 else None
         if hq is None or hq.device.type != "cpu" or not hq.is_pinned() or not hq.is_contiguous():
@@ -413,20 +433,24 @@ class IVFPQIndex:
         key = (hq.data_ptr(), nq, hid.data_ptr(), hdd.data_ptr(), tuple(hid.shape), int(chunks), zero_copy,
                *vars(params).values())
         graphs = self.__dict__.setdefault("_host_graphs", {})
-        g = graphs.get(key)
-        if g is None:
+        entry = graphs.get(key)
+        if entry is None:
             mapped = _host_mapped(hid) and _host_mapped(hdd)
-            # an eager call first: it sets up the streams, buffers and workspace
-            # the graph will use, and the kernels' shared-memory attributes
-            self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped)
+            nch = max(1, min(int(chunks), nq)) if nq else 1
+            per = (nq + nch - 1) // nch if nq else 0
+            # the graph owns its streams, buffers and workspace: the addresses it
+            # replays stay valid whatever other calls do with theirs
+            state = self._new_host_state(per, params)
+            # an eager call first: it sets the kernels' shared-memory attributes
+            self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped, _state=state)
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped)
+                self.search_host(hq, params, out, chunks, zero_copy, _mapped=mapped, _state=state)
             if len(graphs) >= 8:
                 graphs.pop(next(iter(graphs)))
-            graphs[key] = g
-        g.replay()
+            graphs[key] = entry = (g, state)
+        entry[0].replay()
         return hid, hdd
 
     def capture(self, nq: int, params: SearchParams | None = None) -> "SearchGraph":
@@ -465,15 +489,18 @@ class SearchGraph:
         self.queries = torch.zeros((nq, index.dim), dtype=torch.float32, device=dev)
         self.ids = torch.empty((nq, params.final_k), dtype=torch.int32, device=dev)
         self.dists = torch.empty((nq, params.final_k), dtype=torch.float32, device=dev)
-        index.workspace(nq, params)  # allocate before capture
+        # the graph's own workspace, allocated before capture and held as long as
+        # the graph: the index's shared workspace may be replaced by a larger
+        # search, and eager searches on other streams use it concurrently
+        self.ws = _workspace(index.workspace_bytes(nq, params), dev)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):  # warm up (attributes, tensor maps) outside the graph
-            index.search(self.queries, params, out=(self.ids, self.dists))
+            index.search(self.queries, params, out=(self.ids, self.dists), ws=self.ws)
         torch.cuda.current_stream(dev).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            index.search(self.queries, params, out=(self.ids, self.dists))
+            index.search(self.queries, params, out=(self.ids, self.dists), ws=self.ws)
 
     def replay(self, queries=None):
         if queries is not None:

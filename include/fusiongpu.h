@@ -109,15 +109,18 @@ int fg_coarse_search_tc(const float* centroids, int32_t nlist, int32_t dim, cons
 
 /* ---- allocation-free coarse search (no counterpart in the reference)
  * For callers that cannot give this library device memory when they call it:
- * code inside CUDA stream capture, plugins whose host runtime owns all device
- * pools, serving loops that must never reach cudaMalloc.  Same results as
+ * plugins whose host runtime owns every device pool and forbids its plugins
+ * the CUDA allocator, and serving loops that must never reach cudaMalloc or
+ * cudaFree (both can synchronise the whole device).  Same results as
  * fg_coarse_search_simt, with the scratch in a fixed 16 MiB device array built
  * into the library (held on every GPU that loads it).  Returns
  * FG_ERR_INVALID_ARG when one query's scratch row (4*nlist bytes, plus
  * 8*top_m per 8192 centroids past the first 8192) exceeds it.  The first call
- * on each device resolves the array's address; make it outside stream
- * capture.  All calls on a device share the array: calls whose GPU work
- * overlaps race and must be serialised by the caller. */
+ * on each device resolves the array's address and caches it for the life of
+ * the process; make that first call before any stream capture, and do not
+ * call this entry point on a device after cudaDeviceReset there (the cached
+ * address would be stale).  All calls on a device share the array: calls
+ * whose GPU work overlaps race and must be serialised by the caller. */
 int fg_coarse_search_noalloc(const float* centroids, int32_t nlist, int32_t dim, const float* queries,
                              int32_t nq, int32_t top_m, uint32_t* out_ids, float* out_dists,
                              void* stream);
@@ -324,10 +327,12 @@ int fg_kmeans_init(const float* data, int64_t n, int32_t dim, int32_t k, uint32_
  * gpu_assign_to_centroids / gpu_assign_initial_clusters (kmeans_gpu.cuh:329-394).
  * For dim <= 128 (k >= 64, n >= 4096) the assignment runs on the tensor cores
  * (the coarse search with top_m = 1: split-bf16 tcgen05 GEMM, exact rescore,
- * certificate or exact fallback) with stream-ordered scratch; the result is
- * identical to the CUDA-core path.  fg_kmeans uses the same dispatch. */
+ * certificate or exact fallback) in the caller's workspace (at least
+ * fg_assign_workspace_size bytes; 0 when the CUDA-core path runs); the result
+ * is identical to the CUDA-core path.  fg_kmeans uses the same dispatch. */
+int fg_assign_workspace_size(int64_t n, int32_t dim, int32_t k, size_t* bytes);
 int fg_assign(const float* data, int64_t n, int32_t dim, const float* centroids, int32_t k,
-              int32_t* out_assign, void* stream);
+              int32_t* out_assign, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Stable counting sort of point ids by assignment: order[] lists the points
  * of cluster 0, then cluster 1, ... each in increasing id; offsets [k+1]. */

@@ -197,10 +197,13 @@ void run_kmeans_gpu(const float* h_data, int n, int dim, int k, std::vector<floa
 void gpu_assign_to_centroids(const float* h_data, const float* h_centroids, int n, int dim, int k,
                              std::vector<int>& assignments) {
     using namespace fg_compat_detail;
-    DevBuf x((size_t)n * dim * 4), c((size_t)k * dim * 4), a((size_t)n * 4);
+    size_t wb = 0;
+    if (!ok(fg_assign_workspace_size(n, dim, k, &wb), "gpu_assign_to_centroids")) return;
+    DevBuf x((size_t)n * dim * 4), c((size_t)k * dim * 4), a((size_t)n * 4), ws(wb ? wb : 256);
     cudaMemcpy(x.p, h_data, (size_t)n * dim * 4, cudaMemcpyHostToDevice);
     cudaMemcpy(c.p, h_centroids, (size_t)k * dim * 4, cudaMemcpyHostToDevice);
-    if (!ok(fg_assign(x.as<float>(), n, dim, c.as<float>(), k, a.as<int32_t>(), nullptr), "gpu_assign_to_centroids"))
+    if (!ok(fg_assign(x.as<float>(), n, dim, c.as<float>(), k, a.as<int32_t>(), ws.p, wb, nullptr),
+            "gpu_assign_to_centroids"))
         return;
     assignments.resize(n);
     cudaMemcpy(assignments.data(), a.p, (size_t)n * 4, cudaMemcpyDeviceToHost);

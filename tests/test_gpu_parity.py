@@ -517,3 +517,52 @@ def test_search_graph_replay_matches_eager(fg):
         ei, ed = idx.search(qb, p)
         np.testing.assert_array_equal(_np(ids), _np(ei))
         np.testing.assert_array_equal(_np(d), _np(ed))
+
+
+def test_search_host_graphs_of_two_settings_alternate(fg):
+    """Two search_host(graph=True) settings (piece count and rerank depth)
+    used in turn: each replay keeps the streams, buffers and workspace it was
+    captured with, so every replay still equals the device search."""
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    pa = _params(fg, "c1", False)
+    pb = pa.replace(rerank_m=max(pa.final_k, pa.rerank_m // 2))
+    n = q.shape[0] // 2
+    hq = torch.empty((n, q.shape[1]), dtype=torch.float32).pin_memory()
+    outs = {}
+    for rows, p, chunks in ((slice(0, n), pa, 1), (slice(n, 2 * n), pb, 2), (slice(n, 2 * n), pa, 1),
+                            (slice(0, n), pb, 2), (slice(0, n), pa, 1)):
+        key = (p.rerank_m, chunks)
+        if key not in outs:
+            outs[key] = (torch.empty((n, p.final_k), dtype=torch.int32).pin_memory(),
+                         torch.empty((n, p.final_k), dtype=torch.float32).pin_memory())
+        out = outs[key]
+        qs = np.ascontiguousarray(q[rows])
+        hq.copy_(torch.from_numpy(qs))
+        out[0].fill_(-7)
+        # an eager host search with yet another piece size replaces the cached eager state
+        idx.search_host(torch.from_numpy(qs[:17]).pin_memory(), p, chunks=3)
+        hi, hd = idx.search_host(hq, p, out=out, chunks=chunks, graph=True)
+        torch.cuda.synchronize()
+        ids, d = idx.search(qs, p)
+        np.testing.assert_array_equal(hi.numpy(), _np(ids))
+        np.testing.assert_array_equal(hd.numpy(), _np(d))
+
+
+def test_search_graph_survives_a_larger_search(fg):
+    """A captured SearchGraph holds its own workspace: a later, larger eager
+    search (which grows the index's shared workspace) leaves the replay
+    correct."""
+    index, base, q = dataset("int128")
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    p = fg.SearchParams(**PARAMS["c1"])
+    g = idx.capture(32, p)
+    big = torch.from_numpy(np.ascontiguousarray(np.concatenate([q] * 4))).cuda()
+    idx.search(big, p)
+    for s in (0, 32, 64):
+        qb = torch.from_numpy(np.ascontiguousarray(q[s:s + 32])).cuda()
+        ids, d = g.replay(qb)
+        ei, ed = idx.search(qb, p)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(_np(ids), _np(ei))
+        np.testing.assert_array_equal(_np(d), _np(ed))

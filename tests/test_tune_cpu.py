@@ -107,9 +107,11 @@ def test_compat_header_compiles_for_reference_callers(tmp_path):
 
 
 def test_compat_header_compiles_with_reference_defs():
-    defs = os.path.join(os.environ.get("FG_REFERENCE_DIR", "/root/reference"), "defs.h")
-    if not os.path.exists(defs):
-        pytest.skip("reference sources not present")
+    import __graft_entry__
+    ref = __graft_entry__.reference_dir()
+    defs = os.path.join(ref, "defs.h")
+    if not ref or not os.path.exists(defs):
+        pytest.skip("reference sources not found (set FG_REFERENCE_DIR)")
     src = os.path.join(ROOT, "tests", "compat", "compat_search.cpp")
     r = subprocess.run(["/usr/bin/g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-include", defs,
                         "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "fusiongpu_b200", "host"),

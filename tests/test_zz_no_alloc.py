@@ -1,8 +1,8 @@
 """The allocation-free coarse search (fg_coarse_search_noalloc).
 
-It exists for callers that cannot pass device memory at call time -- code
-under CUDA stream capture, plugins whose host runtime owns every device pool,
-serving loops that must not reach cudaMalloc.  It must return exactly what the
+It exists for callers that cannot pass device memory at call time -- plugins
+whose host runtime owns every device pool, serving loops that must not reach
+cudaMalloc or cudaFree.  It must return exactly what the
 workspace-based exact path (fg_coarse_search_simt) returns, on consecutive
 calls that reuse its built-in scratch array.  This file sorts last so that a
 run stopping at the first failure has run every other test already.
