@@ -72,11 +72,29 @@ def interp_at_recall(points, target=RECALL_TARGET):
     return best[2], False
 
 
-def search_params(nprobe, SearchParams):
+def search_params(nprobe, SearchParams, ref_compat=False):
     return SearchParams(top_m=nprobe, p1_lists=CONFIG["p1_lists"], limit_k=CONFIG["limit_k"],
                         threshold_coeff=CONFIG["threshold_coeff"], prune_ratio=100.0,
                         rerank_m=CONFIG["rerank_m"], final_k=CONFIG["k"], mini_batch=CONFIG["mini_batch"],
-                        epsilon=CONFIG["epsilon"], beta=CONFIG["beta"], ref_compat=False)
+                        epsilon=CONFIG["epsilon"], beta=CONFIG["beta"], ref_compat=ref_compat)
+
+
+def oracle_kw(p):
+    return dict(top_m=p.top_m, p1_lists=p.p1_lists, limit_k=p.limit_k, threshold_coeff=p.threshold_coeff,
+                prune_ratio=p.prune_ratio, rerank_m=p.rerank_m, final_k=p.final_k, mini_batch=p.mini_batch,
+                epsilon=p.epsilon, beta=p.beta, ref_compat=bool(p.ref_compat))
+
+
+def compare_results(gi, gd, oi, od):
+    """(ids differing where the distances differ by more than 1e-5 relative,
+    the largest relative distance difference) between two [nq][k] results."""
+    gd = gd.astype(np.float64)
+    od = od.astype(np.float64)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        rel = np.where(gd == od, 0.0, np.abs(gd - od) / np.maximum(np.abs(od), 1e-30))
+    rel = np.nan_to_num(rel, nan=np.inf)
+    mism = int(((gi != oi) & (rel > 1e-5)).sum())
+    return mism, float(rel.max()) if rel.size else 0.0
 
 
 class ClockSampler:
@@ -143,9 +161,13 @@ def setup(device, quick):
     base, queries = ds.generate(spec)
     xb = torch.from_numpy(base).to(device)
     idx = IVFPQIndex.build(xb, nlist, CONFIG["pq_m"], kmeans_iters=20, pq_sample=50000, pq_iters=8, device=device)
-    gt, _ = knn_exact(xb, torch.from_numpy(queries).to(device), 10, device=device)
+    # the ground truth both arms use (exact_gt), and the library's own exact
+    # k-NN beside it as a check
+    gt = exact_gt(base, queries, 10, device)
+    g2, _ = knn_exact(xb, torch.from_numpy(queries).to(device), 10, device=device)
     torch.cuda.synchronize(device)
-    return dict(spec=spec, base=base, queries=queries, index=idx, gt=gt.cpu().numpy(), setup_s=time.time() - t0)
+    return dict(spec=spec, base=base, queries=queries, index=idx, gt=gt, setup_s=time.time() - t0,
+                gt_equals_knn_exact=bool(np.array_equal(gt, g2.cpu().numpy())))
 
 
 def main():
@@ -185,6 +207,8 @@ def main():
 
     if args.profile:
         return profile_stage(args, device)
+    if world > 1:
+        return main_sharded(args, rank, world, local, device, barrier, max_over_ranks)
     W = setup(device, args.quick)
     idx, queries, gt = W["index"], W["queries"], W["gt"]
     nq = queries.shape[0]
@@ -197,9 +221,11 @@ def main():
         # + bound + filter GEMM + finish; then the scan and the rerank
         return (4 if nprobe <= 4 else 6) + 2
     clocks = ClockSampler(local)
-    with clocks:
+
+    def run_sweep(ref_compat):
+        out = []
         for nprobe in (SWEEP if not args.nprobe else (args.nprobe,)):
-            p = search_params(nprobe, SearchParams)
+            p = search_params(nprobe, SearchParams, ref_compat)
             ids = torch.empty((nq, p.final_k), dtype=torch.int32, device=device)
             dd = torch.empty((nq, p.final_k), dtype=torch.float32, device=device)
             for _ in range(args.warmup):
@@ -219,11 +245,19 @@ def main():
             barrier()
             ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
             ms = max_over_ranks(ms)
-            sweep.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=world * nq / (ms / 1e3)))
+            out.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=world * nq / (ms / 1e3)))
+        return out
+
+    with clocks:
+        sweep = run_sweep(False)
+        # the reference's own output semantics (128-entry gather and rerank window)
+        sweep_rc = run_sweep(True)
 
     pts = [(s["nprobe"], s["recall"], s["qps"]) for s in sweep]
     value, met = interp_at_recall(pts)
     op = next((s for s in sweep if s["recall"] >= RECALL_TARGET), max(sweep, key=lambda s: s["recall"]))
+    rc_value, rc_met = interp_at_recall([(s["nprobe"], s["recall"], s["qps"]) for s in sweep_rc])
+    op_rc = next((s for s in sweep_rc if s["recall"] >= RECALL_TARGET), max(sweep_rc, key=lambda s: s["recall"]))
 
     # ---- end to end through the public API: pinned host queries in, host results out
     E2E_CHUNKS = int(os.environ.get("FG_E2E_CHUNKS", "2"))
@@ -278,22 +312,142 @@ def main():
         "config": dict(CONFIG, parallelism=f"replicas x{world} (full index per GPU, own 10k-query batch)",
                        l2="flushed (256 MB write) between timed steps",
                        recall_target_met=met, operating_nprobe=op["nprobe"],
-                       quick=bool(args.quick)),
+                       quick=bool(args.quick), lists=idx.nlist,
+                       recall_on=f"all {nq} queries (exact float64 ground truth; equals fg_knn_exact: "
+                                 f"{W['gt_equals_knn_exact']})"),
         "sweep": sweep,
+        "ref_compat": {"mode": "reference output semantics (ref_compat=1: 128-lane gather, 128-entry rerank "
+                               "window, phase-1 clamp, phase-2 overflow re-emission)",
+                       "value": rc_value, "recall_target_met": rc_met, "operating_nprobe": op_rc["nprobe"],
+                       "ms_per_step": op_rc["ms_per_step"], "sweep": sweep_rc},
         "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
-        "gpu_launches": sum(launches_per_step(s["nprobe"]) for s in sweep) * args.steps,
+        "gpu_launches": sum(launches_per_step(s["nprobe"]) for s in sweep + sweep_rc) * args.steps,
         "gpu_launches_per_step": launches_per_step(op["nprobe"]),
         "roofline": roof,
         "clocks": clocks.summary(),
         "setup_s": W["setup_s"],
     }
     if rank == 0 and world == 1 and not args.no_cpu:
-        out["cpu_baseline"] = cpu_baseline(W, op["nprobe"], args.cpu_sample)
+        out["cpu_baseline"], out["parity"] = cpu_baseline_and_parity(W, idx, qd, op["nprobe"], args.cpu_sample,
+                                                                     SearchParams)
+        out["ref_gpu"] = ref_gpu_block(W, idx, qd, args, device, SearchParams, flush)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def main_sharded(args, rank, world, local, device, barrier, max_over_ranks):
+    """C2 on N GPUs as the list-sharded search: every rank builds the same
+    (deterministic) index and keeps the lists LPT deals it, with their codes,
+    ids and raw vectors; the 10,000 queries go to every rank; each rank runs
+    the exact coarse search (centroids replicated), scans and reranks its own
+    lists, and one NCCL all-gather of packed (distance, global id) keys feeds
+    the device merge.  Strong scaling: the batch is the same at every N.
+    Times are CUDA events per rank, the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from fusiongpu_b200.index import SearchParams, recall_at
+    from fusiongpu_b200.sharded import ShardedIndex, elapsed_ms
+    W = setup(device, args.quick)
+    idx, queries, gt = W["index"], W["queries"], W["gt"]
+    host = idx.to_numpy()
+    nlists = idx.nlist
+    del idx, W["index"]
+    torch.cuda.empty_cache()
+    sh = ShardedIndex(host, W["base"], rank, world, device=device)
+    nq = queries.shape[0]
+    qd = torch.from_numpy(queries).to(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    sweep = []
+    clocks = ClockSampler(local)
+    with clocks:
+        for nprobe in (SWEEP if not args.nprobe else (args.nprobe,)):
+            p = search_params(nprobe, SearchParams)
+            for _ in range(args.warmup):
+                ids, dd = sh.search(qd, p)
+            torch.cuda.synchronize(device)
+            rec = recall_at(ids[:, :10].cpu().numpy(), gt[:, :10], 10)
+            barrier()
+            torch.cuda.synchronize(device)
+            tot = 0.0
+            stages = {}
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                sh.search(qd, p, timings=stages)
+                e1.record(stream)
+                e1.synchronize()
+                tot += e0.elapsed_time(e1)
+            barrier()
+            ms = max_over_ranks(tot / args.steps)
+            st = {k: max_over_ranks(v) for k, v in sorted(elapsed_ms(stages).items())}
+            sweep.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=nq / (ms / 1e3), stage_ms=st))
+    pts = [(s_["nprobe"], s_["recall"], s_["qps"]) for s_ in sweep]
+    value, met = interp_at_recall(pts)
+    op = next((s_ for s_ in sweep if s_["recall"] >= RECALL_TARGET), max(sweep, key=lambda s_: s_["recall"]))
+    # end to end: pinned host queries in, every rank's merged result back to pinned host memory
+    hq = torch.from_numpy(queries).pin_memory()
+    e2e_pts = []
+    for s_ in sweep:
+        p = search_params(s_["nprobe"], SearchParams)
+        hid = torch.empty((nq, p.final_k), dtype=torch.int32).pin_memory()
+        hdd = torch.empty((nq, p.final_k), dtype=torch.float32).pin_memory()
+        qdev = torch.empty_like(qd)
+        barrier()
+        tot = 0.0
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            qdev.copy_(hq, non_blocking=True)
+            r_ids, r_d = sh.search(qdev, p)
+            hid.copy_(r_ids, non_blocking=True)
+            hdd.copy_(r_d, non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= args.warmup:
+                tot += e0.elapsed_time(e1)
+        barrier()
+        ms = max_over_ranks(tot / args.steps)
+        s_["e2e_ms_per_step"] = ms
+        e2e_pts.append((s_["nprobe"], s_["recall"], nq / (ms / 1e3)))
+    e2e_value, _ = interp_at_recall(e2e_pts)
+    n_local = torch.tensor([sh.n_local], dtype=torch.int64, device=device)
+    all_local = [torch.zeros_like(n_local) for _ in range(world)]
+    dist.all_gather(all_local, n_local)
+    out = {
+        "metric": "QPS at recall@10=0.95 (C2 1M x 128 IVF-PQ)",
+        "value": value,
+        "unit": "queries/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": op["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture standing in for a dataset; index built on the GPU)",
+        "config": dict(CONFIG, parallelism=f"inverted lists dealt to {world} GPUs by length (LPT); queries "
+                                           "broadcast; exact coarse replicated; one NCCL all-gather of packed "
+                                           "(distance, global id) keys; device merge",
+                       vectors_per_gpu=[int(t.item()) for t in all_local], lists=nlists,
+                       l2="flushed (256 MB write) between timed steps", recall_target_met=met,
+                       operating_nprobe=op["nprobe"], quick=bool(args.quick),
+                       allgather_bytes_per_rank=int(nq * CONFIG["k"] * 8)),
+        "sweep": sweep,
+        "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
+                "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
+        "gpu_launches": sum((4 if s_["nprobe"] <= 4 else 6) + 4 for s_ in sweep) * args.steps * 2,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    dist.destroy_process_group()
 
 
 def profile_stage(args, device):
@@ -378,61 +532,297 @@ def roofline(idx, qd, nprobe, args, device, SearchParams, flush):
             "traffic": traffic, "algorithmic_bytes": alg, "ms_per_launch": ms, "nprobe": nprobe}
 
 
-def cpu_baseline(W, nprobe, sample):
+def cpu_baseline_and_parity(W, idx, qd, nprobe, sample, SearchParams):
     """The oracle (C restatement of the reference search, OpenMP over all
-    host cores) on the first `sample` queries at the operating nprobe."""
+    host cores) on the first `sample` queries at the operating nprobe: its
+    time is the CPU baseline, and its results -- in the intended and in the
+    reference (ref_compat) mode -- are compared with the GPU search of the
+    same queries on the same index: ids that differ where the distances
+    differ by more than 1e-5 relative, the largest relative distance error,
+    and recall@10 of both on this one query set."""
     import oracle
-    from fusiongpu_b200.index import SearchParams
-    p = search_params(nprobe, SearchParams)
+    from fusiongpu_b200.index import recall_at
     index = W["index"].to_numpy()
     q = np.ascontiguousarray(W["queries"][:sample])
-    kw = dict(top_m=p.top_m, p1_lists=p.p1_lists, limit_k=p.limit_k, threshold_coeff=p.threshold_coeff,
-              prune_ratio=p.prune_ratio, rerank_m=p.rerank_m, final_k=p.final_k, mini_batch=p.mini_batch,
-              epsilon=p.epsilon, beta=p.beta, ref_compat=False)
+    gt = W["gt"][:sample, :10]
     cores = os.cpu_count() or 1
-    oracle.search(index, W["base"], q[:8], nthreads=cores, **kw)  # warm caches
-    t0 = time.perf_counter()
-    oracle.search(index, W["base"], q, nthreads=cores, **kw)
-    dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"first {sample} of {W['queries'].shape[0]} queries at nprobe={nprobe}, same index",
-            "seconds": dt}
+    parity = {"queries": int(sample), "nprobe": int(nprobe), "tie_rule": "ids may differ where distances are "
+              "within 1e-5 relative", "index": "the GPU arm's index", "modes": {}}
+    cpu = None
+    for mode, rc in (("intended", False), ("ref_compat", True)):
+        p = search_params(nprobe, SearchParams, rc)
+        kw = oracle_kw(p)
+        if cpu is None:
+            oracle.search(index, W["base"], q[:8], nthreads=cores, **kw)  # warm caches
+        t0 = time.perf_counter()
+        oi, od = oracle.search(index, W["base"], q, nthreads=cores, **kw)
+        dt = time.perf_counter() - t0
+        if cpu is None:
+            cpu = {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+                   "sample": f"first {sample} of {W['queries'].shape[0]} queries at nprobe={nprobe}, same index "
+                             "(intended mode)", "seconds": dt}
+        gi, gd = idx.search(qd[:sample].contiguous(), p)
+        gi, gd = gi.cpu().numpy(), gd.cpu().numpy()
+        mism, rel = compare_results(gi, gd, oi, od)
+        parity["modes"][mode] = {"id_mismatches_beyond_1e-5_ties": mism, "max_rel_dist_err": rel,
+                                 "bit_exact": bool(np.array_equal(gi, oi) and np.array_equal(gd, od)),
+                                 "recall_gpu": recall_at(gi[:, :10], gt, 10),
+                                 "recall_oracle": recall_at(oi[:, :10], gt, 10)}
+    return cpu, parity
+
+
+REF_GPU_NPROBE = (1, 2, 4, 8, 16, 32)
+REF_GPU_BATCHES = (128, 10000)
+# the reference's LUT buffer holds bs * top_m * M * 256 floats (gpu_global.cu:108-160)
+REF_GPU_TABLE_LIMIT = 24 << 30
+
+
+def _ref_gg(dim, pq_m):
+    """The reference's gpu_global.cu built for (dim, pq_m) under oracle/_ref,
+    with the timing-context entry points typed, or None."""
+    import ctypes as C
+    import oracle
+    L = oracle.ref_lib("gg", dim, pq_m)
+    if L is None or not hasattr(L, "ref_ctx_create"):
+        return None
+    P, I, F = C.c_void_p, C.c_int, C.c_float
+    L.ref_ctx_create.restype = P
+    L.ref_ctx_create.argtypes = [I, I, I, I, I]
+    L.ref_ctx_destroy.argtypes = [P]
+    L.ref_ctx_stream.restype = P
+    L.ref_ctx_stream.argtypes = [P]
+    L.ref_ctx_search.restype = I
+    L.ref_ctx_search.argtypes = [P, P, P, P, P, P, I, P, I, P, P, P, I, I, F, I, I, F, I, F, I, P, P, P]
+    return L
+
+
+def ref_gpu_block(W, idx, qd, args, device, SearchParams, flush):
+    """The reference's own search kernels (gpu_global.cu:667-874, compiled for
+    sm_100a under oracle/_ref) on this GPU, on the GPU arm's index, with the
+    exact probe lists injected where the reference calls CAGRA
+    (search_pipeline.cu:341): run_gpu_batch_logic + run_gpu_rerank per batch
+    of 128 (the reference's default, search_pipeline.cu:562) and of the whole
+    10,000, on one stream (its function-static scratch is shared by all
+    streams), timed with CUDA events on that stream.  Beside each: this
+    engine's candidate generation + rerank (fg_batch_logic + fg_rerank,
+    ref_compat mode) on the same probes and batch, and how many query rows
+    return other ids than ours.  A point with probes beyond p1_lists runs
+    the reference's phase 2, whose overflow re-emission can write past a
+    query's candidate region: it runs only where the oracle shows every
+    query's candidate count within its region."""
+    import ctypes as C
+    import torch
+    import oracle
+    from fusiongpu_b200.index import recall_at, run_gpu_batch_logic, run_gpu_rerank
+    L = _ref_gg(idx.dim, idx.pq_m)
+    if L is None:
+        return {"unavailable": f"oracle/_ref/libref_gg_{idx.dim}_{idx.pq_m}.so not built (reference sources absent)"}
+    nq = qd.shape[0]
+    gt = W["gt"][:, :10]
+    index_np = None
+    P = lambda t: C.c_void_p(t.data_ptr())
+    steps = max(1, min(args.steps, 5))
+    lens = (idx.offsets[1:] - idx.offsets[:-1]).to(torch.int64)
+    res = {"what": "reference run_gpu_batch_logic + run_gpu_rerank (no coarse stage: exact probes injected) vs "
+                   "fg_batch_logic + fg_rerank (ref_compat) on the same probes",
+           "steps": steps, "stream": "one (the reference's static scratch is shared across streams)", "points": []}
+    for nprobe in REF_GPU_NPROBE:
+        p = search_params(nprobe, SearchParams, True)
+        pid, pd = idx.coarse(qd, nprobe)
+        torch.cuda.synchronize(device)
+        point = {"nprobe": nprobe}
+        if nprobe > p.p1_lists:
+            if index_np is None:
+                index_np = idx.to_numpy()
+            pid_np, pd_np = pid.cpu().numpy().view(np.uint32), pd.cpu().numpy()
+            _, _, _, st = oracle.batch_logic(index_np, W["queries"], pid_np, pd_np, nthreads=os.cpu_count() or 1,
+                                             **oracle_kw(p))
+            budget = np.where(pd_np > pd_np[:, :1] * np.float32(p.prune_ratio), 0,
+                              lens.cpu().numpy()[pid_np.astype(np.int64)]).sum(1)
+            if not (st["count"] <= budget).all():
+                point["skipped"] = "candidate count beyond its region for some query (phase-2 overflow)"
+                res["points"].append(point)
+                continue
+        # ours, same probes, whole batch
+        ours = []
+        for _ in range(args.warmup):
+            ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pd, p)
+            oi, od = run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+        stream = torch.cuda.current_stream(device)
+        for _ in range(steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pd, p)
+            oi, od = run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+            e1.record(stream)
+            e1.synchronize()
+            ours.append(e0.elapsed_time(e1))
+        oi, od = oi.cpu().numpy(), od.cpu().numpy()
+        point["fusiongpu_ms_per_10k"] = sum(ours) / len(ours)
+        point["recall_fusiongpu"] = recall_at(oi[:, :10], gt, 10)
+        for bs in REF_GPU_BATCHES:
+            key = f"batch_{bs}"
+            if bs * nprobe * idx.pq_m * 256 * 4 > REF_GPU_TABLE_LIMIT:
+                point[key] = {"skipped": "the reference's LUT buffer would exceed 24 GB"}
+                continue
+            ctx = L.ref_ctx_create(bs, nprobe, p.rerank_m, p.final_k, p.p1_lists)
+            if not ctx:
+                point[key] = {"skipped": "allocation failed"}
+                continue
+            try:
+                rs = torch.cuda.ExternalStream(L.ref_ctx_stream(ctx), device=device)
+                fi = torch.zeros((nq, p.final_k), dtype=torch.int32, device=device)
+                fd = torch.zeros((nq, p.final_k), dtype=torch.float32, device=device)
+                cnt = torch.zeros(nq, dtype=torch.int32, device=device)
+                pid_u = pid.contiguous()
+
+                def one_pass():
+                    for lo in range(0, nq, bs):
+                        hi = min(nq, lo + bs)
+                        rc = L.ref_ctx_search(ctx, P(idx.codebook), P(idx.offsets), P(idx.codes), P(idx.ids),
+                                              P(idx.centroids), idx.nlist, P(idx.base), idx.base.shape[0],
+                                              C.c_void_p(qd[lo].data_ptr()), C.c_void_p(pid_u[lo].data_ptr()),
+                                              C.c_void_p(pd[lo].data_ptr()), hi - lo, nprobe, p.prune_ratio,
+                                              p.p1_lists, p.limit_k, p.threshold_coeff, p.mini_batch, p.epsilon,
+                                              p.beta, C.c_void_p(fi[lo].data_ptr()), C.c_void_p(fd[lo].data_ptr()),
+                                              C.c_void_p(cnt[lo].data_ptr()))
+                        if rc != 0:
+                            raise RuntimeError(f"reference search failed: cuda error {rc}")
+
+                torch.cuda.synchronize(device)
+                one_pass()  # grows the reference's pools (its own cudaMalloc) outside the timing
+                torch.cuda.synchronize(device)
+                tms = []
+                for _ in range(steps):
+                    flush.zero_()
+                    torch.cuda.synchronize(device)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(rs)
+                    one_pass()
+                    e1.record(rs)
+                    e1.synchronize()
+                    tms.append(e0.elapsed_time(e1))
+                ri, rd = fi.cpu().numpy(), fd.cpu().numpy()
+                mism, rel = compare_results(ri, rd, oi, od)
+                ms = sum(tms) / len(tms)
+                point[key] = {"ms_per_10k": ms, "qps": nq / (ms / 1e3), "recall": recall_at(ri[:, :10], gt, 10),
+                              "rows_with_other_ids": int((ri != oi).any(1).sum()),
+                              "id_mismatches_beyond_1e-5_ties": mism, "max_rel_dist_err": rel,
+                              "candidate_counts_equal": bool(np.array_equal(cnt.cpu().numpy(), cc.cpu().numpy())),
+                              "speedup_fusiongpu": ms / point["fusiongpu_ms_per_10k"]}
+            finally:
+                torch.cuda.synchronize(device)
+                L.ref_ctx_destroy(ctx)
+        res["points"].append(point)
+    return res
+
+
+def recall10(results, gt):
+    """compute_recall (search_pipeline.cu:531-557): hits of the first 10
+    predicted ids (deduplicated) in the ground-truth rows, over nq*10."""
+    hits = 0
+    for r, g in zip(results[:, :10].tolist(), gt[:, :10].tolist()):
+        hits += len(set(r) & set(g))
+    return hits / (results.shape[0] * 10)
+
+
+def exact_gt(base, queries, k, device, chunk=1000):
+    """Exact L2 k-NN in float64 on the GPU (torch matmul), ties by lower id.
+    The C2 vectors are integers in [0, 255], so every distance is an integer
+    below 2^25 and float64 holds it exactly whatever the summation order;
+    the key distance * 2^20 + id (ids < 2^20) is then exact too."""
+    import torch
+    b = torch.from_numpy(np.ascontiguousarray(base)).to(device, torch.float64)
+    bn = (b * b).sum(1)
+    ids = torch.arange(b.shape[0], device=device, dtype=torch.float64)
+    out = []
+    for lo in range(0, queries.shape[0], chunk):
+        q = torch.from_numpy(np.ascontiguousarray(queries[lo:lo + chunk])).to(device, torch.float64)
+        d = bn[None, :] + (q * q).sum(1)[:, None] - 2.0 * (q @ b.T)
+        key = d * float(1 << 20) + ids[None, :]
+        out.append(torch.topk(key, k, dim=1, largest=False).indices.to(torch.int32).cpu())
+        del d, key
+    return torch.cat(out).numpy()
+
+
+def reference_build(base, nlist, pq_m):
+    """The index the reference's own build_global writes for this data:
+    oracle/_ref/ref_build_global_<dim>_<pq_m>_<nlist> (build_global.cu
+    compiled from its sources with these constants) runs in a scratch
+    directory on a .fvecs copy of the base, and its ivf_data.bin and
+    global_pq_codebook.bin are read back (formats.load_index, numpy only).
+    Returns (index dict, seconds) or (None, reason)."""
+    import shutil
+    import subprocess
+    import tempfile
+    from fusiongpu_b200 import formats
+    dim = base.shape[1]
+    exe = os.path.join(ROOT, "oracle", "_ref", f"ref_build_global_{dim}_{pq_m}_{nlist}")
+    if not os.path.exists(exe):
+        return None, f"{os.path.relpath(exe, ROOT)} not built (reference sources absent when built)"
+    tmp = tempfile.mkdtemp(prefix="fg_refbuild_")
+    try:
+        os.makedirs(os.path.join(tmp, "run"))
+        os.makedirs(os.path.join(tmp, "res"))
+        fv = os.path.join(tmp, "base.fvecs")
+        formats.write_vecs(fv, np.ascontiguousarray(base, np.float32))
+        t0 = time.time()
+        r = subprocess.run([exe, fv], cwd=os.path.join(tmp, "run"), capture_output=True, text=True, timeout=1200)
+        dt = time.time() - t0
+        if r.returncode != 0:
+            raise RuntimeError(f"reference build_global failed ({r.returncode}): {r.stderr[-500:]}")
+        return formats.load_index(os.path.join(tmp, "res"), pq_m, dim), dt
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def main_reference(args):
     """CPU arm: the oracle restating the reference's search on the host cores,
-    same workload, metric and sweep; each step is a bounded query sample."""
+    same workload, metric and sweep, each step a bounded query sample.  The
+    index is the one the reference's own build_global writes for the same
+    data (its k-means, rebalancing, PQ training and encoding; the CAGRA graph
+    over centroids is not built, cuVS being absent), the ground truth an
+    exact float64 k-NN in torch; nothing of this repository's library runs.
+    Recall is over all 10,000 queries, like the GPU arm's."""
     import torch
-    from fusiongpu_b200.index import SearchParams, recall_at
     import oracle
+    from fusiongpu_b200 import datasets as ds
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    W = setup(device, args.quick)  # index built once (untimed setup) so both arms search the same index
-    index = W["index"].to_numpy()
-    base, queries, gt = W["base"], W["queries"], W["gt"]
+    spec, nlist = workload(args.quick)
+    t0 = time.time()
+    base, queries = ds.generate(spec)
+    index, build_s = reference_build(base, nlist, CONFIG["pq_m"])
+    if index is None:
+        print(json.dumps({"impl": "reference", "unavailable": build_s}), flush=True)
+        return
+    gt = exact_gt(base, queries, 10, device)
+    setup_s = time.time() - t0
     cores = os.cpu_count() or 1
     sample = 128
+    nq = queries.shape[0]
     pts, sweep = [], []
     for nprobe in SWEEP:
-        p = search_params(nprobe, SearchParams)
-        kw = dict(top_m=p.top_m, p1_lists=p.p1_lists, limit_k=p.limit_k, threshold_coeff=p.threshold_coeff,
-                  prune_ratio=p.prune_ratio, rerank_m=p.rerank_m, final_k=p.final_k, mini_batch=p.mini_batch,
-                  epsilon=p.epsilon, beta=p.beta, ref_compat=False)
-        rq = np.ascontiguousarray(queries[:1000])
-        ids, _ = oracle.search(index, base, rq, nthreads=cores, **kw)
-        rec = recall_at(ids[:, :10], gt[:1000, :10], 10)
+        kw = dict(top_m=nprobe, p1_lists=CONFIG["p1_lists"], limit_k=CONFIG["limit_k"],
+                  threshold_coeff=CONFIG["threshold_coeff"], prune_ratio=100.0, rerank_m=CONFIG["rerank_m"],
+                  final_k=CONFIG["k"], mini_batch=CONFIG["mini_batch"], epsilon=CONFIG["epsilon"],
+                  beta=CONFIG["beta"], ref_compat=False)
+        ids, _ = oracle.search(index, base, queries, nthreads=cores, **kw)
+        rec = recall10(ids, gt)
         for s in range(args.warmup):
             oracle.search(index, base, np.ascontiguousarray(queries[:sample]), nthreads=cores, **kw)
         tot = 0.0
         for s in range(args.steps):
-            qs = np.ascontiguousarray(queries[(s * sample) % 9000:(s * sample) % 9000 + sample])
-            t0 = time.perf_counter()
+            lo = (s * sample) % (nq - sample)
+            qs = np.ascontiguousarray(queries[lo:lo + sample])
+            t1 = time.perf_counter()
             oracle.search(index, base, qs, nthreads=cores, **kw)
-            tot += time.perf_counter() - t0
+            tot += time.perf_counter() - t1
         ms = tot / args.steps * 1e3
         sweep.append(dict(nprobe=nprobe, recall=rec, ms_per_step=ms, qps=sample / (ms / 1e3)))
         pts.append((nprobe, rec, sample / (ms / 1e3)))
@@ -453,12 +843,16 @@ def main_reference(args):
         "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture standing in for a dataset)",
         "config": dict(CONFIG, recall_target_met=met, operating_nprobe=op["nprobe"], quick=bool(args.quick),
-                       parallelism="host CPU (OpenMP)"),
+                       parallelism="host CPU (OpenMP)", lists=int(index["centroids"].shape[0]),
+                       index="written by the reference's build_global (oracle/_ref), CAGRA step not built",
+                       recall_on=f"all {nq} queries (exact float64 ground truth)"),
         "sweep": sweep,
         "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} queries per step (recall from the first 1000); the reference "
-                                   "ships no CPU search, so its C restatement (oracle/) runs"},
+                         "sample": f"{sample} queries per step; the reference ships no CPU search, so its C "
+                                   "restatement (oracle/) runs on the reference-built index"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_build_s": build_s,
+        "setup_s": setup_s,
     }
     print(json.dumps(out), flush=True)
 

@@ -69,6 +69,8 @@ _SIGS = {
     "fg_host_memory_mapped": [_P, C.POINTER(C.c_int32)],
     "fg_map_ids": [_P, _I64, _P, _I64, _P, _P],
     "fg_merge_topk": [_P, _P, _I32, _I32, _I32, _P, _P, _P],
+    "fg_pack_topk": [_P, _P, _I64, _P, _I64, _P, _P],
+    "fg_merge_topk_keys": [_P, _I32, _I32, _I32, _P, _P, _P],
     "fg_kmeans_init": [_P, _I64, _I32, _I32, _U32, _P, _P, _SZ, _P],
     "fg_assign_workspace_size": [_I64, _I32, _I32, _P],
     "fg_assign": [_P, _I64, _I32, _P, _I32, _P, _P, _SZ, _P],

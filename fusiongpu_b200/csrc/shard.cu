@@ -41,6 +41,47 @@ __global__ void __launch_bounds__(MG_WARPS * 32)
     }
 }
 
+// The same selection over packed keys: one all-gather of [nshards][nq][k]
+// 64-bit keys (distance key << 32 | global id) replaces two of the distances
+// and the ids.
+__global__ void __launch_bounds__(MG_WARPS * 32)
+    merge_keys_kernel(const unsigned long long* __restrict__ in, int nshards, int nq, int k, int npow,
+                      int32_t* __restrict__ out_ids, float* __restrict__ out_d) {
+    extern __shared__ __align__(16) unsigned long long keys[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * MG_WARPS + w;
+    if (q >= nq) return;
+    unsigned long long* s = keys + (size_t)w * npow;
+    const int n = nshards * k;
+    for (int i = lane; i < npow; i += 32) {
+        unsigned long long key = ~0ull;
+        if (i < n) {
+            const int sh = i / k, j = i % k;
+            key = in[((size_t)sh * nq + q) * k + j];
+        }
+        s[i] = key;
+    }
+    __syncwarp();
+    warp_bitonic_sort(s, npow);
+    for (int j = lane; j < k; j += 32) {
+        const unsigned long long e = s[j];
+        out_ids[(size_t)q * k + j] = (int32_t)(uint32_t)(e & 0xffffffffu);
+        out_d[(size_t)q * k + j] = key2f((uint32_t)(e >> 32));
+    }
+}
+
+// key[i] = f2key(dists[i]) << 32 | global id, the global id being map[ids[i]]
+// (ids[i] itself without a map; -1, which sorts last, for an id outside it).
+__global__ void pack_topk_kernel(const int32_t* __restrict__ ids, const float* __restrict__ d, long long n,
+                                 const int32_t* __restrict__ map, long long nmap,
+                                 unsigned long long* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int32_t v = ids[i];
+    if (map) v = (v >= 0 && v < nmap) ? map[v] : -1;
+    out[i] = ((unsigned long long)f2key(d[i]) << 32) | (uint32_t)v;
+}
+
 __global__ void map_ids_kernel(const int32_t* __restrict__ in, long long n, const int32_t* __restrict__ map,
                                long long nmap, int32_t* __restrict__ out) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -63,6 +104,29 @@ int merge_topk(const float* dists, const int32_t* ids, int nshards, int nq, int 
     return check_launch("merge_topk_kernel");
 }
 
+int merge_keys(const unsigned long long* in, int nshards, int nq, int k, int32_t* out_ids, float* out_d,
+               cudaStream_t s) {
+    FG_REQUIRE(nshards >= 1 && nq >= 0 && k >= 1, "bad merge shape");
+    if (nq == 0) return FG_OK;
+    FG_REQUIRE(in && out_ids && out_d, "null buffer");
+    const int npow = next_pow2(nshards * k);
+    FG_REQUIRE(npow <= 4096, "nshards * k = %d exceeds 4096", nshards * k);
+    const size_t smem = (size_t)MG_WARPS * npow * 8;
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&merge_keys_kernel), (int)smem));
+    merge_keys_kernel<<<(nq + MG_WARPS - 1) / MG_WARPS, MG_WARPS * 32, smem, s>>>(in, nshards, nq, k, npow, out_ids,
+                                                                                out_d);
+    return check_launch("merge_keys_kernel");
+}
+
+int pack_topk(const int32_t* ids, const float* d, long long n, const int32_t* map, long long nmap,
+              unsigned long long* out, cudaStream_t s) {
+    FG_REQUIRE(n >= 0 && nmap >= 0, "bad sizes");
+    if (n == 0) return FG_OK;
+    FG_REQUIRE(ids && d && out && (map || nmap == 0), "null buffer");
+    pack_topk_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ids, d, n, map, nmap, out);
+    return check_launch("pack_topk_kernel");
+}
+
 int map_ids(const int32_t* in, long long n, const int32_t* map, long long nmap, int32_t* out, cudaStream_t s) {
     FG_REQUIRE(n >= 0 && nmap >= 0, "bad sizes");
     if (n == 0) return FG_OK;
@@ -81,4 +145,16 @@ extern "C" int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nsh
 extern "C" int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, int32_t* out,
                           void* stream) {
     return fg::map_ids(in, n, map, nmap, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fg_pack_topk(const int32_t* ids, const float* dists, int64_t n, const int32_t* map, int64_t nmap,
+                            uint64_t* keys, void* stream) {
+    return fg::pack_topk(ids, dists, n, map, nmap, reinterpret_cast<unsigned long long*>(keys),
+                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fg_merge_topk_keys(const uint64_t* keys, int32_t nshards, int32_t nq, int32_t k, int32_t* out_ids,
+                                  float* out_dists, void* stream) {
+    return fg::merge_keys(reinterpret_cast<const unsigned long long*>(keys), nshards, nq, k, out_ids, out_dists,
+                          static_cast<cudaStream_t>(stream));
 }

@@ -9,8 +9,10 @@ that is sharded by inverted list:
 * queries are broadcast; each GPU runs the whole search on its lists
   (``fg_search``: probes it does not own are empty lists), maps its shard-local
   vector ids to global ids (``fg_map_ids``) and returns its local top-k;
-* one all-gather (NCCL over NVLink) puts the per-GPU top-k side by side and
-  ``fg_merge_topk`` keeps the k best per query by (distance, global id).
+* ``fg_pack_topk`` maps its shard-local vector ids to global ids and packs
+  each (distance, id) into one 64-bit key; ONE all-gather (NCCL over NVLink)
+  puts the per-GPU [nq][k] keys side by side and ``fg_merge_topk_keys`` keeps
+  the k best per query by (distance, global id).
 
 Per-shard semantics: phase 1 / threshold / phase 2 run over each shard's share
 of the probes (a probed list owned elsewhere counts as empty, as a pruned or
@@ -52,6 +54,54 @@ def shard_arrays(index: dict, base: np.ndarray, owner: np.ndarray, rank: int):
     return shard, np.ascontiguousarray(base[l2g]), l2g
 
 
+def exchange(ids, dists, l2g, world, group, device, timings=None):
+    """The exchange step shared by both sharded indexes: pack this GPU's
+    [nq][k] (shard-local id, distance) into global keys, all-gather them in
+    one NCCL call, merge on the device.  `timings` (a dict) receives CUDA
+    events around the all-gather and the merge."""
+    import torch
+    import torch.distributed as dist
+    from . import _lib
+    from .index import _p, _stream
+    nq, k = dists.shape
+    keys = torch.empty((nq * k,), dtype=torch.int64, device=device)
+    nmap = 0 if l2g is None else l2g.numel()
+    _lib.call("fg_pack_topk", _p(ids), _p(dists), ids.numel(), _p(l2g), nmap, _p(keys), _stream())
+    if world == 1:
+        allk = keys
+    else:
+        allk = torch.empty((world * nq * k,), dtype=torch.int64, device=device)
+        ev = _events(timings, "allgather")
+        dist.all_gather_into_tensor(allk, keys, group=group)
+        _events_end(ev)
+    out_i = torch.empty((nq, k), dtype=torch.int32, device=device)
+    out_d = torch.empty((nq, k), dtype=torch.float32, device=device)
+    ev = _events(timings, "merge")
+    _lib.call("fg_merge_topk_keys", _p(allk), world, nq, k, _p(out_i), _p(out_d), _stream())
+    _events_end(ev)
+    return out_i, out_d
+
+
+def _events(timings, name):
+    if timings is None:
+        return None
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    timings.setdefault(name, []).append((e0, e1))
+    return e1
+
+
+def _events_end(e1):
+    if e1 is not None:
+        e1.record()
+
+
+def elapsed_ms(timings) -> dict:
+    """Mean milliseconds per stage of a `timings` dict (after a synchronize)."""
+    return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in timings.items() if v}
+
+
 class ShardedIndex:
     """This process's shard of a list-sharded IVF-PQ index on one GPU."""
 
@@ -76,29 +126,20 @@ class ShardedIndex:
         _lib.call("fg_map_ids", _p(ids), ids.numel(), _p(self.l2g), self.l2g.numel(), _p(gids), _stream())
         return gids, d
 
-    def search(self, queries, params):
-        """Global top-k on every rank: local search, all-gather, device merge."""
+    def search(self, queries, params, timings=None):
+        """Global top-k on every rank: local search, one all-gather of packed
+        keys, device merge.  `timings` (a dict) receives CUDA events per
+        stage ("local", "allgather", "merge")."""
         import torch
-        import torch.distributed as dist
-        from . import _lib
-        from .index import _p, _stream
         if self.n_local == 0:
             nq = queries.shape[0]
             d = torch.full((nq, params.final_k), float(np.finfo(np.float32).max), device=self.device)
-            gids = torch.full((nq, params.final_k), -1, dtype=torch.int32, device=self.device)
+            ids = torch.full((nq, params.final_k), -1, dtype=torch.int32, device=self.device)
         else:
-            gids, d = self.local_search(queries, params)
-        if self.world == 1:
-            return gids, d
-        nq, k = d.shape
-        all_d = torch.empty((self.world * nq * k,), dtype=torch.float32, device=self.device)
-        all_i = torch.empty((self.world * nq * k,), dtype=torch.int32, device=self.device)
-        dist.all_gather_into_tensor(all_d, d.reshape(-1), group=self.group)
-        dist.all_gather_into_tensor(all_i, gids.reshape(-1), group=self.group)
-        out_i = torch.empty((nq, k), dtype=torch.int32, device=self.device)
-        out_d = torch.empty((nq, k), dtype=torch.float32, device=self.device)
-        _lib.call("fg_merge_topk", _p(all_d), _p(all_i), self.world, nq, k, _p(out_i), _p(out_d), _stream())
-        return out_i, out_d
+            ev = _events(timings, "local")
+            ids, d = self.local.search(queries, params)
+            _events_end(ev)
+        return exchange(ids, d, self.l2g, self.world, self.group, self.device, timings)
 
 
 def graph_shard_rows(n: int, nshards: int, rank: int) -> tuple[int, int]:
@@ -141,20 +182,8 @@ class ShardedGraphIndex:
         _lib.call("fg_map_ids", _p(ids), ids.numel(), _p(self.l2g), self.l2g.numel(), _p(gids), _stream())
         return gids, d
 
-    def search(self, queries, params):
-        import torch
-        import torch.distributed as dist
-        from . import _lib
-        from .index import _p, _stream
-        gids, d = self.local_search(queries, params)
-        if self.world == 1:
-            return gids, d
-        nq, k = d.shape
-        all_d = torch.empty((self.world * nq * k,), dtype=torch.float32, device=self.device)
-        all_i = torch.empty((self.world * nq * k,), dtype=torch.int32, device=self.device)
-        dist.all_gather_into_tensor(all_d, d.reshape(-1), group=self.group)
-        dist.all_gather_into_tensor(all_i, gids.reshape(-1), group=self.group)
-        out_i = torch.empty((nq, k), dtype=torch.int32, device=self.device)
-        out_d = torch.empty((nq, k), dtype=torch.float32, device=self.device)
-        _lib.call("fg_merge_topk", _p(all_d), _p(all_i), self.world, nq, k, _p(out_i), _p(out_d), _stream())
-        return out_i, out_d
+    def search(self, queries, params, timings=None):
+        ev = _events(timings, "local")
+        ids, d = self.local.search(queries, params)
+        _events_end(ev)
+        return exchange(ids, d, self.l2g, self.world, self.group, self.device, timings)

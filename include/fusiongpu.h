@@ -203,6 +203,17 @@ int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, i
 int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nshards, int32_t nq, int32_t k,
                   int32_t* out_ids, float* out_dists, void* stream);
 
+/* The exchange as ONE all-gather: fg_pack_topk writes keys[i] =
+ * orderable(dists[i]) << 32 | global id (global id = map[ids[i]], or ids[i]
+ * when map is null; -1 for an id outside the map), so that each GPU's [nq][k]
+ * result is a single uint64 tensor; after the all-gather of those keys
+ * ([nshards][nq][k]) fg_merge_topk_keys keeps the k smallest keys per query,
+ * i.e. by (distance, global id), and unpacks them.  nshards * k <= 4096. */
+int fg_pack_topk(const int32_t* ids, const float* dists, int64_t n, const int32_t* map, int64_t nmap,
+                 uint64_t* keys, void* stream);
+int fg_merge_topk_keys(const uint64_t* keys, int32_t nshards, int32_t nq, int32_t k, int32_t* out_ids,
+                       float* out_dists, void* stream);
+
 /* ---- search-parameter tuner: replaces tune_search_parameters
  * (tune_parameters.cu:459-1013).  For nq sample queries with their exact k
  * nearest base vectors gt_ids [nq][k] (ascending distance; fg_knn_exact),

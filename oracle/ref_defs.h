@@ -28,7 +28,10 @@
 #define PQ_M REF_PQ_M
 #define PQ_K 256
 #define PQ_SUB_DIM (DIM / PQ_M)
-#define K_CLUSTERS 2048
+#ifndef REF_K_CLUSTERS
+#define REF_K_CLUSTERS 2048
+#endif
+#define K_CLUSTERS REF_K_CLUSTERS
 #define DEFAULT_BATCH_SIZE 128
 #define DEFAULT_TOP_M 20
 #define DEFAULT_RERANK_M 10000

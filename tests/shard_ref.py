@@ -21,6 +21,26 @@ def merge_topk_host(dists: np.ndarray, ids: np.ndarray, k: int) -> tuple[np.ndar
     return out_i, out_d
 
 
+def pack_keys_host(ids: np.ndarray, dists: np.ndarray) -> np.ndarray:
+    """Host statement of fg_pack_topk (without a map): orderable distance bits
+    in the high word (sign set: all bits flipped; else the sign bit set), the
+    id as unsigned in the low word."""
+    u = np.ascontiguousarray(dists, np.float32).view(np.uint32).astype(np.uint64)
+    hi = np.where(u & 0x80000000, ~u & 0xFFFFFFFF, u | 0x80000000)
+    return ((hi << np.uint64(32)) | ids.astype(np.uint32).astype(np.uint64)).view(np.int64)
+
+
+def merge_keys_host(keys: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Host statement of fg_merge_topk_keys: [nshards][nq][k] keys -> the k
+    smallest per query, unpacked."""
+    ns, nq, kk = keys.shape
+    u = np.transpose(keys.view(np.uint64), (1, 0, 2)).reshape(nq, ns * kk)
+    top = np.sort(u, axis=1)[:, :k]
+    hi = (top >> np.uint64(32)).astype(np.uint32)
+    bits = np.where(hi & 0x80000000, hi & 0x7FFFFFFF, ~hi).astype(np.uint32)
+    return (top & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.int32), bits.view(np.float32)
+
+
 def oracle_sharded_search(index: dict, base: np.ndarray, queries: np.ndarray, world: int, **params):
     """The sharded semantics restated with the CPU oracle: per-shard search,
     global ids, host merge."""

@@ -46,6 +46,23 @@ def test_shards_cover_every_vector_once():
     assert np.array_equal(np.sort(allv), np.arange(base.shape[0]))
 
 
+def test_packed_key_merge_equals_pair_merge():
+    """Packing (distance, id) into one 64-bit word and merging the words
+    selects what the pair merge selects, with negative distances (inner
+    product), ties and -1 padding."""
+    rng = np.random.default_rng(9)
+    ns, nq, k = 4, 60, 12
+    d = np.sort(rng.integers(-8, 8, size=(ns, nq, k)).astype(np.float32) * 0.5, axis=2)
+    i = rng.permutation(ns * nq * k).reshape(ns, nq, k).astype(np.int32)
+    d[:, :, -2:] = np.finfo(np.float32).max
+    i[:, :, -2:] = -1
+    keys = np.stack([shard_ref.pack_keys_host(i[s], d[s]) for s in range(ns)])
+    ki, kd = shard_ref.merge_keys_host(keys, k)
+    ei, ed = shard_ref.merge_topk_host(d, i, k)
+    np.testing.assert_array_equal(ki, ei)
+    np.testing.assert_array_equal(kd, ed)
+
+
 def test_merge_host_orders_by_distance_then_id():
     d = np.array([[[1.0, 2.0, 3.0]], [[1.0, 1.5, np.finfo(np.float32).max]]], np.float32)
     i = np.array([[[7, 3, 4]], [[2, 9, -1]]], np.int32)
@@ -66,13 +83,11 @@ def _worker(rank, world, port, out_dir):
     shard, sbase, l2g = sharded.shard_arrays(index, base, owner, rank)
     li, ld = oracle.search(shard, sbase, q, **P)
     gi = np.where(li >= 0, l2g[np.clip(li, 0, l2g.size - 1)], -1).astype(np.int32)
-    td, ti = torch.from_numpy(ld), torch.from_numpy(gi)
-    all_d = [torch.empty_like(td) for _ in range(world)]
-    all_i = [torch.empty_like(ti) for _ in range(world)]
-    dist.all_gather(all_d, td)
-    dist.all_gather(all_i, ti)
-    mi, md = shard_ref.merge_topk_host(np.stack([x.numpy() for x in all_d]), np.stack([x.numpy() for x in all_i]),
-                                     P["final_k"])
+    # the exchange is one all-gather of packed (distance key, global id) words
+    tk = torch.from_numpy(shard_ref.pack_keys_host(gi, ld))
+    all_k = torch.empty((world * tk.numel(),), dtype=torch.int64)
+    dist.all_gather_into_tensor(all_k, tk.reshape(-1))
+    mi, md = shard_ref.merge_keys_host(all_k.numpy().reshape((world,) + tuple(tk.shape)), P["final_k"])
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), ids=mi, dists=md)
     dist.barrier()
     dist.destroy_process_group()
@@ -138,13 +153,10 @@ def _graph_worker(rank, world, port, out_dir):
     g, ec, en = oracle.graph_build(part.astype(np.float32), entries=True, **b)
     li, ld, _ = oracle.graph_search(part, g, q, entry_centroids=ec, entry_nodes=en, **GS)
     gi = np.where(li >= 0, li + lo, -1).astype(np.int32)
-    td, ti = torch.from_numpy(ld), torch.from_numpy(gi)
-    all_d = [torch.empty_like(td) for _ in range(world)]
-    all_i = [torch.empty_like(ti) for _ in range(world)]
-    dist.all_gather(all_d, td)
-    dist.all_gather(all_i, ti)
-    mi, md = shard_ref.merge_topk_host(np.stack([a.numpy() for a in all_d]), np.stack([a.numpy() for a in all_i]),
-                                     GS["k"])
+    tk = torch.from_numpy(shard_ref.pack_keys_host(gi, ld))
+    all_k = torch.empty((world * tk.numel(),), dtype=torch.int64)
+    dist.all_gather_into_tensor(all_k, tk.reshape(-1))
+    mi, md = shard_ref.merge_keys_host(all_k.numpy().reshape((world,) + tuple(tk.shape)), GS["k"])
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), ids=mi, dists=md)
     dist.barrier()
     dist.destroy_process_group()
