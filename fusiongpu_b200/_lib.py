@@ -60,6 +60,9 @@ _SIGS = {
     "fg_coarse_search_tc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P, _P],
     "fg_coarse_search_noalloc": [_P, _I32, _I32, _P, _I32, _I32, _P, _P, _P],
     "fg_batch_logic": [C.POINTER(IvfpqView), _P, _I32, _P, _P, C.POINTER(SearchParams), _P, _P, _P, _P, _P],
+    "fg_batch_logic_workspace_size": [C.POINTER(IvfpqView), C.POINTER(SearchParams), _I32, C.POINTER(_SZ)],
+    "fg_batch_logic_ws": [C.POINTER(IvfpqView), _P, _I32, _P, _P, C.POINTER(SearchParams), _P, _P, _P, _P, _P, _SZ,
+                          _P],
     "fg_probe_budget": [_P, _I32, _P, _P, _I32, _I32, _F, _P, _P, _P],
     "fg_rerank": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
     "fg_rerank_u8": [_P, _I32, _I32, _P, _P, _P, _I64, C.POINTER(SearchParams), _P, _P, _P],
@@ -69,7 +72,7 @@ _SIGS = {
     "fg_host_memory_mapped": [_P, C.POINTER(C.c_int32)],
     "fg_map_ids": [_P, _I64, _P, _I64, _P, _P],
     "fg_merge_topk": [_P, _P, _I32, _I32, _I32, _P, _P, _P],
-    "fg_pack_topk": [_P, _P, _I64, _P, _I64, _P, _P],
+    "fg_pack_topk": [_P, _P, _I32, _I32, _P, _I64, _P, _P],
     "fg_merge_topk_keys": [_P, _I32, _I32, _I32, _P, _P, _P],
     "fg_kmeans_init": [_P, _I64, _I32, _I32, _U32, _P, _P, _SZ, _P],
     "fg_assign_workspace_size": [_I64, _I32, _I32, _P],

@@ -69,7 +69,9 @@ cudaError_t ensure_smem(const void* func, int bytes) {
 
 // implemented in the kernel files
 int batch_logic(const fg_ivfpq_view*, const float*, int, const uint32_t*, const float*, const fg_search_params*,
-                int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad, int* work_counter = nullptr);
+                int32_t*, float*, int32_t*, int32_t*, cudaStream_t, bool write_pad, int* work_counter = nullptr,
+                void* ws = nullptr, size_t ws_bytes = 0);
+size_t batch_logic_workspace(const fg_ivfpq_view* ix, const fg_search_params* p, int nq);
 int rerank(const float*, int, int, const int32_t*, const int32_t*, const void*, int, long long,
            const fg_search_params*, int32_t*, float*, cudaStream_t);
 int knn_like(const float* Y, long long ny, int dim, const float* Q, long long nq, int k, int32_t* out_i,
@@ -226,6 +228,23 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                        candidate_counts, as_stream(stream), true);
 }
 
+int fg_batch_logic_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params, int32_t nq,
+                                  size_t* bytes) {
+    FG_REQUIRE(index && params && bytes && nq >= 0, "bad arguments");
+    *bytes = batch_logic_workspace(index, params, nq);
+    return FG_OK;
+}
+
+int fg_batch_logic_ws(const fg_ivfpq_view* index, const float* queries, int32_t nq, const uint32_t* probe_ids,
+                      const float* probe_dists, const fg_search_params* params, int32_t* top_ids, float* top_dists,
+                      int32_t* top_counts, int32_t* candidate_counts, void* ws, size_t ws_bytes, void* stream) {
+    FG_REQUIRE(index && params, "null index or params");
+    int rc = need_ws(ws, ws_bytes, batch_logic_workspace(index, params, nq));
+    if (rc) return rc;
+    return batch_logic(index, queries, nq, probe_ids, probe_dists, params, top_ids, top_dists, top_counts,
+                       candidate_counts, as_stream(stream), true, nullptr, ws, ws_bytes);
+}
+
 int fg_probe_budget(const int32_t* list_offsets, int32_t nlist, const uint32_t* probe_ids, const float* probe_dists,
                     int32_t nq, int32_t top_m, float prune_ratio, int32_t* counts, int32_t* offsets, void* stream) {
     return probe_budget(list_offsets, nlist, probe_ids, probe_dists, nq, top_m, prune_ratio, counts, offsets,
@@ -252,7 +271,8 @@ int fg_search_workspace_size(const fg_ivfpq_view* index, const fg_search_params*
     FG_REQUIRE(nq >= 0 && params->top_m >= 1 && params->top_m <= index->nlist && params->rerank_m >= 1,
                "bad search shape");
     *bytes = search_fixed_bytes(std::max(nq, 1), params) +
-             coarse_workspace(std::max(nq, 1), index->nlist, index->dim, params->top_m) + 1024;
+             std::max(coarse_workspace(std::max(nq, 1), index->nlist, index->dim, params->top_m),
+                      batch_logic_workspace(index, params, std::max(nq, 1))) + 1024;
     return FG_OK;
 }
 
@@ -280,9 +300,11 @@ static int search_any(const fg_ivfpq_view* index, const void* base, int base_u8,
     rc = coarse(index->centroids, index->nlist, index->dim, queries, nq, params->top_m, pids, pd,
                 static_cast<char*>(ws) + used, ws_bytes - used, s);
     if (rc) return rc;
-    // the rerank reads only the first top_counts[q] entries: skip the padding
+    // the rerank reads only the first top_counts[q] entries: skip the padding.
+    // The coarse scratch is dead once the probes exist: the split scan reuses it.
     FG_CUDA_TRY(cudaMemsetAsync(qctr, 0, sizeof(int), s));
-    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false, qctr);
+    rc = batch_logic(index, queries, nq, pids, pd, params, tid, td, tc, nullptr, s, false, qctr,
+                     static_cast<char*>(ws) + used, ws_bytes - used);
     if (rc) return rc;
     return rerank(queries, nq, index->dim, tid, tc, base, base_u8, nbase, params, out_ids, out_dists, s);
 }

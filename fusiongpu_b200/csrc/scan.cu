@@ -21,6 +21,7 @@
 // The ADC arithmetic is bit-identical to the reference: each LUT entry is the
 // same fmaf expression as gpu_global.cu:115-157 / 274-313, and the ADC sum runs
 // over subspaces in order with round-to-nearest adds.
+#include <algorithm>
 #include <cstdlib>
 #include <string>
 
@@ -53,6 +54,14 @@ struct ScanArgs {
     float* top_dists;
     int32_t* top_counts;
     int32_t* cand_counts;
+    // split path (one CTA per probed list): per-query phase-1 cutoffs [nq][p1],
+    // candidate counts [nq], candidate keys [nq][capg] and fallback flags [nq]
+    float* cut_g;
+    int32_t* cnt_g;
+    unsigned long long* cand_g;
+    int32_t* flags;       // split select: 1 where the query falls back to the per-query kernel
+    const int32_t* only;  // per-query kernel: run only the queries flagged here (null: all)
+    int capg;
 };
 
 struct ScanMisc {
@@ -313,6 +322,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
 
     const int tid = threadIdx.x;
     const int q = blockIdx.x;
+    if (a.only && !a.only[q]) return;
     const int P = a.top_m;
     const float* qv = a.queries + (size_t)q * a.dim;
 
@@ -1338,6 +1348,381 @@ __global__ void __launch_bounds__(TEAM_THREADS, 1)
 
 using TeamKernel = void (*)(const ScanArgs, int, int, int);
 
+// ---- split path: one CTA per (query, probed list) -----------------------------
+//
+// For long lists (hundreds of vectors per list, tens of probes per query) the
+// per-query kernel serialises a query's probes inside one CTA, with block
+// barriers around every LUT, selection and emission round.  The split path
+// gives every (query, probed list) pair its own CTA of SPLIT_NT threads:
+//
+//   split_p1_kernel   phase 1 (the first p1 probes): LUT, ADC of the list,
+//                     the limit_k smallest by (distance, position), the cutoff
+//                     (gpu_global.cu:79-166, 212-253, 321-390);
+//   split_p2_kernel   phase 2 (the other probes): threshold from the query's
+//                     phase-1 cutoffs (gpu_global.cu:394-426), LUT, ADC, the
+//                     passing vectors with the reference's 128-slot buffer and
+//                     overflow re-emission in ref_compat mode (:428-527);
+//   split_select_kernel  per query: the rerank_m smallest candidates, sorted,
+//                     with their vector ids (gpu_global.cu:533-576, 838-871).
+//
+// Candidates go to a per-query region of capg 64-bit keys in global memory as
+// (distance key << 32 | order), order = probe index << 20 | position (plus
+// 1 << 19 for an overflow re-emission).  Sorting by that key is sorting by
+// distance with ties in emission order -- the order the per-query kernel
+// appends in -- so the slots themselves can be taken in any order.  A query
+// whose candidates overflow its region, or whose ties at the selection
+// boundary overflow the sort buffer, is flagged and recomputed by the
+// per-query kernel.  Every float is the same expression as in the per-query
+// kernel, so both paths return identical results.
+
+constexpr int SPLIT_NT = 128;
+constexpr int SEL_NT = 512;
+
+__host__ __device__ inline int split_keys_bytes(int lmax) { return ((lmax > 0 ? lmax : 1) * 4 + 15) / 16 * 16; }
+
+struct SplitMisc {
+    uint32_t hist[256];
+    int warp[SPLIT_NT / 32];
+    uint32_t b[2];
+    int base, n_pass;
+    float thr;
+};
+
+// The probed list of pair (q, j) after the prune, as start/len (len 0: skipped).
+__device__ __forceinline__ void split_probe(const ScanArgs& a, int q, int j, uint32_t& c, int& start, int& len) {
+    const int P = a.top_m;
+    const float best = a.probe_dists[(size_t)q * P];
+    const float d = a.probe_dists[(size_t)q * P + j];
+    c = a.probe_ids[(size_t)q * P + j];
+    start = 0;
+    len = 0;
+    if (d > best * a.prune_ratio || c >= (uint32_t)a.nlist) {
+        c = FG_INVALID_PROBE;
+        return;
+    }
+    start = a.offsets[c];
+    len = a.offsets[c + 1] - start;
+}
+
+// LUT of (query, list c) in shared memory: the entries of build_lut.
+template <int M, int SD>
+__device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, uint32_t c, float* res, float* lut) {
+    const float* cv = a.centroids + (size_t)c * a.dim;
+    for (int t = threadIdx.x; t < a.dim; t += SPLIT_NT) res[t] = qv[t] - cv[t];
+    __syncthreads();
+#pragma unroll 4
+    for (int e = threadIdx.x; e < M * 256; e += SPLIT_NT) {
+        const int m = e >> 8;
+        lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
+    }
+    __syncthreads();
+}
+
+// Keys of rows [0, n) of the list: thread t takes rows t, t + SPLIT_NT, ...
+template <int M>
+__device__ __forceinline__ void split_keys(const ScanArgs& a, int start, int n, const float* lut, uint32_t* keys) {
+    for (int i = threadIdx.x; i < n; i += SPLIT_NT) keys[i] = f2key(adc<M>(a.codes + (size_t)(start + i) * M, lut));
+    __syncthreads();
+}
+
+template <int M, int SD>
+__global__ void __launch_bounds__(SPLIT_NT) split_p1_kernel(const ScanArgs a, int nq) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* lut = reinterpret_cast<float*>(smem);
+    float* res = lut + M * 256;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(res + (a.dim + 3) / 4 * 4);
+    SplitMisc* ms = reinterpret_cast<SplitMisc*>(reinterpret_cast<unsigned char*>(keys) + split_keys_bytes(a.lmax));
+    const int pair = blockIdx.x;
+    const int q = pair / a.p1, j = pair - (pair / a.p1) * a.p1;
+    if (q >= nq) return;
+    uint32_t c;
+    int start, len;
+    split_probe(a, q, j, c, start, len);
+    if (len <= 0) {
+        if (threadIdx.x == 0) a.cut_g[(size_t)q * a.p1 + j] = 0.0f;
+        return;
+    }
+    const int wc = len < a.limit_k ? len : a.limit_k;
+    const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
+    split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
+    split_keys<M>(a, start, scan, lut, keys);
+    uint32_t kth;
+    int n_less;
+    block_radix_select<SPLIT_NT>(keys, scan, wc, ms->hist, ms->b, kth, n_less);
+    if (threadIdx.x == 0) {
+        a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
+        ms->base = atomicAdd(a.cnt_g + q, wc);
+    }
+    // the wc selected rows in position order: keys below kth, then the first
+    // need_eq equal to it (the stable order of gpu_global.cu:321-390)
+    const int need_eq = wc - n_less;
+    int eq_base = 0, out = 0;
+    unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
+    for (int r0 = 0; r0 < scan; r0 += SPLIT_NT) {
+        const int i = r0 + threadIdx.x;
+        const bool in = i < scan;
+        const uint32_t key = in ? keys[i] : 0xffffffffu;
+        const int is_eq = (in && key == kth) ? 1 : 0;
+        int eq_tot, s_tot;
+        const int eq_pre = block_exclusive_scan<SPLIT_NT>(is_eq, ms->warp, eq_tot);
+        const bool sel = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
+        const int s_pre = block_exclusive_scan<SPLIT_NT>(sel ? 1 : 0, ms->warp, s_tot);
+        if (sel) {
+            const int slot = ms->base + out + s_pre;
+            if (slot < a.capg) dst[slot] = ((unsigned long long)key << 32) | ((uint32_t)j << 20) | (uint32_t)i;
+        }
+        eq_base += eq_tot;
+        out += s_tot;
+    }
+}
+
+template <int M, int SD>
+__global__ void __launch_bounds__(SPLIT_NT) split_p2_kernel(const ScanArgs a, int nq) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* lut = reinterpret_cast<float*>(smem);
+    float* res = lut + M * 256;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(res + (a.dim + 3) / 4 * 4);
+    SplitMisc* ms = reinterpret_cast<SplitMisc*>(reinterpret_cast<unsigned char*>(keys) + split_keys_bytes(a.lmax));
+    const int np2 = a.top_m - a.p1;
+    const int pair = blockIdx.x;
+    const int q = pair / np2, j = a.p1 + (pair - (pair / np2) * np2);
+    if (q >= nq) return;
+    uint32_t c;
+    int start, len;
+    split_probe(a, q, j, c, start, len);
+    if (len <= 0) return;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        // threshold = min positive phase-1 cutoff * coeff (gpu_global.cu:394-426)
+        float mn = FLT_MAX;
+        for (int u = 0; u < a.p1; ++u) {
+            const float cu = a.cut_g[(size_t)q * a.p1 + u];
+            if (cu > 0.0f && cu < mn) mn = cu;
+        }
+        ms->thr = (mn < FLT_MAX) ? mn * a.coeff : FLT_MAX;
+    }
+    split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
+    split_keys<M>(a, start, len, lut, keys);
+    const float thr = ms->thr;
+    unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
+    const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
+    auto passes = [&](int i) { return key2f(keys[i]) <= thr; };
+    if (!a.ref_compat) {
+        int n_t = 0;
+        for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
+        int tot;
+        const int pre = block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, tot);
+        if (tot == 0) return;
+        if (tid == 0) ms->base = atomicAdd(a.cnt_g + q, tot);
+        __syncthreads();
+        int slot = ms->base + pre;
+        for (int i = tid; i < len; i += SPLIT_NT)
+            if (passes(i)) {
+                if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (uint32_t)i;
+                ++slot;
+            }
+        return;
+    }
+    // ref_compat: the reference's 128 threads (thread t: rows t, t + 128, ...)
+    // keep the first 128 passing vectors in list order in a shared buffer, and
+    // past 128 each thread re-emits its own first (count - 128) passing ones
+    // (gpu_global.cu:466-526).  SPLIT_NT == 128, so thread t is the
+    // reference's thread t.
+    static_assert(SPLIT_NT == REF_BLOCK, "the overflow rule follows the reference's thread-to-row map");
+    int n_t = 0;
+    for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
+    int s_count;
+    (void)block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, s_count);
+    if (s_count == 0) return;
+    const int quota = s_count > REF_BLOCK ? s_count - REF_BLOCK : 0;
+    const int re_t = n_t < quota ? n_t : quota;
+    // regular emissions of this thread: rows whose list-order rank is < 128
+    int reg_t = 0;
+    {
+        int carry = 0;
+        for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
+            const int i = r0 + tid;
+            const int pf = (i < len && passes(i)) ? 1 : 0;
+            int tot;
+            const int pre = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot);
+            if (pf && carry + pre < REF_BLOCK) ++reg_t;
+            carry += tot;
+        }
+    }
+    int tot;
+    const int pre = block_exclusive_scan<SPLIT_NT>(reg_t + re_t, ms->warp, tot);
+    if (tid == 0) ms->base = atomicAdd(a.cnt_g + q, tot);
+    __syncthreads();
+    int slot = ms->base + pre;
+    {
+        int carry = 0;
+        for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
+            const int i = r0 + tid;
+            const int pf = (i < len && passes(i)) ? 1 : 0;
+            int tot2;
+            const int pre2 = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot2);
+            if (pf && carry + pre2 < REF_BLOCK) {
+                if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (uint32_t)i;
+                ++slot;
+            }
+            carry += tot2;
+        }
+    }
+    int left = re_t;
+    for (int i = tid; i < len && left > 0; i += SPLIT_NT)
+        if (passes(i)) {
+            if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (1u << 19) | (uint32_t)i;
+            ++slot;
+            --left;
+        }
+}
+
+// k-th smallest high word (1-based) of n 64-bit keys in global memory; the
+// block_radix_select scheme (four 8-bit MSD passes).
+__device__ void sel_radix_select_hi(const unsigned long long* keys, int n, int k, uint32_t* s_hist, uint32_t* s_b,
+                                    uint32_t& kth, int& n_less) {
+    uint32_t prefix = 0, mask = 0, kk = (uint32_t)k, less = 0;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += SEL_NT) s_hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += SEL_NT) {
+            const uint32_t key = (uint32_t)(keys[i] >> 32);
+            if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            uint32_t c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = s_hist[lane * 8 + j];
+                s += c[j];
+            }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - s;
+            if (excl < kk && kk <= incl) {
+                uint32_t run = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run + c[j] >= kk) {
+                        s_b[0] = (uint32_t)(lane * 8 + j);
+                        s_b[1] = run;
+                        break;
+                    }
+                    run += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        const uint32_t b = s_b[0], below = s_b[1];
+        prefix |= b << shift;
+        mask |= 255u << shift;
+        kk -= below;
+        less += below;
+        __syncthreads();
+    }
+    kth = prefix;
+    n_less = (int)less;
+}
+
+struct SelMisc {
+    uint32_t hist[256];
+    uint32_t b[2];
+    int n_col;
+};
+
+__global__ void __launch_bounds__(SEL_NT) split_select_kernel(const ScanArgs a, int nq, int sort_cap) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    unsigned long long* sortb = reinterpret_cast<unsigned long long*>(smem);
+    SelMisc* ms = reinterpret_cast<SelMisc*>(smem + (size_t)sort_cap * 8);
+    const int q = blockIdx.x;
+    if (q >= nq) return;
+    const int tid = threadIdx.x;
+    const int count = a.cnt_g[q];
+    const int rm = a.rerank_m;
+    const int ak = count < rm ? count : rm;
+    const int nsel = a.ref_compat ? (ak < REF_BLOCK ? ak : REF_BLOCK) : ak;
+    const unsigned long long* cand = a.cand_g + (size_t)q * a.capg;
+    bool ok = count <= a.capg;
+    int n_sort = 0;
+    if (ok && nsel > 0) {
+        if (count <= sort_cap) {
+            for (int i = tid; i < count; i += SEL_NT) sortb[i] = cand[i];
+            n_sort = count;
+        } else {
+            uint32_t kth;
+            int n_less;
+            sel_radix_select_hi(cand, count, nsel, ms->hist, ms->b, kth, n_less);
+            if (tid == 0) ms->n_col = 0;
+            __syncthreads();
+            for (int i = tid; i < count; i += SEL_NT) {
+                const unsigned long long e = cand[i];
+                if ((uint32_t)(e >> 32) <= kth) {
+                    const int s = atomicAdd(&ms->n_col, 1);
+                    if (s < sort_cap) sortb[s] = e;
+                }
+            }
+            __syncthreads();
+            n_sort = ms->n_col;
+            ok = n_sort <= sort_cap;  // more ties at the boundary than the buffer holds
+        }
+    }
+    if (tid == 0) a.flags[q] = ok ? 0 : 1;
+    if (!ok) return;  // the per-query kernel writes this query
+    const int npow = next_pow2(n_sort > 0 ? n_sort : 1);
+    for (int i = n_sort + tid; i < npow; i += SEL_NT) sortb[i] = ~0ull;
+    __syncthreads();
+    if (n_sort > 1) block_bitonic_sort<SEL_NT>(sortb, npow);
+    const int pend = a.write_pad ? rm : ak;
+    const int P = a.top_m;
+    for (int p = tid; p < pend; p += SEL_NT) {
+        const size_t o = (size_t)q * rm + p;
+        if (a.ref_compat && p >= REF_BLOCK) {
+            a.top_ids[o] = 0;  // never written by the reference's 128-thread gather (zeroed memory)
+            a.top_dists[o] = 0.0f;
+        } else if (p < ak) {
+            const unsigned long long e = sortb[p];
+            const uint32_t ord = (uint32_t)(e & 0xffffffffu);
+            const uint32_t c = a.probe_ids[(size_t)q * P + (ord >> 20)];
+            a.top_ids[o] = __ldg(a.vids + a.offsets[c] + (ord & 0x7ffffu));
+            a.top_dists[o] = key2f((uint32_t)(e >> 32));
+        } else {
+            a.top_ids[o] = -1;
+            a.top_dists[o] = FLT_MAX;
+        }
+    }
+    if (tid == 0) {
+        a.top_counts[q] = ak;
+        if (a.cand_counts) a.cand_counts[q] = count;
+    }
+}
+
+using SplitKernel = void (*)(const ScanArgs, int);
+
+template <bool P2>
+static SplitKernel pick_split_kernel(int M, int SD) {
+#define FG_SPLIT_CASE(m, sd) \
+    if (M == m && SD == sd) return P2 ? split_p2_kernel<m, sd> : split_p1_kernel<m, sd>;
+    FG_SPLIT_CASE(4, 4)  // small test indexes
+    FG_SPLIT_CASE(16, 4)
+    FG_SPLIT_CASE(16, 8)
+    FG_SPLIT_CASE(32, 2)
+    FG_SPLIT_CASE(32, 3)
+    FG_SPLIT_CASE(32, 4)
+    FG_SPLIT_CASE(48, 2)
+    FG_SPLIT_CASE(64, 2)
+    FG_SPLIT_CASE(96, 8)
+    FG_SPLIT_CASE(128, 1)
+#undef FG_SPLIT_CASE
+    return nullptr;
+}
+
 template <bool LUT, int NT>
 static TeamKernel pick_team_kernel(int M, int SD) {
 #define FG_TEAM_CASE(m, sd) \
@@ -1375,10 +1760,127 @@ static ScanKernel pick_scan_kernel(int M, int SD) {
     return nullptr;
 }
 
+// ---- the split path's choice and workspace ---------------------------------------
+
+static int split_rsel(const fg_search_params* p) {
+    return p->ref_compat ? (p->rerank_m < REF_BLOCK ? p->rerank_m : REF_BLOCK) : p->rerank_m;
+}
+
+static int split_capg(const fg_search_params* p) {
+    const int r = split_rsel(p);
+    return (std::max(4096, 2 * r) + 31) / 32 * 32;
+}
+
+// Whether the split path runs for this index, parameters and batch: long
+// lists (mean length above the team kernel's limit) and a supported shape,
+// unless FG_SCAN_KERNEL names another kernel (FG_SCAN_KERNEL=split forces it).
+static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
+    if (!ix || !p || nq <= 0 || ix->pq_m <= 0 || ix->dim % ix->pq_m) return false;
+    const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
+    if (!pick_split_kernel<false>(M, SD) || p->top_m > 4096 || ix->max_list_len >= (1 << 19)) return false;
+    const char* force = getenv("FG_SCAN_KERNEL");
+    const std::string mode = force ? force : "";
+    if (mode == "split") return true;
+    if (!mode.empty()) return false;
+    return (double)ix->total / std::max(ix->nlist, 1) > TEAM_OTF_MAX_LEN;
+}
+
+struct SplitWs {
+    float* cut;
+    int32_t* cnt;
+    int32_t* flags;
+    unsigned long long* cand;
+};
+
+static size_t split_carve(void* ws, int nq, const fg_search_params* p, SplitWs* out) {
+    const int p1 = std::max(1, std::min(p->top_m, p->p1_lists));
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t r = o;
+        o += (bytes + 255) / 256 * 256;
+        return r;
+    };
+    const size_t oc = take((size_t)nq * p1 * 4), on = take((size_t)nq * 4), of = take((size_t)nq * 4),
+                 oa = take((size_t)nq * split_capg(p) * 8);
+    if (out) {
+        char* b = static_cast<char*>(ws);
+        out->cut = reinterpret_cast<float*>(b + oc);
+        out->cnt = reinterpret_cast<int32_t*>(b + on);
+        out->flags = reinterpret_cast<int32_t*>(b + of);
+        out->cand = reinterpret_cast<unsigned long long*>(b + oa);
+    }
+    return o;
+}
+
+// Launches the split path: zero the counts, phase 1, phase 2, per-query
+// selection, then the per-query kernel for the queries the selection flagged
+// (its CTAs for the others return at once).
+static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* ws, cudaStream_t stream,
+                             int smem_max) {
+    const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
+    fg_search_params pp{};
+    pp.top_m = a.top_m;
+    pp.p1_lists = a.p1;
+    pp.rerank_m = a.rerank_m;
+    pp.ref_compat = a.ref_compat;
+    SplitWs w;
+    split_carve(ws, nq, &pp, &w);
+    a.cut_g = w.cut;
+    a.cnt_g = w.cnt;
+    a.flags = w.flags;
+    a.cand_g = w.cand;
+    a.capg = split_capg(&pp);
+    // the fallback kernel's shared memory must fit, as on the per-query path
+    ScanKernel k = pick_scan_kernel(M, SD);
+    a.cap = a.rsel + SCAN_NT;
+    const ScanLayout L = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
+    if (!k || L.total > smem_max)
+        return fail(FG_ERR_UNSUPPORTED, "scan needs %d bytes of shared memory (max %d): rerank_m=%d "
+                    "max_list_len=%d", L.total, smem_max, a.rerank_m, a.lmax);
+    FG_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, (size_t)nq * 4, stream));
+    const int dpad = (a.dim + 3) / 4 * 4;
+    if (a.p1 > 0) {
+        SplitKernel k1 = pick_split_kernel<false>(M, SD);
+        const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a.lmax) + (int)sizeof(SplitMisc);
+        if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 1 needs %d bytes of shared memory", bytes);
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k1), bytes));
+        k1<<<(unsigned)((long long)nq * a.p1), SPLIT_NT, bytes, stream>>>(a, nq);
+        int rc = check_launch("split_p1_kernel");
+        if (rc) return rc;
+    }
+    if (a.top_m > a.p1) {
+        ScanArgs a2 = a;
+        a2.lmax = std::max(ix->max_list_len, 1);  // phase 2 has no 1024-row clamp
+        SplitKernel k2 = pick_split_kernel<true>(M, SD);
+        const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a2.lmax) + (int)sizeof(SplitMisc);
+        if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 2 needs %d bytes of shared memory", bytes);
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k2), bytes));
+        k2<<<(unsigned)((long long)nq * (a.top_m - a.p1)), SPLIT_NT, bytes, stream>>>(a2, nq);
+        int rc = check_launch("split_p2_kernel");
+        if (rc) return rc;
+    }
+    const int sort_cap = next_pow2(std::max(256, 2 * a.rsel));
+    const int sbytes = sort_cap * 8 + (int)sizeof(SelMisc);
+    if (sbytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split select needs %d bytes of shared memory", sbytes);
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&split_select_kernel), sbytes));
+    split_select_kernel<<<nq, SEL_NT, sbytes, stream>>>(a, nq, sort_cap);
+    int rc = check_launch("split_select_kernel");
+    if (rc) return rc;
+    a.only = w.flags;
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k), L.total));
+    k<<<nq, SCAN_NT, L.total, stream>>>(a);
+    return check_launch("ivfpq_batch_kernel");
+}
+
+size_t batch_logic_workspace(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
+    if (!split_chosen(ix, p, nq)) return 0;
+    return split_carve(nullptr, nq, p, nullptr) + 256;
+}
+
 int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uint32_t* probe_ids,
                 const float* probe_dists, const fg_search_params* p, int32_t* top_ids,
                 float* top_dists, int32_t* top_counts, int32_t* cand_counts, cudaStream_t stream,
-                bool write_pad, int* work_counter) {
+                bool write_pad, int* work_counter, void* ws, size_t ws_bytes) {
     FG_REQUIRE(ix && p, "null index or params");
     FG_REQUIRE(nq >= 0, "nq < 0");
     FG_REQUIRE(ix->dim > 0 && ix->pq_m > 0 && ix->dim % ix->pq_m == 0, "dim %d not divisible by pq_m %d",
@@ -1434,12 +1936,24 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.write_pad = write_pad ? 1 : 0;
     a.small = 0;
     a.work_counter = work_counter;
+    a.cut_g = nullptr;
+    a.cnt_g = nullptr;
+    a.cand_g = nullptr;
+    a.flags = nullptr;
+    a.only = nullptr;
+    a.capg = 0;
 
     int smem_max = 0, smem_sm = 0;
     smem_max = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin);
     smem_sm = device_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor);
     if (smem_max <= 0 || smem_sm <= 0) return fail(FG_ERR_CUDA, "cannot read the device's shared-memory limits");
 
+    if (split_chosen(ix, p, nq)) {
+        const size_t need = split_carve(nullptr, nq, p, nullptr);
+        if (ws && ws_bytes >= need) return batch_logic_split(a, ix, nq, ws, stream, smem_max);
+        if (getenv("FG_SCAN_KERNEL") && std::string(getenv("FG_SCAN_KERNEL")) == "split")
+            return fail(FG_ERR_WORKSPACE, "FG_SCAN_KERNEL=split needs %zu workspace bytes", need);
+    }
     // The team kernel when the codebook and at least one team fit in shared
     // memory (two teams for on-the-fly ADC).  FG_SCAN_KERNEL=block|team|team_lut|team_otf
     // and FG_SCAN_TEAM_NT=64|128|256 override the choice (for tests and measurements).

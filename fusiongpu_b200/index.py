@@ -523,8 +523,10 @@ def run_gpu_batch_logic(index: IVFPQIndex, queries, probe_ids, probe_dists, para
     tc = torch.empty(nq, dtype=torch.int32, device=dev)
     cc = torch.empty(nq, dtype=torch.int32, device=dev)
     cp = params.c()
-    _lib.call("fg_batch_logic", C.byref(index.view), _p(q), nq, _p(pid), _p(pd), C.byref(cp), _p(tid), _p(td),
-              _p(tc), _p(cc), _stream())
+    wb = _lib.size_query("fg_batch_logic_workspace_size", C.byref(index.view), C.byref(cp), nq)
+    ws = _workspace(wb, dev)
+    _lib.call("fg_batch_logic_ws", C.byref(index.view), _p(q), nq, _p(pid), _p(pd), C.byref(cp), _p(tid), _p(td),
+              _p(tc), _p(cc), _p(ws), ws.numel(), _stream())
     return tid, td, tc, cc
 
 

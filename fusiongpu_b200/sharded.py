@@ -66,7 +66,7 @@ def exchange(ids, dists, l2g, world, group, device, timings=None):
     nq, k = dists.shape
     keys = torch.empty((nq * k,), dtype=torch.int64, device=device)
     nmap = 0 if l2g is None else l2g.numel()
-    _lib.call("fg_pack_topk", _p(ids), _p(dists), ids.numel(), _p(l2g), nmap, _p(keys), _stream())
+    _lib.call("fg_pack_topk", _p(ids), _p(dists), nq, k, _p(l2g), nmap, _p(keys), _stream())
     if world == 1:
         allk = keys
     else:

@@ -142,6 +142,20 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
                    const fg_search_params* params, int32_t* top_ids, float* top_dists,
                    int32_t* top_counts, int32_t* candidate_counts, void* stream);
 
+/* The same with a caller workspace of at least fg_batch_logic_workspace_size
+ * bytes (256-byte aligned; 0 bytes, and any pointer, when the size is 0).
+ * With it, long lists (mean length above 400) run the split path: one CTA
+ * per (query, probed list) for phase 1 and for phase 2, candidates in a
+ * per-query region of the workspace, then one selection CTA per query --
+ * the same results as fg_batch_logic, bit for bit.  fg_search uses it. */
+int fg_batch_logic_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params, int32_t nq,
+                                  size_t* bytes);
+int fg_batch_logic_ws(const fg_ivfpq_view* index, const float* queries, int32_t nq,
+                      const uint32_t* probe_ids, const float* probe_dists,
+                      const fg_search_params* params, int32_t* top_ids, float* top_dists,
+                      int32_t* top_counts, int32_t* candidate_counts, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* ---- candidate budget: replaces prune_and_count_fused_kernel + the offsets
  * scan (gpu_global.cu:31-77, 709-725).  counts[q] = summed length of the
  * probed lists whose distance is <= probe_dists[q][0] * prune_ratio (the
@@ -203,14 +217,16 @@ int fg_map_ids(const int32_t* in, int64_t n, const int32_t* map, int64_t nmap, i
 int fg_merge_topk(const float* dists, const int32_t* ids, int32_t nshards, int32_t nq, int32_t k,
                   int32_t* out_ids, float* out_dists, void* stream);
 
-/* The exchange as ONE all-gather: fg_pack_topk writes keys[i] =
- * orderable(dists[i]) << 32 | global id (global id = map[ids[i]], or ids[i]
- * when map is null; -1 for an id outside the map), so that each GPU's [nq][k]
- * result is a single uint64 tensor; after the all-gather of those keys
- * ([nshards][nq][k]) fg_merge_topk_keys keeps the k smallest keys per query,
- * i.e. by (distance, global id), and unpacks them.  nshards * k <= 4096. */
-int fg_pack_topk(const int32_t* ids, const float* dists, int64_t n, const int32_t* map, int64_t nmap,
-                 uint64_t* keys, void* stream);
+/* The exchange as ONE all-gather: fg_pack_topk turns each GPU's [nq][k]
+ * result into one uint64 tensor, key = orderable(distance) << 32 | global id
+ * (global id = map[id], or the id itself when map is null; -1 for an id
+ * outside the map), each row of k keys sorted ascending; after the all-gather
+ * of those keys ([nshards][nq][k], rows as fg_pack_topk wrote them)
+ * fg_merge_topk_keys merges the nshards sorted rows of each query, keeps the
+ * k smallest keys, i.e. by (distance, global id), and unpacks them.
+ * k <= 4096, nshards * k <= 4096. */
+int fg_pack_topk(const int32_t* ids, const float* dists, int32_t nq, int32_t k, const int32_t* map,
+                 int64_t nmap, uint64_t* keys, void* stream);
 int fg_merge_topk_keys(const uint64_t* keys, int32_t nshards, int32_t nq, int32_t k, int32_t* out_ids,
                        float* out_dists, void* stream);
 

@@ -28,15 +28,16 @@ def fg():
 
 
 SCAN_KERNELS = ["auto", "block", "team_otf/64", "team_otf/128", "team_otf/256", "team_lut/64", "team_lut/128",
-                "team_lut/256", "team_otf/64/teamselect"]
+                "team_lut/256", "team_otf/64/teamselect", "split"]
 
 
 @pytest.fixture(params=SCAN_KERNELS)
 def scan_kernel(request, monkeypatch):
-    """Runs the test once per scan kernel: the per-query CTA kernel and the
+    """Runs the test once per scan kernel: the per-query CTA kernel, the
     team kernel with table or on-the-fly ADC, teams of 64, 128 or 256 threads
-    (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat), and
-    the team-wide list selection (FG_SCAN_WARP_SELECT=0)."""
+    (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat), the
+    team-wide list selection (FG_SCAN_WARP_SELECT=0), and the split path (one
+    CTA per probed list, candidates in the workspace)."""
     if request.param != "auto":
         kern, _, rest = request.param.partition("/")
         nt, _, sel = rest.partition("/")
@@ -566,3 +567,27 @@ def test_search_graph_survives_a_larger_search(fg):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(_np(ids), _np(ei))
         np.testing.assert_array_equal(_np(d), _np(ed))
+
+
+@pytest.mark.parametrize("coeff", [50.0, 1.6])
+@pytest.mark.parametrize("ref_compat", [True, False])
+def test_split_overflow_falls_back_to_per_query_kernel(fg, monkeypatch, coeff, ref_compat):
+    """Queries whose candidates overflow the split path's per-query region
+    (4096 keys) are recomputed by the per-query kernel: with every phase-2
+    vector passing (coefficient 50) all queries overflow, with 1.6 some do;
+    the results still equal the oracle's."""
+    monkeypatch.setenv("FG_SCAN_KERNEL", "split")
+    index, base, q = dataset("int128")
+    pd = dict(top_m=64, p1_lists=2, limit_k=20, threshold_coeff=coeff, prune_ratio=100.0, rerank_m=600,
+              final_k=10, mini_batch=64, epsilon=0.1, beta=2, ref_compat=ref_compat)
+    p = fg.SearchParams(**pd)
+    eids, ed = oracle.coarse(index["centroids"], q, p.top_m)
+    idx = fg.IVFPQIndex.from_arrays(index, base)
+    ti, td, tc, cc = fg.run_gpu_batch_logic(idx, q, eids.view(np.int32), ed, p)
+    oi, od, oc, st = oracle.batch_logic(index, q, eids, ed, **pd)
+    if coeff > 10:
+        assert (st["count"] > 4096).all()
+    np.testing.assert_array_equal(_np(cc), st["count"])
+    np.testing.assert_array_equal(_np(tc), oc)
+    np.testing.assert_array_equal(_np(td), od)
+    np.testing.assert_array_equal(_np(ti), oi)

@@ -48,22 +48,23 @@ def _merge_keys_gpu(d, i, k):
     for s in range(ns):
         td = torch.from_numpy(np.ascontiguousarray(d[s])).cuda()
         ti = torch.from_numpy(np.ascontiguousarray(i[s])).cuda()
-        _lib.call("fg_pack_topk", _p(ti), _p(td), ti.numel(), None, 0, _p(keys[s]), _stream())
+        _lib.call("fg_pack_topk", _p(ti), _p(td), nq, kk, None, 0, _p(keys[s]), _stream())
     oi = torch.empty((nq, k), dtype=torch.int32, device="cuda")
     od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
     _lib.call("fg_merge_topk_keys", _p(keys), ns, nq, k, _p(oi), _p(od), _stream())
     return keys.cpu().numpy(), oi.cpu().numpy(), od.cpu().numpy()
 
 
-def test_packed_key_merge_matches_host_statements():
-    rng = np.random.default_rng(4)
-    ns, nq, k = 6, 150, 20
+@pytest.mark.parametrize("ns,nq,k", [(6, 150, 20), (1, 33, 7), (2, 70, 100), (8, 40, 100), (3, 9, 1)])
+def test_packed_key_merge_matches_host_statements(ns, nq, k):
+    rng = np.random.default_rng(4 + ns + k)
     d = np.sort(rng.integers(-10, 10, size=(ns, nq, k)).astype(np.float32) * 0.25, axis=2)  # ties, negatives
     i = rng.permutation(ns * nq * k).reshape(ns, nq, k).astype(np.int32)
     d[:, :, -3:] = np.finfo(np.float32).max
     i[:, :, -3:] = -1
     keys, oi, od = _merge_keys_gpu(d, i, k)
-    np.testing.assert_array_equal(keys, np.stack([shard_ref.pack_keys_host(i[s], d[s]) for s in range(ns)]))
+    want = np.stack([np.sort(shard_ref.pack_keys_host(i[s], d[s]).view(np.uint64), axis=1) for s in range(ns)])
+    np.testing.assert_array_equal(keys.view(np.uint64), want)
     ei, ed = shard_ref.merge_topk_host(d, i, k)
     np.testing.assert_array_equal(oi, ei)
     np.testing.assert_array_equal(od, ed)
@@ -76,9 +77,9 @@ def test_pack_maps_local_ids():
     d = torch.tensor([1.0, 2.0, 3.0, 4.0, 0.5], device="cuda")
     m = torch.tensor([10, 11, 12, 13], dtype=torch.int32, device="cuda")
     keys = torch.empty(5, dtype=torch.int64, device="cuda")
-    _lib.call("fg_pack_topk", _p(ids), _p(d), 5, _p(m), 4, _p(keys), _stream())
+    _lib.call("fg_pack_topk", _p(ids), _p(d), 1, 5, _p(m), 4, _p(keys), _stream())
     want = shard_ref.pack_keys_host(np.array([10, 13, -1, -1, 12], np.int32), d.cpu().numpy())
-    np.testing.assert_array_equal(keys.cpu().numpy(), want)
+    np.testing.assert_array_equal(keys.cpu().numpy().view(np.uint64), np.sort(want.view(np.uint64)))
 
 
 def test_merge_kernel_matches_host_statement():
