@@ -81,6 +81,51 @@ __global__ void gather_rows_kernel(const float* __restrict__ data, int dim, cons
     for (int t = threadIdx.x; t < dim; t += blockDim.x) out[(size_t)i * dim + t] = src[t];
 }
 
+// Uniform integer in [0, range) from a 32-bit MT19937 by multiply-shift with
+// rejection (D. Lemire, "Fast Random Integer Generation in an Interval", ACM
+// TOMACS 29(1), 2019) -- how GCC's uniform_int_distribution bounds a 32-bit
+// generator.
+static uint32_t mt_below(Mt19937& g, uint32_t range) {
+    uint64_t prod = (uint64_t)g.next() * range;
+    uint32_t low = (uint32_t)prod;
+    if (low < range) {
+        const uint32_t thr = (0u - range) % range;
+        while (low < thr) {
+            prod = (uint64_t)g.next() * range;
+            low = (uint32_t)prod;
+        }
+    }
+    return (uint32_t)(prod >> 32);
+}
+
+// v = a permutation of 0..n-1: std::shuffle(iota, MT19937(seed)) as GCC's
+// standard library performs it, the draw the reference's PQ trainer makes
+// (pq_utils.h:24-26, :90-93).  Fisher-Yates: element i swaps with a uniform
+// position in [0, i]; while the generator's range covers n*n, one draw in
+// [0, (i+1)(i+2)) gives the positions of elements i and i+1 (quotient and
+// remainder by i+2), after one draw in [0, 1] for element 1 when n is even.
+static void std_shuffle_iota(int64_t n, uint32_t seed, std::vector<int32_t>& v) {
+    v.resize(n);
+    for (int64_t i = 0; i < n; ++i) v[i] = (int32_t)i;
+    if (n <= 1) return;
+    Mt19937 g(seed);
+    if (0xffffffffull / (uint64_t)n >= (uint64_t)n) {
+        int64_t i = 1;
+        if (n % 2 == 0) {
+            std::swap(v[1], v[mt_below(g, 2u)]);
+            i = 2;
+        }
+        for (; i < n; i += 2) {
+            const uint64_t b1 = (uint64_t)i + 2;
+            const uint32_t x = mt_below(g, (uint32_t)(((uint64_t)i + 1) * b1));
+            std::swap(v[i], v[x / b1]);
+            std::swap(v[i + 1], v[x % b1]);
+        }
+        return;
+    }
+    for (int64_t i = 1; i < n; ++i) std::swap(v[i], v[mt_below(g, (uint32_t)(i + 1))]);
+}
+
 static int upload_rows(const std::vector<int64_t>& rows, int64_t* d_rows, cudaStream_t s) {
     // pageable source: cudaMemcpyAsync stages it before returning
     FG_CUDA_TRY(cudaMemcpyAsync(d_rows, rows.data(), rows.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
@@ -326,8 +371,10 @@ __global__ void pq_assign_kernel(const float* __restrict__ res, int64_t S, int d
     for (int kc = 0; kc < 256; ++kc) {
         float d = 0.0f;
         for (int t = 0; t < sd; ++t) {
+            // `d += diff * diff` with two roundings, as the reference trainer
+            // computes it (pq_utils.h:44-47; built without FMA contraction)
             const float df = x[t] - scb[kc * sd + t];
-            d = fmaf(df, df, d);
+            d = __fadd_rn(d, __fmul_rn(df, df));
         }
         if (d < best) {
             best = d;
@@ -383,13 +430,14 @@ int pq_train(const float* data, int64_t n, int dim, const int32_t* assign, const
     void* sws = static_cast<char*>(ws) + used;
     const size_t sws_bytes = ws_bytes - used;
 
-    // strided sample of residuals (seed 12345)
+    // the sample: the first S rows of std::shuffle(0..n-1, MT19937(12345)),
+    // residuals in that order (pq_utils.h:88-104)
+    FG_REQUIRE(n <= 0x7fffffffll, "pq_train samples from at most 2^31 - 1 rows");
     std::vector<int64_t> hrows;
     {
-        Mt19937 g(12345u);
-        const int64_t stride = std::max<int64_t>(1, n / S);
-        hrows.resize(S);
-        for (int64_t i = 0; i < S; ++i) hrows[i] = (i * stride + (int64_t)(g.next() % (uint32_t)stride)) % n;
+        std::vector<int32_t> perm;
+        std_shuffle_iota(n, 12345u, perm);
+        hrows.assign(perm.begin(), perm.begin() + S);
     }
     int rc = upload_rows(hrows, rows, s);
     if (rc) return rc;
@@ -397,12 +445,13 @@ int pq_train(const float* data, int64_t n, int dim, const int32_t* assign, const
     if ((rc = check_launch("gather_residuals_kernel"))) return rc;
     FG_CUDA_TRY(cudaStreamSynchronize(s));  // before the host row list is reused
 
-    // per-subspace seeds 1234 + m, strided over the sample
+    // subspace m starts from the sample rows at the first 256 positions of
+    // std::shuffle(0..S-1, MT19937(1234 + m)) (pq_utils.h:20-31)
     std::vector<int64_t> init((size_t)pq_m * 256);
     for (int m = 0; m < pq_m; ++m) {
-        std::vector<int64_t> r;
-        strided_rows(S, 256, 1234u + (uint32_t)m, r);
-        std::copy(r.begin(), r.end(), init.begin() + (size_t)m * 256);
+        std::vector<int32_t> r;
+        std_shuffle_iota(S, 1234u + (uint32_t)m, r);
+        std::copy(r.begin(), r.begin() + 256, init.begin() + (size_t)m * 256);
     }
     if ((rc = upload_rows(init, rows, s))) return rc;
     pq_init_kernel<<<pq_m, 256, 0, s>>>(res, dim, sd, rows, pq_m, codebook);

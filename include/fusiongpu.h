@@ -379,9 +379,14 @@ int fg_kmeans_workspace_size(int64_t n, int32_t dim, int32_t k, size_t* bytes);
 int fg_kmeans(const float* data, int64_t n, int32_t dim, int32_t k, int32_t iters, uint32_t seed,
               float* centroids, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Residual PQ codebook training on a strided sample (seed 12345) with a
- * 256-way k-means per subspace (seed 1234+m).  Replaces
- * train_residual_pq_codebooks (pq_utils.h:77-138). */
+/* Residual PQ codebook training, the codebook the reference's
+ * train_residual_pq_codebooks (pq_utils.h:77-138) writes, bit for bit: the
+ * sample is the first `sample` rows of std::shuffle(0..n-1, MT19937(12345))
+ * (GCC's shuffle, restated on the host), and each subspace runs a 256-way
+ * k-means seeded with the rows at the first 256 positions of
+ * std::shuffle(0..S-1, MT19937(1234 + m)), distances `d += diff * diff` with
+ * two roundings, means summed in sample order in double.  n < 2^31.
+ * Synchronises the host (the shuffles run there). */
 int fg_pq_train_workspace_size(int64_t n, int32_t dim, int32_t pq_m, int32_t sample, size_t* bytes);
 int fg_pq_train(const float* data, int64_t n, int32_t dim, const int32_t* assign,
                 const float* centroids, int32_t pq_m, int32_t sample, int32_t iters,

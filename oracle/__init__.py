@@ -197,6 +197,35 @@ def mt19937(seed: int, skip: int = 0) -> int:
     return int(lib().fgo_mt19937_first(C.c_uint32(seed), skip))
 
 
+def std_shuffle(n: int, seed: int) -> np.ndarray:
+    """std::shuffle(0..n-1, std::mt19937(seed)) as libstdc++ performs it."""
+    a = np.arange(n, dtype=np.int32)
+    lib().fgo_std_shuffle(_p(a), C.c_int64(n), C.c_uint32(seed))
+    return a
+
+
+def pq_sample_rows(n: int, sample: int, pq_m: int) -> tuple[np.ndarray, np.ndarray]:
+    """(rows [S], init [pq_m][256]) that pq_train samples and seeds with."""
+    S = min(sample, n)
+    rows = np.empty(S, np.int32)
+    init = np.empty((pq_m, 256), np.int32)
+    _check(lib().fgo_pq_sample_rows(C.c_int64(n), C.c_int64(S), pq_m, _p(rows), _p(init)), "pq_sample_rows")
+    return rows, init
+
+
+def ref_std_shuffle(n: int, seed: int):
+    """std::shuffle from the C++ standard library itself (oracle/_ref), or None."""
+    for f in sorted(os.listdir(REF_DIR)) if os.path.isdir(REF_DIR) else []:
+        if f.startswith("libref_pq_"):
+            L = C.CDLL(os.path.join(REF_DIR, f))
+            if not hasattr(L, "ref_std_shuffle"):
+                return None
+            out = np.empty(n, np.int32)
+            L.ref_std_shuffle(n, C.c_uint(seed), _p(out))
+            return out
+    return None
+
+
 def kmeans(data, k, iters, seed=42, nthreads=0):
     data = np.ascontiguousarray(data, np.float32)
     cen = np.empty((k, data.shape[1]), np.float32)
@@ -383,3 +412,54 @@ def graph_search(data, graph, queries, itopk=128, search_width=4, max_iterations
                                   C.c_uint32(seed), 1 if metric == "ip" else 0, _p(oi), _p(od), _p(cnt), nthreads),
            "graph_search")
     return oi, od, cnt
+
+
+# ---- the reference's kmeans_gpu.cuh (oracle/_ref/libref_km.so; needs a GPU) ----
+
+def _ref_km():
+    so = os.path.join(REF_DIR, "libref_km.so")
+    return C.CDLL(so) if os.path.exists(so) else None
+
+
+def ref_kmeans(data, k, iters):
+    """run_kmeans_gpu (kmeans_gpu.cuh:234-324) on host data, or None."""
+    L = _ref_km()
+    if L is None:
+        return None
+    data = np.ascontiguousarray(data, np.float32)
+    out = np.empty((k, data.shape[1]), np.float32)
+    _check(L.ref_run_kmeans(_p(data), data.shape[0], data.shape[1], k, iters, _p(out)), "ref_run_kmeans")
+    return out
+
+
+def ref_assign(data, centroids):
+    """gpu_assign_to_centroids (kmeans_gpu.cuh:367-394), or None."""
+    L = _ref_km()
+    if L is None:
+        return None
+    data = np.ascontiguousarray(data, np.float32)
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    out = np.empty(data.shape[0], np.int32)
+    _check(L.ref_assign(_p(data), _p(centroids), data.shape[0], data.shape[1], centroids.shape[0], _p(out)),
+           "ref_assign")
+    return out
+
+
+def ref_encode(data, assignment, centroids, codebook):
+    """encode_residuals_to_pq_gpu (kmeans_gpu.cuh:450-508), or None."""
+    L = _ref_km()
+    if L is None:
+        return None
+    data = np.ascontiguousarray(data, np.float32)
+    pq_m = codebook.shape[0]
+    codes = np.empty((data.shape[0], pq_m), np.uint8)
+    _check(L.ref_encode(_p(data), data.shape[0], data.shape[1], _p(np.ascontiguousarray(assignment, np.int32)),
+                        _p(np.ascontiguousarray(centroids, np.float32)), centroids.shape[0],
+                        _p(np.ascontiguousarray(codebook, np.float32)), pq_m, _p(codes)), "ref_encode")
+    return codes
+
+
+def ref_kmeans_cleanup():
+    L = _ref_km()
+    if L is not None:
+        L.ref_kmeans_cleanup()

@@ -441,6 +441,58 @@ uint32_t fgo_mt19937_first(uint32_t seed, int skip) {
     return mt_next(&s);
 }
 
+/* ---- std::shuffle over MT19937, as the reference's PQ trainer draws it -----
+ * pq_utils.h:24-26 and :90-93 call std::shuffle(v.begin(), v.end(), mt19937)
+ * on a std::vector<int>.  With GCC's libstdc++ that is a Fisher-Yates shuffle
+ * (element i swaps with a uniform position in [0, i], i = 1 .. n-1) whose
+ * bounded integers come from Lemire's multiply-shift method with rejection
+ * ("Fast Random Integer Generation in an Interval", ACM TOMACS 29(1), 2019)
+ * on the 32-bit generator; when the generator's range covers n*n, one draw
+ * in [0, (i+1)(i+2)) yields the swap positions of elements i and i+1 (the
+ * quotient and the remainder by i+2), after a single draw in [0, 1] for
+ * element 1 when n is even.  Pinned against std::shuffle itself by the CPU
+ * tests (oracle/_ref). */
+static uint32_t mt_below(mt19937_t* g, uint32_t range) {
+    uint64_t prod = (uint64_t)mt_next(g) * range;
+    uint32_t low = (uint32_t)prod;
+    if (low < range) {
+        const uint32_t thr = (uint32_t)(0u - range) % range;
+        while (low < thr) {
+            prod = (uint64_t)mt_next(g) * range;
+            low = (uint32_t)prod;
+        }
+    }
+    return (uint32_t)(prod >> 32);
+}
+
+static void swap_i32(int32_t* a, int64_t i, int64_t j) {
+    const int32_t t = a[i];
+    a[i] = a[j];
+    a[j] = t;
+}
+
+void fgo_std_shuffle(int32_t* a, int64_t n, uint32_t seed) {
+    if (n <= 1) return;
+    mt19937_t g;
+    mt_seed(&g, seed);
+    if (0xffffffffull / (uint64_t)n >= (uint64_t)n) {
+        int64_t i = 1;
+        if (n % 2 == 0) {
+            swap_i32(a, 1, (int64_t)mt_below(&g, 2u));
+            i = 2;
+        }
+        while (i < n) {
+            const uint64_t b1 = (uint64_t)i + 2;
+            const uint32_t x = mt_below(&g, (uint32_t)(((uint64_t)i + 1) * b1));
+            swap_i32(a, i, (int64_t)(x / b1));
+            swap_i32(a, i + 1, (int64_t)(x % b1));
+            i += 2;
+        }
+        return;
+    }
+    for (int64_t i = 1; i < n; ++i) swap_i32(a, i, (int64_t)mt_below(&g, (uint32_t)(i + 1)));
+}
+
 /* Strided initial centroids: point (i*stride + rng() % stride) % n for
  * centroid i, stride = max(1, n/k) (kmeans_gpu.cuh:259-267). */
 int fgo_kmeans_init(const float* data, int64_t n, int dim, int k, uint32_t seed, float* centroids) {
@@ -642,9 +694,31 @@ int fgo_rebalance(const float* data, int64_t n, int dim, const int32_t* assign,
     return rc;
 }
 
-/* Residual PQ training: a strided sample of `sample` residuals (seed 12345),
- * then an independent 256-way k-means per subspace (seed 1234 + m, `iters`
- * Lloyd steps), as pq_utils.h:77-138 structures it. */
+/* Residual PQ training as pq_utils.h:77-138 computes it: the first `sample`
+ * rows of std::shuffle(0..n-1, MT19937(12345)) give the residuals (in that
+ * order); per subspace m, an independent 256-way k-means (pq_utils.h:17-72):
+ * codeword c starts as the sample row at position c of
+ * std::shuffle(0..S-1, MT19937(1234 + m)); `iters` Lloyd steps assign each
+ * row to the first nearest codeword by `d += diff * diff` evaluated as a
+ * rounded product then a rounded sum (the reference is built without FMA
+ * contraction), and move each non-empty codeword to the mean of its rows,
+ * summed in sample order in double and rounded to float. */
+static void pq_assign_sep(const float* sub, int64_t S, int sd, const float* cb, int32_t* as) {
+    for (int64_t i = 0; i < S; ++i) {
+        float best = FLT_MAX;
+        int32_t bc = 0;
+        for (int c = 0; c < 256; ++c) {
+            float d = 0.0f;
+            for (int t = 0; t < sd; ++t) {
+                const float df = sub[(size_t)i * sd + t] - cb[(size_t)c * sd + t];
+                d = d + df * df; /* two roundings: this file is built with -ffp-contract=off */
+            }
+            if (d < best) { best = d; bc = c; }
+        }
+        as[i] = bc;
+    }
+}
+
 int fgo_pq_train(const float* data, int64_t n, int dim, const int32_t* assign,
                  const float* centroids, int pq_m, int sample, int iters, float* codebook,
                  int nthreads) {
@@ -653,16 +727,17 @@ int fgo_pq_train(const float* data, int64_t n, int dim, const int32_t* assign,
     int64_t S = sample < n ? sample : n;
     if (S < 256) return 1;
     float* res = (float*)malloc((size_t)S * dim * sizeof(float));
-    if (!res) return 2;
-    mt19937_t s;
-    mt_seed(&s, 12345u);
-    int64_t stride = n / S > 1 ? n / S : 1;
+    int32_t* perm = (int32_t*)malloc((size_t)n * sizeof(int32_t));
+    if (!res || !perm) { free(res); free(perm); return 2; }
+    for (int64_t i = 0; i < n; ++i) perm[i] = (int32_t)i;
+    fgo_std_shuffle(perm, n, 12345u);
     for (int64_t i = 0; i < S; ++i) {
-        int64_t id = (i * stride + (int64_t)(mt_next(&s) % (uint32_t)stride)) % n;
+        const int64_t id = perm[i];
         const float* x = data + (size_t)id * dim;
         const float* c = centroids + (size_t)assign[id] * dim;
         for (int j = 0; j < dim; ++j) res[(size_t)i * dim + j] = x[j] - c[j];
     }
+    free(perm);
     int rc = 0;
     set_threads(nthreads);
 #pragma omp parallel for schedule(dynamic, 1)
@@ -671,22 +746,44 @@ int fgo_pq_train(const float* data, int64_t n, int dim, const int32_t* assign,
         float* cb = codebook + (size_t)m * 256 * sd;
         int32_t* as = (int32_t*)malloc((size_t)S * sizeof(int32_t));
         int32_t* cnt = (int32_t*)malloc(256 * sizeof(int32_t));
-        if (!sub || !as || !cnt) {
+        int32_t* idx = (int32_t*)malloc((size_t)S * sizeof(int32_t));
+        if (!sub || !as || !cnt || !idx) {
 #pragma omp atomic write
             rc = 2;
         } else {
             for (int64_t i = 0; i < S; ++i)
                 for (int t = 0; t < sd; ++t) sub[(size_t)i * sd + t] = res[(size_t)i * dim + m * sd + t];
-            fgo_kmeans_init(sub, S, sd, 256, 1234u + (uint32_t)m, cb);
+            for (int64_t i = 0; i < S; ++i) idx[i] = (int32_t)i;
+            fgo_std_shuffle(idx, S, 1234u + (uint32_t)m);
+            for (int c = 0; c < 256; ++c)
+                memcpy(cb + (size_t)c * sd, sub + (size_t)idx[c] * sd, (size_t)sd * sizeof(float));
             for (int it = 0; it < iters; ++it) {
-                fgo_assign(sub, S, sd, cb, 256, as, 1);
+                pq_assign_sep(sub, S, sd, cb, as);
                 fgo_kmeans_update(sub, S, sd, as, 256, cb, cnt);
             }
         }
-        free(sub); free(as); free(cnt);
+        free(sub); free(as); free(cnt); free(idx);
     }
     free(res);
     return rc;
+}
+
+/* The rows fg_pq_train samples and the codeword seeds of each subspace, for
+ * tests: rows[0..S) = first S of std::shuffle(0..n-1, MT19937(12345));
+ * init[m*256 + c] = position c of std::shuffle(0..S-1, MT19937(1234 + m)). */
+int fgo_pq_sample_rows(int64_t n, int64_t S, int pq_m, int32_t* rows, int32_t* init) {
+    int32_t* perm = (int32_t*)malloc((size_t)(n > S ? n : S) * sizeof(int32_t));
+    if (!perm) return 2;
+    for (int64_t i = 0; i < n; ++i) perm[i] = (int32_t)i;
+    fgo_std_shuffle(perm, n, 12345u);
+    memcpy(rows, perm, (size_t)S * sizeof(int32_t));
+    for (int m = 0; m < pq_m; ++m) {
+        for (int64_t i = 0; i < S; ++i) perm[i] = (int32_t)i;
+        fgo_std_shuffle(perm, S, 1234u + (uint32_t)m);
+        memcpy(init + (size_t)m * 256, perm, 256 * sizeof(int32_t));
+    }
+    free(perm);
+    return 0;
 }
 
 /* code[i][m] = nearest sub-codeword of the residual (first minimum wins), with

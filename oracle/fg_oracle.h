@@ -74,6 +74,10 @@ int fgo_knn_exact(const float* base, int64_t n, int dim, const float* queries, i
 
 /* build side */
 uint32_t fgo_mt19937_first(uint32_t seed, int skip);
+/* std::shuffle(a, a + n, std::mt19937(seed)) as GCC's libstdc++ performs it */
+void fgo_std_shuffle(int32_t* a, int64_t n, uint32_t seed);
+/* the sample rows and per-subspace codeword seeds of fgo_pq_train */
+int fgo_pq_sample_rows(int64_t n, int64_t S, int pq_m, int32_t* rows, int32_t* init);
 int fgo_kmeans_init(const float* data, int64_t n, int dim, int k, uint32_t seed, float* centroids);
 int fgo_assign(const float* data, int64_t n, int dim, const float* centroids, int k,
                int32_t* out_assign, int nthreads);

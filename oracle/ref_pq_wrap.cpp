@@ -36,3 +36,14 @@ extern "C" int ref_pq_encode(const float* data, int n, const int* vec_cluster_id
     encode_residuals_to_pq(reinterpret_cast<const point_t<float>*>(data), n, ids, cl, cb, codes);
     return 0;
 }
+
+/* std::shuffle of 0..n-1 with std::mt19937(seed), the draw pq_utils.h:24-26
+ * and :90-93 make, from this compiler's standard library: pins the oracle's
+ * restatement of it. */
+extern "C" void ref_std_shuffle(int n, unsigned seed, int* out) {
+    std::vector<int> v(n);
+    std::iota(v.begin(), v.end(), 0);
+    std::mt19937 rng(seed);
+    std::shuffle(v.begin(), v.end(), rng);
+    std::memcpy(out, v.data(), (size_t)n * sizeof(int));
+}

@@ -591,3 +591,19 @@ def test_split_overflow_falls_back_to_per_query_kernel(fg, monkeypatch, coeff, r
     np.testing.assert_array_equal(_np(tc), oc)
     np.testing.assert_array_equal(_np(td), od)
     np.testing.assert_array_equal(_np(ti), oi)
+
+
+@pytest.mark.parametrize("dim,pq_m,sample", [(128, 32, 6000), (96, 48, 50000)])
+def test_pq_training_equals_reference_codebook(fg, dim, pq_m, sample):
+    """fg_pq_train writes the codebook the reference's own
+    train_residual_pq_codebooks (pq_utils.h:77-138, oracle/_ref) writes."""
+    if oracle.ref_lib("pq", dim, pq_m) is None:
+        pytest.skip("oracle/_ref not built")
+    from fusiongpu_b200 import datasets as ds
+    spec = ds.dataclasses.replace(ds.scaled(ds.C1, 20000, 10, n_centres=16), dim=dim)
+    base, _ = ds.generate(spec)
+    cen = oracle.kmeans(base, 40, 3)
+    a = oracle.assign(base, cen)
+    cb = fg.train_residual_pq_codebooks(torch.from_numpy(base).cuda(), torch.from_numpy(a).cuda(),
+                                        torch.from_numpy(cen).cuda(), pq_m, sample, 6)
+    np.testing.assert_array_equal(_np(cb), oracle.ref_pq_train(base, a, cen, pq_m, sample, 6))

@@ -119,31 +119,40 @@ def test_kmeans_objective_decreases():
         prev = obj
 
 
-def test_pq_training_quality_matches_reference_pq_utils():
-    """The oracle's residual PQ trainer against the reference's own
+@pytest.mark.parametrize("n,seed", [(1, 5), (2, 7), (11, 2), (4096, 1234), (50000, 1234), (50001, 1235),
+                                    (65535, 3), (65536, 3), (300000, 12345)])
+def test_shuffle_equals_std_shuffle(n, seed):
+    """The oracle's std::shuffle restatement against std::shuffle of the C++
+    standard library the reference is compiled with (oracle/_ref): both the
+    paired-draw path (n*n within the generator's range) and the single-draw
+    path."""
+    ref = oracle.ref_std_shuffle(n, seed)
+    if ref is None:
+        pytest.skip("oracle/_ref not built (reference sources absent)")
+    np.testing.assert_array_equal(oracle.std_shuffle(n, seed), ref)
+
+
+@pytest.mark.parametrize("dim,pq_m,sample", [(64, 16, 4000), (128, 32, 50000), (96, 48, 7000), (128, 64, 3000)])
+def test_pq_training_equals_reference_pq_utils(dim, pq_m, sample):
+    """The oracle's residual PQ trainer reproduces the reference's own
     train_residual_pq_codebooks (pq_utils.h:77-138, compiled from source into
-    oracle/_ref): quantisation error within 2%."""
-    if oracle.ref_lib("pq", 64, 16) is None:
+    oracle/_ref) bit for bit: the same shuffled sample, the same seeded
+    codewords, the same two-rounding distances and double means."""
+    if oracle.ref_lib("pq", dim, pq_m) is None:
         pytest.skip("oracle/_ref not built (reference sources absent)")
     from fusiongpu_b200 import datasets as ds
-    spec = ds.scaled(ds.C1, 6000, 10, n_centres=16)
-    spec = ds.dataclasses.replace(spec, dim=64)
+    spec = ds.dataclasses.replace(ds.scaled(ds.C1, 9000, 10, n_centres=16), dim=dim)
     base, _ = ds.generate(spec)
-    cen = oracle.kmeans(base, 16, 5)
+    cen = oracle.kmeans(base, 24, 3)
     a = oracle.assign(base, cen)
-    ours = oracle.pq_train(base, a, cen, 16, 4000, 6)
-    ref = oracle.ref_pq_train(base, a, cen, 16, 4000, 6)
-
-    def mse(cb):
-        codes = oracle.pq_encode(base, a, cen, cb)
-        rec = cen[a] + cb[np.arange(16)[None, :], codes.astype(np.int64)].reshape(len(base), -1)
-        return float(((rec - base) ** 2).sum(1).mean())
-
-    assert abs(mse(ours) / mse(ref) - 1.0) < 0.02
-    # and the encoders agree where the reference's unfused arithmetic has no near-ties
-    rc = oracle.ref_pq_encode(base, a, cen, ref)
-    oc = oracle.pq_encode(base, a, cen, ref)
-    assert (rc == oc).mean() > 0.999
+    ours = oracle.pq_train(base, a, cen, pq_m, sample, 5)
+    ref = oracle.ref_pq_train(base, a, cen, pq_m, sample, 5)
+    np.testing.assert_array_equal(ours, ref)
+    if dim == 64:
+        # the encoders agree where the reference's unfused arithmetic has no near-ties
+        rc = oracle.ref_pq_encode(base, a, cen, ref)
+        oc = oracle.pq_encode(base, a, cen, ref)
+        assert (rc == oc).mean() > 0.999
 
 
 def skewed_lists(seed=3, n=12000, k=16):
