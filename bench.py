@@ -1125,6 +1125,11 @@ def main_c5(args):
             tot += e0.elapsed_time(e1)
         barrier()
         ms = max_over_ranks(tot / args.steps)
+    # one GPU: the oracle on a query sample of the same index (parity), and
+    # recall against rerank depth (what bounds recall at this nprobe)
+    parity, depth = None, None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        parity, depth = c5_parity(idx, queries, qd, gt, p, cfg, args)
     hq = torch.from_numpy(queries).pin_memory()
     hid = torch.empty((nq, cfg["k"]), dtype=torch.int32).pin_memory()
     qdev = torch.empty_like(qd)
@@ -1167,11 +1172,59 @@ def main_c5(args):
         "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(),
         "build_s": t_build,
+        "parity": parity,
+        "recall_by_knob": depth,
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def c5_parity(idx, queries, qd, gt, p, cfg, args):
+    """The GPU search of the first `sample` queries against the oracle on the
+    same index: the oracle's candidate generation, then its rerank over a
+    float copy of just the candidate rows (the oracle takes float vectors;
+    ids are renumbered in increasing order, so every comparison and tie
+    keeps its order) -- plus recall@10 at deeper reranks."""
+    import torch
+    import oracle
+    from fusiongpu_b200.index import recall_at, run_gpu_batch_logic
+    sample = 300
+    qs = np.ascontiguousarray(queries[:sample])
+    pid, pdist = idx.coarse(qd[:sample].contiguous(), p.top_m)
+    eids, ed = oracle.coarse(idx.centroids.cpu().numpy(), qs, p.top_m)
+    coarse_equal = bool(np.array_equal(pid.cpu().numpy().view(np.uint32), eids) and
+                        np.array_equal(pdist.cpu().numpy(), ed))
+    index_np = idx.to_numpy()
+    kw = oracle_kw(p)
+    t0 = time.perf_counter()
+    oi, od, oc, st = oracle.batch_logic(index_np, qs, eids, ed, nthreads=os.cpu_count() or 1, **kw)
+    rows = np.unique(oi[oi >= 0])
+    sub = idx.base[torch.from_numpy(rows).to(idx.device).long()].float().cpu().numpy()
+    remap = np.searchsorted(rows, np.where(oi >= 0, oi, 0)).astype(np.int32)
+    ri, rd = oracle.rerank(qs, np.where(oi >= 0, remap, oi).astype(np.int32), oc, sub, **kw)
+    ri = np.where(ri >= 0, rows[np.clip(ri, 0, rows.size - 1)], ri).astype(np.int32)
+    dt = time.perf_counter() - t0
+    gi, gd = idx.search(qd[:sample].contiguous(), p)
+    gi, gd = gi.cpu().numpy(), gd.cpu().numpy()
+    mism, rel = compare_results(gi, gd, ri, rd)
+    parity = {"queries": sample, "coarse_equal": coarse_equal, "id_mismatches_beyond_1e-5_ties": mism,
+              "max_rel_dist_err": rel, "bit_exact": bool(np.array_equal(gi, ri) and np.array_equal(gd, rd)),
+              "recall_gpu": recall_at(gi, gt[:sample], 10), "recall_oracle": recall_at(ri, gt[:sample], 10),
+              "oracle_s": dt, "mode": "intended"}
+    # recall@10 on the ground-truth queries as the candidate-generation knobs
+    # move: the rerank depth, the phase-1 per-list cap (limit_k) and the
+    # phase-2 threshold coefficient
+    depth = {}
+    ng = gt.shape[0]
+    for name, q in (("config", {}), ("rerank_m=1024", dict(rerank_m=1024)), ("rerank_m=4096", dict(rerank_m=4096)),
+                    ("limit_k=200", dict(limit_k=200)), ("limit_k=200,rerank_m=1024", dict(limit_k=200, rerank_m=1024)),
+                    ("threshold_coeff=1.5", dict(threshold_coeff=1.5)), ("p1_lists=64", dict(p1_lists=64)),
+                    ("nprobe=128", dict(top_m=128))):
+        ids, _ = idx.search(qd[:ng].contiguous(), p.replace(**q))
+        depth[name] = recall_at(ids.cpu().numpy(), gt, 10)
+    return parity, depth
 
 
 # ---- C4: graph index ------------------------------------------------------------
