@@ -1476,6 +1476,38 @@ __global__ void __launch_bounds__(SPLIT_NT) split_p1_kernel(const ScanArgs a, in
     }
 }
 
+// Phase-2 keys with early rejection: every LUT entry is a sum of squares
+// (>= 0), so the running ADC sum never decreases under round-to-nearest and a
+// row whose partial sum already exceeds thr cannot pass; it is abandoned after
+// that 16-subspace chunk and gets the key 0xffffffff (never emitted).  Rows
+// that pass are summed to the end in subspace order, so their keys are the
+// adc<M> ones bit for bit.
+template <int M>
+__device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int n, const float* lut, float thr,
+                                               uint32_t* keys) {
+    static_assert(M % 16 == 0, "16-code chunks");
+    for (int i = threadIdx.x; i < n; i += SPLIT_NT) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(a.codes + (size_t)(start + i) * M);
+        float d = 0.0f;
+        bool alive = true;
+#pragma unroll
+        for (int w = 0; w < M / 16; ++w) {
+            if (alive) {
+                const uint4 v = __ldg(r4 + w);
+                const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int b = 0; b < 16; ++b) {
+                    const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
+                    d = __fadd_rn(d, lut[(16 * w + b) * 256 + code]);
+                }
+                alive = d <= thr;
+            }
+        }
+        keys[i] = alive ? f2key(d) : 0xffffffffu;
+    }
+    __syncthreads();
+}
+
 template <int M, int SD>
 __global__ void __launch_bounds__(SPLIT_NT) split_p2_kernel(const ScanArgs a, int nq) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -1502,11 +1534,14 @@ __global__ void __launch_bounds__(SPLIT_NT) split_p2_kernel(const ScanArgs a, in
         ms->thr = (mn < FLT_MAX) ? mn * a.coeff : FLT_MAX;
     }
     split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
-    split_keys<M>(a, start, len, lut, keys);
     const float thr = ms->thr;
+    if constexpr (M % 16 == 0)
+        split_keys_thr<M>(a, start, len, lut, thr, keys);
+    else
+        split_keys<M>(a, start, len, lut, keys);
     unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
     const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
-    auto passes = [&](int i) { return key2f(keys[i]) <= thr; };
+    auto passes = [&](int i) { return keys[i] != 0xffffffffu && key2f(keys[i]) <= thr; };
     if (!a.ref_compat) {
         int n_t = 0;
         for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
