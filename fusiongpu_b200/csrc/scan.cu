@@ -1410,10 +1410,22 @@ __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, ui
     const float* cv = a.centroids + (size_t)c * a.dim;
     for (int t = threadIdx.x; t < a.dim; t += SPLIT_NT) res[t] = qv[t] - cv[t];
     __syncthreads();
+    if constexpr (SD == 2) {
+        // two codewords per thread: one 16-byte codebook load, one 8-byte store
 #pragma unroll 4
-    for (int e = threadIdx.x; e < M * 256; e += SPLIT_NT) {
-        const int m = e >> 8;
-        lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
+        for (int e2 = threadIdx.x; e2 < M * 128; e2 += SPLIT_NT) {
+            const int m = e2 >> 7;
+            const float4 cb = __ldg(reinterpret_cast<const float4*>(a.codebook) + e2);
+            const float2 r = *reinterpret_cast<const float2*>(res + m * 2);
+            const float rv[2] = {r.x, r.y}, c0[2] = {cb.x, cb.y}, c1[2] = {cb.z, cb.w};
+            reinterpret_cast<float2*>(lut)[e2] = make_float2(sd_arith<2>(rv, c0), sd_arith<2>(rv, c1));
+        }
+    } else {
+#pragma unroll 4
+        for (int e = threadIdx.x; e < M * 256; e += SPLIT_NT) {
+            const int m = e >> 8;
+            lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
+        }
     }
     __syncthreads();
 }
@@ -1425,8 +1437,35 @@ __device__ __forceinline__ void split_keys(const ScanArgs& a, int start, int n, 
     __syncthreads();
 }
 
+// ADC key of one row, or 0xffffffff once the running sum exceeds `bound`:
+// every LUT entry is a sum of squares (>= 0), so under round-to-nearest the
+// running sum never decreases and such a row's full distance exceeds bound too.
+// Rows within the bound are summed to the end in subspace order, so their keys
+// are adc<M>'s bit for bit.
+template <int M>
+__device__ __forceinline__ uint32_t adc_bounded(const uint8_t* row, const float* lut, float bound) {
+    static_assert(M % 16 == 0, "16-code chunks");
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    float d = 0.0f;
+    bool alive = true;
+#pragma unroll
+    for (int w = 0; w < M / 16; ++w) {
+        if (alive) {
+            const uint4 v = __ldg(r4 + w);
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int b = 0; b < 16; ++b) {
+                const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
+                d = __fadd_rn(d, lut[(16 * w + b) * 256 + code]);
+            }
+            alive = d <= bound;
+        }
+    }
+    return alive ? f2key(d) : 0xffffffffu;
+}
+
 template <int M, int SD>
-__global__ void __launch_bounds__(SPLIT_NT) split_p1_kernel(const ScanArgs a, int nq) {
+__global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a, int nq) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
@@ -1445,9 +1484,24 @@ __global__ void __launch_bounds__(SPLIT_NT) split_p1_kernel(const ScanArgs a, in
     const int wc = len < a.limit_k ? len : a.limit_k;
     const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
     split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
-    split_keys<M>(a, start, scan, lut, keys);
     uint32_t kth;
     int n_less;
+    if constexpr (M % 16 == 0) {
+        // the first SPLIT_NT rows in full; their wc-th smallest distance bounds
+        // the list's wc-th from above, so a later row whose partial sum passes
+        // it cannot be among the wc selected, and it gets the largest key
+        // (which changes neither the wc-th key nor the count below it)
+        const int head = (scan < SPLIT_NT || wc > SPLIT_NT) ? scan : SPLIT_NT;
+        split_keys<M>(a, start, head, lut, keys);
+        if (scan > head && wc <= head) {
+            block_radix_select<SPLIT_NT>(keys, head, wc, ms->hist, ms->b, kth, n_less);
+            for (int i = head + threadIdx.x; i < scan; i += SPLIT_NT)
+                keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, key2f(kth));
+            __syncthreads();
+        }
+    } else {
+        split_keys<M>(a, start, scan, lut, keys);
+    }
     block_radix_select<SPLIT_NT>(keys, scan, wc, ms->hist, ms->b, kth, n_less);
     if (threadIdx.x == 0) {
         a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
@@ -1476,40 +1530,17 @@ __global__ void __launch_bounds__(SPLIT_NT) split_p1_kernel(const ScanArgs a, in
     }
 }
 
-// Phase-2 keys with early rejection: every LUT entry is a sum of squares
-// (>= 0), so the running ADC sum never decreases under round-to-nearest and a
-// row whose partial sum already exceeds thr cannot pass; it is abandoned after
-// that 16-subspace chunk and gets the key 0xffffffff (never emitted).  Rows
-// that pass are summed to the end in subspace order, so their keys are the
-// adc<M> ones bit for bit.
+// Phase-2 keys: a row whose running sum passes thr cannot pass the threshold
+// and gets the key 0xffffffff (never emitted).
 template <int M>
 __device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int n, const float* lut, float thr,
                                                uint32_t* keys) {
-    static_assert(M % 16 == 0, "16-code chunks");
-    for (int i = threadIdx.x; i < n; i += SPLIT_NT) {
-        const uint4* r4 = reinterpret_cast<const uint4*>(a.codes + (size_t)(start + i) * M);
-        float d = 0.0f;
-        bool alive = true;
-#pragma unroll
-        for (int w = 0; w < M / 16; ++w) {
-            if (alive) {
-                const uint4 v = __ldg(r4 + w);
-                const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int b = 0; b < 16; ++b) {
-                    const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
-                    d = __fadd_rn(d, lut[(16 * w + b) * 256 + code]);
-                }
-                alive = d <= thr;
-            }
-        }
-        keys[i] = alive ? f2key(d) : 0xffffffffu;
-    }
+    for (int i = threadIdx.x; i < n; i += SPLIT_NT) keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, thr);
     __syncthreads();
 }
 
 template <int M, int SD>
-__global__ void __launch_bounds__(SPLIT_NT) split_p2_kernel(const ScanArgs a, int nq) {
+__global__ void __launch_bounds__(SPLIT_NT, 4) split_p2_kernel(const ScanArgs a, int nq) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
