@@ -893,7 +893,7 @@ def main_c3(args):
                      threshold_coeff=cfg["threshold_coeff"], prune_ratio=100.0, rerank_m=cfg["rerank_m"],
                      final_k=cfg["k"], mini_batch=cfg["mini_batch"], epsilon=cfg["epsilon"], beta=cfg["beta"],
                      ref_compat=False)
-    if args.profile in ("scan", "search", "rerank"):
+    if args.profile in ("scan", "search", "rerank", "coarse"):
         # warmup+1 launches of one stage alone (the target of ncu -s <warmup> -c 1)
         pid, pdist = idx.coarse(qd, cfg["nprobe"])
         ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pdist, p)
@@ -904,6 +904,8 @@ def main_c3(args):
                 run_gpu_batch_logic(idx, qd, pid, pdist, p)
             elif args.profile == "rerank":
                 run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+            elif args.profile == "coarse":
+                idx.coarse(qd, cfg["nprobe"])
             else:
                 idx.search(qd, p)
         torch.cuda.synchronize(device)
@@ -1092,6 +1094,24 @@ def main_c5(args):
                      final_k=cfg["k"], mini_batch=cfg["mini_batch"], epsilon=cfg["epsilon"], beta=cfg["beta"],
                      ref_compat=False)
     qd = torch.from_numpy(queries).to(device)
+    if args.profile in ("scan", "coarse", "rerank", "search") and world == 1:
+        # warmup+1 launches of one stage alone (the target of ncu -s <warmup> -c 1)
+        from fusiongpu_b200.index import run_gpu_batch_logic, run_gpu_rerank
+        pid, pdist = idx.coarse(qd, cfg["nprobe"])
+        ti, td, tc, cc = run_gpu_batch_logic(idx, qd, pid, pdist, p)
+        torch.cuda.synchronize(device)
+        for _ in range(args.warmup + 1):
+            if args.profile == "scan":
+                run_gpu_batch_logic(idx, qd, pid, pdist, p)
+            elif args.profile == "coarse":
+                idx.coarse(qd, cfg["nprobe"])
+            elif args.profile == "rerank":
+                run_gpu_rerank(qd, ti, tc, idx.base, p, device)
+            else:
+                idx.search(qd, p)
+        torch.cuda.synchronize(device)
+        print(json.dumps({"profile": args.profile, "workload": spec.name, "nq": int(queries.shape[0])}))
+        return
     gt = None
     if rank == 0:
         ng = cfg["gt_queries"]
