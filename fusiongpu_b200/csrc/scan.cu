@@ -1380,9 +1380,11 @@ constexpr int SEL_NT = 512;
 
 __host__ __device__ inline int split_keys_bytes(int lmax) { return ((lmax > 0 ? lmax : 1) * 4 + 15) / 16 * 16; }
 
+constexpr int SPLIT_P2_NT = 256;  // phase-2 CTAs outside ref_compat (more warps hide the code loads)
+
 struct SplitMisc {
     uint32_t hist[256];
-    int warp[SPLIT_NT / 32];
+    int warp[SPLIT_P2_NT / 32];
     uint32_t b[2];
     int base, n_pass;
     float thr;
@@ -1405,15 +1407,15 @@ __device__ __forceinline__ void split_probe(const ScanArgs& a, int q, int j, uin
 }
 
 // LUT of (query, list c) in shared memory: the entries of build_lut.
-template <int M, int SD>
+template <int M, int SD, int NT = SPLIT_NT>
 __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, uint32_t c, float* res, float* lut) {
     const float* cv = a.centroids + (size_t)c * a.dim;
-    for (int t = threadIdx.x; t < a.dim; t += SPLIT_NT) res[t] = qv[t] - cv[t];
+    for (int t = threadIdx.x; t < a.dim; t += NT) res[t] = qv[t] - cv[t];
     __syncthreads();
     if constexpr (SD == 2) {
         // two codewords per thread: one 16-byte codebook load, one 8-byte store
 #pragma unroll 4
-        for (int e2 = threadIdx.x; e2 < M * 128; e2 += SPLIT_NT) {
+        for (int e2 = threadIdx.x; e2 < M * 128; e2 += NT) {
             const int m = e2 >> 7;
             const float4 cb = __ldg(reinterpret_cast<const float4*>(a.codebook) + e2);
             const float2 r = *reinterpret_cast<const float2*>(res + m * 2);
@@ -1422,7 +1424,7 @@ __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, ui
         }
     } else {
 #pragma unroll 4
-        for (int e = threadIdx.x; e < M * 256; e += SPLIT_NT) {
+        for (int e = threadIdx.x; e < M * 256; e += NT) {
             const int m = e >> 8;
             lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
         }
@@ -1431,9 +1433,9 @@ __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, ui
 }
 
 // Keys of rows [0, n) of the list: thread t takes rows t, t + SPLIT_NT, ...
-template <int M>
+template <int M, int NT = SPLIT_NT>
 __device__ __forceinline__ void split_keys(const ScanArgs& a, int start, int n, const float* lut, uint32_t* keys) {
-    for (int i = threadIdx.x; i < n; i += SPLIT_NT) keys[i] = f2key(adc<M>(a.codes + (size_t)(start + i) * M, lut));
+    for (int i = threadIdx.x; i < n; i += NT) keys[i] = f2key(adc<M>(a.codes + (size_t)(start + i) * M, lut));
     __syncthreads();
 }
 
@@ -1502,6 +1504,55 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
     } else {
         split_keys<M>(a, start, scan, lut, keys);
     }
+    unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
+    const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
+    // The rows still in the running (key below 0xffffffff) go to a compact
+    // (key, position) list in the LUT's space, dead by now; the selection runs
+    // over them alone (the others all lie above the wc-th key, so the wc-th
+    // key and the count below it do not change).
+    {
+        const int ccap = M * 128;
+        uint32_t* ckey = reinterpret_cast<uint32_t*>(lut);
+        int32_t* cpos = reinterpret_cast<int32_t*>(lut) + ccap;
+        int n_t = 0;
+        for (int i = threadIdx.x; i < scan; i += SPLIT_NT) n_t += keys[i] != 0xffffffffu ? 1 : 0;
+        int n_c;
+        int o = block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, n_c);
+        if (n_c <= ccap) {
+            for (int i = threadIdx.x; i < scan; i += SPLIT_NT)
+                if (keys[i] != 0xffffffffu) {
+                    ckey[o] = keys[i];
+                    cpos[o++] = i;
+                }
+            __syncthreads();
+            block_radix_select<SPLIT_NT>(ckey, n_c, wc, ms->hist, ms->b, kth, n_less);
+            int eq_t = 0, sel_t = 0;
+            for (int u = threadIdx.x; u < n_c; u += SPLIT_NT) {
+                eq_t += ckey[u] == kth ? 1 : 0;
+                sel_t += ckey[u] <= kth ? 1 : 0;
+            }
+            int eq_tot;
+            (void)block_exclusive_scan<SPLIT_NT>(eq_t, ms->warp, eq_tot);
+            if (eq_tot == wc - n_less) {
+                // every row at the cutoff is selected: no position order needed
+                if (threadIdx.x == 0) {
+                    a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
+                    ms->base = atomicAdd(a.cnt_g + q, wc);
+                }
+                int tot;
+                const int pre = block_exclusive_scan<SPLIT_NT>(sel_t, ms->warp, tot);
+                int slot = ms->base + pre;
+                for (int u = threadIdx.x; u < n_c; u += SPLIT_NT)
+                    if (ckey[u] <= kth) {
+                        if (slot < a.capg) dst[slot] = ((unsigned long long)ckey[u] << 32) | jo | (uint32_t)cpos[u];
+                        ++slot;
+                    }
+                return;
+            }
+        }
+    }
+    // ties at the cutoff beyond what is selected (or too many rows in the
+    // running): the full selection in position order
     block_radix_select<SPLIT_NT>(keys, scan, wc, ms->hist, ms->b, kth, n_less);
     if (threadIdx.x == 0) {
         a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
@@ -1511,7 +1562,6 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
     // need_eq equal to it (the stable order of gpu_global.cu:321-390)
     const int need_eq = wc - n_less;
     int eq_base = 0, out = 0;
-    unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
     for (int r0 = 0; r0 < scan; r0 += SPLIT_NT) {
         const int i = r0 + threadIdx.x;
         const bool in = i < scan;
@@ -1523,7 +1573,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
         const int s_pre = block_exclusive_scan<SPLIT_NT>(sel ? 1 : 0, ms->warp, s_tot);
         if (sel) {
             const int slot = ms->base + out + s_pre;
-            if (slot < a.capg) dst[slot] = ((unsigned long long)key << 32) | ((uint32_t)j << 20) | (uint32_t)i;
+            if (slot < a.capg) dst[slot] = ((unsigned long long)key << 32) | jo | (uint32_t)i;
         }
         eq_base += eq_tot;
         out += s_tot;
@@ -1532,15 +1582,15 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
 
 // Phase-2 keys: a row whose running sum passes thr cannot pass the threshold
 // and gets the key 0xffffffff (never emitted).
-template <int M>
+template <int M, int NT>
 __device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int n, const float* lut, float thr,
                                                uint32_t* keys) {
-    for (int i = threadIdx.x; i < n; i += SPLIT_NT) keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, thr);
+    for (int i = threadIdx.x; i < n; i += NT) keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, thr);
     __syncthreads();
 }
 
-template <int M, int SD>
-__global__ void __launch_bounds__(SPLIT_NT, 4) split_p2_kernel(const ScanArgs a, int nq) {
+template <int M, int SD, int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) split_p2_kernel(const ScanArgs a, int nq) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
@@ -1564,25 +1614,25 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p2_kernel(const ScanArgs a,
         }
         ms->thr = (mn < FLT_MAX) ? mn * a.coeff : FLT_MAX;
     }
-    split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
+    split_lut<M, SD, NT>(a, a.queries + (size_t)q * a.dim, c, res, lut);
     const float thr = ms->thr;
     if constexpr (M % 16 == 0)
-        split_keys_thr<M>(a, start, len, lut, thr, keys);
+        split_keys_thr<M, NT>(a, start, len, lut, thr, keys);
     else
-        split_keys<M>(a, start, len, lut, keys);
+        split_keys<M, NT>(a, start, len, lut, keys);
     unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
     const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
     auto passes = [&](int i) { return keys[i] != 0xffffffffu && key2f(keys[i]) <= thr; };
     if (!a.ref_compat) {
         int n_t = 0;
-        for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
+        for (int i = tid; i < len; i += NT) n_t += passes(i) ? 1 : 0;
         int tot;
-        const int pre = block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, tot);
+        const int pre = block_exclusive_scan<NT>(n_t, ms->warp, tot);
         if (tot == 0) return;
         if (tid == 0) ms->base = atomicAdd(a.cnt_g + q, tot);
         __syncthreads();
         int slot = ms->base + pre;
-        for (int i = tid; i < len; i += SPLIT_NT)
+        for (int i = tid; i < len; i += NT)
             if (passes(i)) {
                 if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (uint32_t)i;
                 ++slot;
@@ -1592,55 +1642,57 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p2_kernel(const ScanArgs a,
     // ref_compat: the reference's 128 threads (thread t: rows t, t + 128, ...)
     // keep the first 128 passing vectors in list order in a shared buffer, and
     // past 128 each thread re-emits its own first (count - 128) passing ones
-    // (gpu_global.cu:466-526).  SPLIT_NT == 128, so thread t is the
-    // reference's thread t.
-    static_assert(SPLIT_NT == REF_BLOCK, "the overflow rule follows the reference's thread-to-row map");
-    int n_t = 0;
-    for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
-    int s_count;
-    (void)block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, s_count);
-    if (s_count == 0) return;
-    const int quota = s_count > REF_BLOCK ? s_count - REF_BLOCK : 0;
-    const int re_t = n_t < quota ? n_t : quota;
-    // regular emissions of this thread: rows whose list-order rank is < 128
-    int reg_t = 0;
-    {
-        int carry = 0;
-        for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
-            const int i = r0 + tid;
-            const int pf = (i < len && passes(i)) ? 1 : 0;
-            int tot;
-            const int pre = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot);
-            if (pf && carry + pre < REF_BLOCK) ++reg_t;
-            carry += tot;
-        }
-    }
-    int tot;
-    const int pre = block_exclusive_scan<SPLIT_NT>(reg_t + re_t, ms->warp, tot);
-    if (tid == 0) ms->base = atomicAdd(a.cnt_g + q, tot);
-    __syncthreads();
-    int slot = ms->base + pre;
-    {
-        int carry = 0;
-        for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
-            const int i = r0 + tid;
-            const int pf = (i < len && passes(i)) ? 1 : 0;
-            int tot2;
-            const int pre2 = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot2);
-            if (pf && carry + pre2 < REF_BLOCK) {
-                if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (uint32_t)i;
-                ++slot;
+    // (gpu_global.cu:466-526).  This instance has 128 threads, so thread t is
+    // the reference's thread t.
+    if constexpr (NT != REF_BLOCK) return;  // launched with NT == 128 under ref_compat
+    else {
+        int n_t = 0;
+        for (int i = tid; i < len; i += SPLIT_NT) n_t += passes(i) ? 1 : 0;
+        int s_count;
+        (void)block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, s_count);
+        if (s_count == 0) return;
+        const int quota = s_count > REF_BLOCK ? s_count - REF_BLOCK : 0;
+        const int re_t = n_t < quota ? n_t : quota;
+        // regular emissions of this thread: rows whose list-order rank is < 128
+        int reg_t = 0;
+        {
+            int carry = 0;
+            for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
+                const int i = r0 + tid;
+                const int pf = (i < len && passes(i)) ? 1 : 0;
+                int tot;
+                const int pre = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot);
+                if (pf && carry + pre < REF_BLOCK) ++reg_t;
+                carry += tot;
             }
-            carry += tot2;
         }
+        int tot;
+        const int pre = block_exclusive_scan<SPLIT_NT>(reg_t + re_t, ms->warp, tot);
+        if (tid == 0) ms->base = atomicAdd(a.cnt_g + q, tot);
+        __syncthreads();
+        int slot = ms->base + pre;
+        {
+            int carry = 0;
+            for (int r0 = 0; r0 < len && carry < REF_BLOCK; r0 += SPLIT_NT) {
+                const int i = r0 + tid;
+                const int pf = (i < len && passes(i)) ? 1 : 0;
+                int tot2;
+                const int pre2 = block_exclusive_scan<SPLIT_NT>(pf, ms->warp, tot2);
+                if (pf && carry + pre2 < REF_BLOCK) {
+                    if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (uint32_t)i;
+                    ++slot;
+                }
+                carry += tot2;
+            }
+        }
+        int left = re_t;
+        for (int i = tid; i < len && left > 0; i += SPLIT_NT)
+            if (passes(i)) {
+                if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (1u << 19) | (uint32_t)i;
+                ++slot;
+                --left;
+            }
     }
-    int left = re_t;
-    for (int i = tid; i < len && left > 0; i += SPLIT_NT)
-        if (passes(i)) {
-            if (slot < a.capg) dst[slot] = ((unsigned long long)keys[i] << 32) | jo | (1u << 19) | (uint32_t)i;
-            ++slot;
-            --left;
-        }
 }
 
 // k-th smallest high word (1-based) of n 64-bit keys in global memory; the
@@ -1771,10 +1823,13 @@ __global__ void __launch_bounds__(SEL_NT) split_select_kernel(const ScanArgs a, 
 
 using SplitKernel = void (*)(const ScanArgs, int);
 
-template <bool P2>
+// P2: 0 phase 1, 1 phase 2 in ref_compat (128 threads), 2 phase 2 otherwise
+template <int P2>
 static SplitKernel pick_split_kernel(int M, int SD) {
-#define FG_SPLIT_CASE(m, sd) \
-    if (M == m && SD == sd) return P2 ? split_p2_kernel<m, sd> : split_p1_kernel<m, sd>;
+#define FG_SPLIT_CASE(m, sd)                                                                        \
+    if (M == m && SD == sd)                                                                       \
+        return P2 == 2 ? split_p2_kernel<m, sd, SPLIT_P2_NT>                                      \
+                       : (P2 == 1 ? split_p2_kernel<m, sd, SPLIT_NT> : split_p1_kernel<m, sd>);
     FG_SPLIT_CASE(4, 4)  // small test indexes
     FG_SPLIT_CASE(16, 4)
     FG_SPLIT_CASE(16, 8)
@@ -1843,7 +1898,7 @@ static int split_capg(const fg_search_params* p) {
 static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
     if (!ix || !p || nq <= 0 || ix->pq_m <= 0 || ix->dim % ix->pq_m) return false;
     const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
-    if (!pick_split_kernel<false>(M, SD) || p->top_m > 4096 || ix->max_list_len >= (1 << 19)) return false;
+    if (!pick_split_kernel<0>(M, SD) || p->top_m > 4096 || ix->max_list_len >= (1 << 19)) return false;
     const char* force = getenv("FG_SCAN_KERNEL");
     const std::string mode = force ? force : "";
     if (mode == "split") return true;
@@ -1906,7 +1961,7 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     FG_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, (size_t)nq * 4, stream));
     const int dpad = (a.dim + 3) / 4 * 4;
     if (a.p1 > 0) {
-        SplitKernel k1 = pick_split_kernel<false>(M, SD);
+        SplitKernel k1 = pick_split_kernel<0>(M, SD);
         const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a.lmax) + (int)sizeof(SplitMisc);
         if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 1 needs %d bytes of shared memory", bytes);
         FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k1), bytes));
@@ -1917,11 +1972,12 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     if (a.top_m > a.p1) {
         ScanArgs a2 = a;
         a2.lmax = std::max(ix->max_list_len, 1);  // phase 2 has no 1024-row clamp
-        SplitKernel k2 = pick_split_kernel<true>(M, SD);
+        SplitKernel k2 = a.ref_compat ? pick_split_kernel<1>(M, SD) : pick_split_kernel<2>(M, SD);
+        const int nt2 = a.ref_compat ? SPLIT_NT : SPLIT_P2_NT;
         const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a2.lmax) + (int)sizeof(SplitMisc);
         if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 2 needs %d bytes of shared memory", bytes);
         FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k2), bytes));
-        k2<<<(unsigned)((long long)nq * (a.top_m - a.p1)), SPLIT_NT, bytes, stream>>>(a2, nq);
+        k2<<<(unsigned)((long long)nq * (a.top_m - a.p1)), nt2, bytes, stream>>>(a2, nq);
         int rc = check_launch("split_p2_kernel");
         if (rc) return rc;
     }
