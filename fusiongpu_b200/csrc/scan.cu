@@ -1439,22 +1439,20 @@ __device__ __forceinline__ void split_keys(const ScanArgs& a, int start, int n, 
     __syncthreads();
 }
 
-// ADC key of one row, or 0xffffffff once the running sum exceeds `bound`:
+// ADC key of one row (its codes in registers), or 0xffffffff once the running
+// sum exceeds `bound`:
 // every LUT entry is a sum of squares (>= 0), so under round-to-nearest the
 // running sum never decreases and such a row's full distance exceeds bound too.
 // Rows within the bound are summed to the end in subspace order, so their keys
 // are adc<M>'s bit for bit.
 template <int M>
-__device__ __forceinline__ uint32_t adc_bounded(const uint8_t* row, const float* lut, float bound) {
-    static_assert(M % 16 == 0, "16-code chunks");
-    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+__device__ __forceinline__ uint32_t adc_bounded_regs(const uint4 (&v)[M / 16], const float* lut, float bound) {
     float d = 0.0f;
     bool alive = true;
 #pragma unroll
     for (int w = 0; w < M / 16; ++w) {
         if (alive) {
-            const uint4 v = __ldg(r4 + w);
-            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t wd[4] = {v[w].x, v[w].y, v[w].z, v[w].w};
 #pragma unroll
             for (int b = 0; b < 16; ++b) {
                 const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
@@ -1464,6 +1462,35 @@ __device__ __forceinline__ uint32_t adc_bounded(const uint8_t* row, const float*
         }
     }
     return alive ? f2key(d) : 0xffffffffu;
+}
+
+template <int M>
+__device__ __forceinline__ void load_row(const uint8_t* row, uint4 (&v)[M / 16]) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+    for (int w = 0; w < M / 16; ++w) v[w] = __ldg(r4 + w);
+}
+
+// keys[i] for rows i = first, first + NT, ... < n of the list at `start`, each
+// bounded by `bound`; a row's codes are all loaded before its sum starts, and
+// the next row's while it runs.
+template <int M, int NT>
+__device__ __forceinline__ void keys_bounded(const ScanArgs& a, int start, int first, int n, const float* lut,
+                                             float bound, uint32_t* keys) {
+    static_assert(M % 16 == 0, "16-code chunks");
+    int i = first + threadIdx.x;
+    if (i >= n) return;
+    uint4 cur[M / 16], nxt[M / 16];
+    load_row<M>(a.codes + (size_t)(start + i) * M, cur);
+    for (; i < n; i += NT) {
+        const bool more = i + NT < n;
+        if (more) load_row<M>(a.codes + (size_t)(start + i + NT) * M, nxt);
+        keys[i] = adc_bounded_regs<M>(cur, lut, bound);
+        if (more) {
+#pragma unroll
+            for (int w = 0; w < M / 16; ++w) cur[w] = nxt[w];
+        }
+    }
 }
 
 template <int M, int SD>
@@ -1497,8 +1524,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
         split_keys<M>(a, start, head, lut, keys);
         if (scan > head && wc <= head) {
             block_radix_select<SPLIT_NT>(keys, head, wc, ms->hist, ms->b, kth, n_less);
-            for (int i = head + threadIdx.x; i < scan; i += SPLIT_NT)
-                keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, key2f(kth));
+            keys_bounded<M, SPLIT_NT>(a, start, head, scan, lut, key2f(kth), keys);
             __syncthreads();
         }
     } else {
@@ -1585,7 +1611,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
 template <int M, int NT>
 __device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int n, const float* lut, float thr,
                                                uint32_t* keys) {
-    for (int i = threadIdx.x; i < n; i += NT) keys[i] = adc_bounded<M>(a.codes + (size_t)(start + i) * M, lut, thr);
+    keys_bounded<M, NT>(a, start, 0, n, lut, thr, keys);
     __syncthreads();
 }
 
