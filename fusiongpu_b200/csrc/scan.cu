@@ -1390,26 +1390,6 @@ struct SplitMisc {
     float thr;
 };
 
-// k-th smallest of n keys in shared memory, selected by warp 0 (no block
-// barriers inside the selection; the few hundred keys of a phase-1 list do
-// not need the whole block) and handed to every thread.
-__device__ __forceinline__ void split_warp_select(const uint32_t* keys, int n, int k, SplitMisc* ms, uint32_t& kth,
-                                                  int& n_less) {
-    if (threadIdx.x < 32) {
-        uint32_t t;
-        int nl;
-        warp_radix_select(keys, n, k, ms->hist, t, nl);
-        if (threadIdx.x == 0) {
-            ms->b[0] = t;
-            ms->b[1] = (uint32_t)nl;
-        }
-    }
-    __syncthreads();
-    kth = ms->b[0];
-    n_less = (int)ms->b[1];
-    __syncthreads();
-}
-
 // The probed list of pair (q, j) after the prune, as start/len (len 0: skipped).
 __device__ __forceinline__ void split_probe(const ScanArgs& a, int q, int j, uint32_t& c, int& start, int& len) {
     const int P = a.top_m;
@@ -1543,7 +1523,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
         const int head = (scan < SPLIT_NT || wc > SPLIT_NT) ? scan : SPLIT_NT;
         split_keys<M>(a, start, head, lut, keys);
         if (scan > head && wc <= head) {
-            split_warp_select(keys, head, wc, ms, kth, n_less);
+            block_radix_select<SPLIT_NT>(keys, head, wc, ms->hist, ms->b, kth, n_less);
             keys_bounded<M, SPLIT_NT>(a, start, head, scan, lut, key2f(kth), keys);
             __syncthreads();
         }
@@ -1571,7 +1551,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
                     cpos[o++] = i;
                 }
             __syncthreads();
-            split_warp_select(ckey, n_c, wc, ms, kth, n_less);
+            block_radix_select<SPLIT_NT>(ckey, n_c, wc, ms->hist, ms->b, kth, n_less);
             int eq_t = 0, sel_t = 0;
             for (int u = threadIdx.x; u < n_c; u += SPLIT_NT) {
                 eq_t += ckey[u] == kth ? 1 : 0;
