@@ -262,22 +262,89 @@ size_t rows_topk_stage_bytes(long long rows, int ncols, int k) {
     return round_up((size_t)rows * nseg * k * 4, 256) * 2;
 }
 
+// The distance matrix with 128 x 128 tiles: 256 threads, each 8 X rows x 8 Y
+// rows, 16 dimensions per shared-memory chunk, so that one dimension step is
+// four 16-byte shared loads for 64 fmaf.  Every pair still accumulates
+// fmaf(.., .., acc) over the dimensions in increasing order, so the values
+// are those of l2_tile_kernel bit for bit.
+constexpr int MT_T = 128;
+constexpr int MT_DC = 16;
+constexpr int MT_LD = MT_T + 4;
+
+template <int METRIC>
+__global__ void __launch_bounds__(L2_NT) l2_matrix128_kernel(const float* __restrict__ X, long long nx,
+                                                             const float* __restrict__ Y, int ny, int dim,
+                                                             float* __restrict__ D, long long ldd) {
+    __shared__ __align__(16) float sX[MT_DC][MT_LD];
+    __shared__ __align__(16) float sY[MT_DC][MT_LD];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const long long x0 = (long long)blockIdx.y * MT_T;
+    const int y0 = blockIdx.x * MT_T;
+    float acc[8][8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+    for (int d0 = 0; d0 < dim; d0 += MT_DC) {
+        // 128 rows x 16 dimensions of each operand, transposed into shared memory
+#pragma unroll 4
+        for (int f = tid; f < MT_T * MT_DC; f += L2_NT) {
+            const int r = f / MT_DC, c = f % MT_DC;
+            const int dj = d0 + c;
+            const long long xr = x0 + r;
+            const int yr = y0 + r;
+            sX[c][r] = (xr < nx && dj < dim) ? __ldg(X + xr * dim + dj) : 0.0f;
+            sY[c][r] = (yr < ny && dj < dim) ? __ldg(Y + (long long)yr * dim + dj) : 0.0f;
+        }
+        __syncthreads();
+        const int dn = min(MT_DC, dim - d0);
+        for (int j = 0; j < dn; ++j) {
+            const float4 xa0 = *reinterpret_cast<const float4*>(&sX[j][tx * 8]);
+            const float4 xa1 = *reinterpret_cast<const float4*>(&sX[j][tx * 8 + 4]);
+            const float4 yb0 = *reinterpret_cast<const float4*>(&sY[j][ty * 8]);
+            const float4 yb1 = *reinterpret_cast<const float4*>(&sY[j][ty * 8 + 4]);
+            const float xa[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+            const float yb[8] = {yb0.x, yb0.y, yb0.z, yb0.w, yb1.x, yb1.y, yb1.z, yb1.w};
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    if (METRIC == FG_METRIC_IP) {
+                        acc[a][b] = fmaf(xa[a], yb[b], acc[a][b]);
+                    } else {
+                        const float df = xa[a] - yb[b];
+                        acc[a][b] = fmaf(df, df, acc[a][b]);
+                    }
+                }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        const long long xr = x0 + tx * 8 + a;
+        if (xr >= nx) continue;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const int yr = y0 + ty * 8 + b;
+            if (yr < ny) D[xr * ldd + yr] = (METRIC == FG_METRIC_IP) ? -acc[a][b] : acc[a][b];
+        }
+    }
+}
+
 int l2_matrix(const float* X, long long nx, const float* Y, int ny, int dim, float* D, long long ldd,
               cudaStream_t s, int metric = FG_METRIC_L2) {
     if (nx <= 0 || ny <= 0) return FG_OK;
-    const int nyt = (ny + L2_T - 1) / L2_T;
+    const int nyt = (ny + MT_T - 1) / MT_T;
     // at most 65535 X tiles per launch (grid.y)
-    const long long xrows = 65535ll * L2_T;
+    const long long xrows = 65535ll * MT_T;
     for (long long r0 = 0; r0 < nx; r0 += xrows) {
         const long long nr = std::min(xrows, nx - r0);
-        dim3 grid((unsigned)nyt, (unsigned)((nr + L2_T - 1) / L2_T));
+        dim3 grid((unsigned)nyt, (unsigned)((nr + MT_T - 1) / MT_T));
         if (metric == FG_METRIC_IP)
-            l2_tile_kernel<EPI_MATRIX, FG_METRIC_IP><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd,
-                                                                           ldd, nullptr, 1);
+            l2_matrix128_kernel<FG_METRIC_IP><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd, ldd);
         else
-            l2_tile_kernel<EPI_MATRIX><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd, ldd, nullptr,
-                                                             1);
-        const int rc = check_launch("l2_tile_kernel(matrix)");
+            l2_matrix128_kernel<FG_METRIC_L2><<<grid, L2_NT, 0, s>>>(X + r0 * dim, nr, Y, ny, dim, D + r0 * ldd, ldd);
+        const int rc = check_launch("l2_matrix128_kernel");
         if (rc) return rc;
     }
     return FG_OK;
