@@ -21,28 +21,19 @@ constexpr int L2_DC = 32;      // dimensions per shared-memory chunk
 constexpr int L2_LD = L2_T + 4;
 constexpr int L2_NT = 256;
 
-enum { EPI_MATRIX = 0, EPI_ARGMIN = 1 };
-
-// Each CTA owns 64 rows of X; blockIdx.y picks a run of `ytiles` 64-row tiles
-// of Y.  EPI_MATRIX writes D[x][y] (row stride ldd); EPI_ARGMIN keeps the
-// nearest y per x row (grid.y must be 1) and writes amin[x].  METRIC is
-// FG_METRIC_L2 or FG_METRIC_IP.
-template <int EPI, int METRIC = FG_METRIC_L2>
-__global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict__ X, long long nx,
-                                                        const float* __restrict__ Y, int ny, int dim,
-                                                        float* __restrict__ D, long long ldd,
-                                                        int32_t* __restrict__ amin, int ytiles) {
+// Nearest Y row of each X row: each CTA owns 64 rows of X and sweeps all of Y
+// in 64-row tiles (256 threads, 4 x 4 pairs each), keeping per thread the
+// smallest distance and, on ties, the lowest Y index; writes amin[x].
+__global__ void __launch_bounds__(L2_NT) l2_argmin_kernel(const float* __restrict__ X, long long nx,
+                                                          const float* __restrict__ Y, int ny, int dim,
+                                                          int32_t* __restrict__ amin) {
     __shared__ __align__(16) float sX[L2_DC][L2_LD];
     __shared__ __align__(16) float sY[L2_DC][L2_LD];
     __shared__ float rd[L2_T][17];
     __shared__ int ri[L2_T][17];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    // EPI_MATRIX: grid.x runs over Y tiles (up to 2^31 - 1), grid.y over X tiles;
-    // EPI_ARGMIN: grid.x runs over X tiles, every CTA sweeps all of Y
-    const long long x0 = (long long)(EPI == EPI_MATRIX ? blockIdx.y : blockIdx.x) * L2_T;
+    const long long x0 = (long long)blockIdx.x * L2_T;
     const int nyt = (ny + L2_T - 1) / L2_T;
-    const int yt0 = (EPI == EPI_MATRIX ? blockIdx.x : blockIdx.y) * ytiles;
-    const int yt1 = min(nyt, yt0 + ytiles);
     float best[4];
     int bidx[4];
 #pragma unroll
@@ -50,7 +41,7 @@ __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict_
         best[a] = FLT_MAX;
         bidx[a] = 0x7fffffff;
     }
-    for (int yt = yt0; yt < yt1; ++yt) {
+    for (int yt = 0; yt < nyt; ++yt) {
         const int y0 = yt * L2_T;
         float acc[4][4];
 #pragma unroll
@@ -78,67 +69,42 @@ __global__ void __launch_bounds__(L2_NT) l2_tile_kernel(const float* __restrict_
                 for (int a = 0; a < 4; ++a)
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
-                        if (METRIC == FG_METRIC_IP) {
-                            acc[a][b] = fmaf(xa[a], yb[b], acc[a][b]);
-                        } else {
-                            const float df = xa[a] - yb[b];
-                            acc[a][b] = fmaf(df, df, acc[a][b]);
-                        }
+                        const float df = xa[a] - yb[b];
+                        acc[a][b] = fmaf(df, df, acc[a][b]);
                     }
             }
             __syncthreads();
         }
-        if (METRIC == FG_METRIC_IP) {
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = -acc[a][b];
-        }
-        if (EPI == EPI_MATRIX) {
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                const long long xr = x0 + tx * 4 + a;
-                if (xr >= nx) continue;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int yr = y0 + ty * 4 + b;
-                    if (yr < ny) D[xr * ldd + yr] = acc[a][b];
+            for (int b = 0; b < 4; ++b) {
+                const int yr = y0 + ty * 4 + b;
+                if (yr < ny && acc[a][b] < best[a]) {
+                    best[a] = acc[a][b];
+                    bidx[a] = yr;
                 }
             }
-        } else {
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int yr = y0 + ty * 4 + b;
-                    if (yr < ny && acc[a][b] < best[a]) {
-                        best[a] = acc[a][b];
-                        bidx[a] = yr;
-                    }
-                }
-        }
     }
-    if (EPI == EPI_ARGMIN) {
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            rd[tx * 4 + a][ty] = best[a];
-            ri[tx * 4 + a][ty] = bidx[a];
-        }
-        __syncthreads();
-        if (tid < L2_T) {
-            float bd = rd[tid][0];
-            int bi = ri[tid][0];
-            for (int t = 1; t < 16; ++t) {
-                const float d = rd[tid][t];
-                const int i = ri[tid][t];
-                if (d < bd || (d == bd && i < bi)) {
-                    bd = d;
-                    bi = i;
-                }
+    for (int a = 0; a < 4; ++a) {
+        rd[tx * 4 + a][ty] = best[a];
+        ri[tx * 4 + a][ty] = bidx[a];
+    }
+    __syncthreads();
+    if (tid < L2_T) {
+        float bd = rd[tid][0];
+        int bi = ri[tid][0];
+        for (int t = 1; t < 16; ++t) {
+            const float d = rd[tid][t];
+            const int i = ri[tid][t];
+            if (d < bd || (d == bd && i < bi)) {
+                bd = d;
+                bi = i;
             }
-            const long long xr = x0 + tid;
-            if (xr < nx) amin[xr] = (bi == 0x7fffffff) ? 0 : bi;
         }
+        const long long xr = x0 + tid;
+        if (xr < nx) amin[xr] = (bi == 0x7fffffff) ? 0 : bi;
     }
 }
 
@@ -266,7 +232,7 @@ size_t rows_topk_stage_bytes(long long rows, int ncols, int k) {
 // rows, 16 dimensions per shared-memory chunk, so that one dimension step is
 // four 16-byte shared loads for 64 fmaf.  Every pair still accumulates
 // fmaf(.., .., acc) over the dimensions in increasing order, so the values
-// are those of l2_tile_kernel bit for bit.
+// are the oracle's sum_j fmaf(...) in dimension order bit for bit.
 constexpr int MT_T = 128;
 constexpr int MT_DC = 16;
 constexpr int MT_LD = MT_T + 4;
@@ -353,10 +319,9 @@ int l2_matrix(const float* X, long long nx, const float* Y, int ny, int dim, flo
 int l2_argmin(const float* X, long long nx, const float* Y, int ny, int dim, int32_t* amin,
               cudaStream_t s) {
     if (nx <= 0) return FG_OK;
-    const int nyt = (ny + L2_T - 1) / L2_T;
     dim3 grid((unsigned)((nx + L2_T - 1) / L2_T), 1);
-    l2_tile_kernel<EPI_ARGMIN><<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, nullptr, 0, amin, nyt);
-    return check_launch("l2_tile_kernel(argmin)");
+    l2_argmin_kernel<<<grid, L2_NT, 0, s>>>(X, nx, Y, ny, dim, amin);
+    return check_launch("l2_argmin_kernel");
 }
 
 // ---- coarse search and exact k-NN (row chunks through a workspace matrix) ----
