@@ -488,12 +488,13 @@ __device__ __forceinline__ void warp_dist(const T* __restrict__ data, long long 
         for (int h = 0; h < GS_CHUNKS; ++h) {
             const int c = c0 + h * 32 + lane;
             if (c >= nch) continue;
-            // the query chunk as float4 reads (16 bytes per lane: no bank conflicts)
+            // the query chunk, stored lane-interleaved (qv_index): the 32 lanes'
+            // float4 reads of one step are consecutive, so conflict-free
             float q[E];
-            const float4* q4 = reinterpret_cast<const float4*>(qv + c * E);
+            const float4* q4 = reinterpret_cast<const float4*>(qv) + (size_t)(c >> 5) * (E / 4) * 32 + lane;
 #pragma unroll
             for (int e4 = 0; e4 < E / 4; ++e4) {
-                const float4 t = q4[e4];
+                const float4 t = q4[e4 * 32];
                 q[4 * e4] = t.x;
                 q[4 * e4 + 1] = t.y;
                 q[4 * e4 + 2] = t.z;
@@ -524,6 +525,16 @@ __device__ __forceinline__ void warp_dist(const T* __restrict__ data, long long 
     }
 }
 
+// Position of query element j in shared memory: element e of the 16-byte
+// chunk c (E elements per chunk) goes to float4 ((c / 32) * E/4 + e / 4) * 32
+// + c % 32, lane (c % 32) of warp_dist's reads of that step.  The layout
+// spans round_up(dim, 256) floats at most.
+template <int E>
+__host__ __device__ __forceinline__ int qv_index(int j) {
+    const int c = j / E, e = j % E;
+    return (((c >> 5) * (E / 4) + e / 4) * 32 + (c & 31)) * 4 + (e & 3);
+}
+
 struct GsShared {
     int ntop;    // valid entries in the top list
     int hcount;  // occupied hash slots
@@ -550,7 +561,7 @@ __host__ __device__ inline GsLayout gs_layout(int dim, int itopk, int width, int
         return r;
     };
     const int WD = width * degree;
-    L.qv = take(dim * 4);
+    L.qv = take((dim + 255) / 256 * 256 * 4);
     L.hash = take(GS_HASH * 4);
     L.top = take(itopk * 8);
     L.top2 = take(itopk * 8);
@@ -592,9 +603,9 @@ __global__ void __launch_bounds__(GS_NT) graph_search_kernel(const GraphSearchAr
     const T* qsrc = static_cast<const T*>(a.queries) + (size_t)q * dim;
     for (int j = tid; j < dim; j += GS_NT) {
         if constexpr (sizeof(T) == 2)
-            qv[j] = __half2float(qsrc[j]);
+            qv[qv_index<Chunk<T>::E>(j)] = __half2float(qsrc[j]);
         else
-            qv[j] = qsrc[j];
+            qv[qv_index<Chunk<T>::E>(j)] = qsrc[j];
     }
     for (int j = tid; j < GS_HASH; j += GS_NT) hash[j] = GS_EMPTY;
     for (int j = tid; j < IT; j += GS_NT) {
