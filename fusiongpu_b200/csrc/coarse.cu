@@ -237,38 +237,59 @@ constexpr int MT_T = 128;
 constexpr int MT_DC = 16;
 constexpr int MT_LD = MT_T + 4;
 
+// 4-byte global -> shared copy that completes asynchronously; `bytes` 0 writes
+// a zero without reading (the source address is then not dereferenced).
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, int bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
 template <int METRIC>
 __global__ void __launch_bounds__(L2_NT) l2_matrix128_kernel(const float* __restrict__ X, long long nx,
                                                              const float* __restrict__ Y, int ny, int dim,
                                                              float* __restrict__ D, long long ldd) {
-    __shared__ __align__(16) float sX[MT_DC][MT_LD];
-    __shared__ __align__(16) float sY[MT_DC][MT_LD];
+    // two chunk buffers: the next 16 dimensions are copied in while this
+    // chunk's fmaf run
+    __shared__ __align__(16) float sX[2][MT_DC][MT_LD];
+    __shared__ __align__(16) float sY[2][MT_DC][MT_LD];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const long long x0 = (long long)blockIdx.y * MT_T;
     const int y0 = blockIdx.x * MT_T;
-    float acc[8][8];
-#pragma unroll
-    for (int a = 0; a < 8; ++a)
-#pragma unroll
-        for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
-    for (int d0 = 0; d0 < dim; d0 += MT_DC) {
-        // 128 rows x 16 dimensions of each operand, transposed into shared memory
+    // 128 rows x 16 dimensions of each operand, transposed into buffer b
+    auto stage = [&](int b, int d0) {
 #pragma unroll 4
         for (int f = tid; f < MT_T * MT_DC; f += L2_NT) {
             const int r = f / MT_DC, c = f % MT_DC;
             const int dj = d0 + c;
             const long long xr = x0 + r;
             const int yr = y0 + r;
-            sX[c][r] = (xr < nx && dj < dim) ? __ldg(X + xr * dim + dj) : 0.0f;
-            sY[c][r] = (yr < ny && dj < dim) ? __ldg(Y + (long long)yr * dim + dj) : 0.0f;
+            const bool xin = xr < nx && dj < dim, yin = yr < ny && dj < dim;
+            cp_async4(&sX[b][c][r], xin ? X + xr * dim + dj : X, xin ? 4 : 0);
+            cp_async4(&sY[b][c][r], yin ? Y + (long long)yr * dim + dj : Y, yin ? 4 : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+    stage(0, 0);
+    int buf = 0;
+    for (int d0 = 0; d0 < dim; d0 += MT_DC) {
+        if (d0 + MT_DC < dim) {
+            stage(buf ^ 1, d0 + MT_DC);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
         const int dn = min(MT_DC, dim - d0);
         for (int j = 0; j < dn; ++j) {
-            const float4 xa0 = *reinterpret_cast<const float4*>(&sX[j][tx * 8]);
-            const float4 xa1 = *reinterpret_cast<const float4*>(&sX[j][tx * 8 + 4]);
-            const float4 yb0 = *reinterpret_cast<const float4*>(&sY[j][ty * 8]);
-            const float4 yb1 = *reinterpret_cast<const float4*>(&sY[j][ty * 8 + 4]);
+            const float4 xa0 = *reinterpret_cast<const float4*>(&sX[buf][j][tx * 8]);
+            const float4 xa1 = *reinterpret_cast<const float4*>(&sX[buf][j][tx * 8 + 4]);
+            const float4 yb0 = *reinterpret_cast<const float4*>(&sY[buf][j][ty * 8]);
+            const float4 yb1 = *reinterpret_cast<const float4*>(&sY[buf][j][ty * 8 + 4]);
             const float xa[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
             const float yb[8] = {yb0.x, yb0.y, yb0.z, yb0.w, yb1.x, yb1.y, yb1.z, yb1.w};
 #pragma unroll
@@ -283,7 +304,8 @@ __global__ void __launch_bounds__(L2_NT) l2_matrix128_kernel(const float* __rest
                     }
                 }
         }
-        __syncthreads();
+        __syncthreads();  // buffer buf is refilled two chunks from now
+        buf ^= 1;
     }
 #pragma unroll
     for (int a = 0; a < 8; ++a) {

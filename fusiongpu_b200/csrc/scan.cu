@@ -1381,6 +1381,10 @@ constexpr int SEL_NT = 512;
 __host__ __device__ inline int split_keys_bytes(int lmax) { return ((lmax > 0 ? lmax : 1) * 4 + 15) / 16 * 16; }
 
 constexpr int SPLIT_P2_NT = 256;  // phase-2 CTAs outside ref_compat (more warps hide the code loads)
+#ifndef FG_SPLIT_P1_NT
+#define FG_SPLIT_P1_NT 256
+#endif
+constexpr int SPLIT_P1_NT = FG_SPLIT_P1_NT;  // phase-1 CTAs; also the rows that set its bound
 
 struct SplitMisc {
     uint32_t hist[256];
@@ -1493,8 +1497,8 @@ __device__ __forceinline__ void keys_bounded(const ScanArgs& a, int start, int f
     }
 }
 
-template <int M, int SD>
-__global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a, int nq) {
+template <int M, int SD, int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) split_p1_kernel(const ScanArgs a, int nq) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
@@ -1512,23 +1516,23 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
     }
     const int wc = len < a.limit_k ? len : a.limit_k;
     const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
-    split_lut<M, SD>(a, a.queries + (size_t)q * a.dim, c, res, lut);
+    split_lut<M, SD, NT>(a, a.queries + (size_t)q * a.dim, c, res, lut);
     uint32_t kth;
     int n_less;
     if constexpr (M % 16 == 0) {
-        // the first SPLIT_NT rows in full; their wc-th smallest distance bounds
+        // the first NT rows in full; their wc-th smallest distance bounds
         // the list's wc-th from above, so a later row whose partial sum passes
         // it cannot be among the wc selected, and it gets the largest key
         // (which changes neither the wc-th key nor the count below it)
-        const int head = (scan < SPLIT_NT || wc > SPLIT_NT) ? scan : SPLIT_NT;
-        split_keys<M>(a, start, head, lut, keys);
+        const int head = (scan < NT || wc > NT) ? scan : NT;
+        split_keys<M, NT>(a, start, head, lut, keys);
         if (scan > head && wc <= head) {
-            block_radix_select<SPLIT_NT>(keys, head, wc, ms->hist, ms->b, kth, n_less);
-            keys_bounded<M, SPLIT_NT>(a, start, head, scan, lut, key2f(kth), keys);
+            block_radix_select<NT>(keys, head, wc, ms->hist, ms->b, kth, n_less);
+            keys_bounded<M, NT>(a, start, head, scan, lut, key2f(kth), keys);
             __syncthreads();
         }
     } else {
-        split_keys<M>(a, start, scan, lut, keys);
+        split_keys<M, NT>(a, start, scan, lut, keys);
     }
     unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
     const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
@@ -1541,24 +1545,24 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
         uint32_t* ckey = reinterpret_cast<uint32_t*>(lut);
         int32_t* cpos = reinterpret_cast<int32_t*>(lut) + ccap;
         int n_t = 0;
-        for (int i = threadIdx.x; i < scan; i += SPLIT_NT) n_t += keys[i] != 0xffffffffu ? 1 : 0;
+        for (int i = threadIdx.x; i < scan; i += NT) n_t += keys[i] != 0xffffffffu ? 1 : 0;
         int n_c;
-        int o = block_exclusive_scan<SPLIT_NT>(n_t, ms->warp, n_c);
+        int o = block_exclusive_scan<NT>(n_t, ms->warp, n_c);
         if (n_c <= ccap) {
-            for (int i = threadIdx.x; i < scan; i += SPLIT_NT)
+            for (int i = threadIdx.x; i < scan; i += NT)
                 if (keys[i] != 0xffffffffu) {
                     ckey[o] = keys[i];
                     cpos[o++] = i;
                 }
             __syncthreads();
-            block_radix_select<SPLIT_NT>(ckey, n_c, wc, ms->hist, ms->b, kth, n_less);
+            block_radix_select<NT>(ckey, n_c, wc, ms->hist, ms->b, kth, n_less);
             int eq_t = 0, sel_t = 0;
-            for (int u = threadIdx.x; u < n_c; u += SPLIT_NT) {
+            for (int u = threadIdx.x; u < n_c; u += NT) {
                 eq_t += ckey[u] == kth ? 1 : 0;
                 sel_t += ckey[u] <= kth ? 1 : 0;
             }
             int eq_tot;
-            (void)block_exclusive_scan<SPLIT_NT>(eq_t, ms->warp, eq_tot);
+            (void)block_exclusive_scan<NT>(eq_t, ms->warp, eq_tot);
             if (eq_tot == wc - n_less) {
                 // every row at the cutoff is selected: no position order needed
                 if (threadIdx.x == 0) {
@@ -1566,9 +1570,9 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
                     ms->base = atomicAdd(a.cnt_g + q, wc);
                 }
                 int tot;
-                const int pre = block_exclusive_scan<SPLIT_NT>(sel_t, ms->warp, tot);
+                const int pre = block_exclusive_scan<NT>(sel_t, ms->warp, tot);
                 int slot = ms->base + pre;
-                for (int u = threadIdx.x; u < n_c; u += SPLIT_NT)
+                for (int u = threadIdx.x; u < n_c; u += NT)
                     if (ckey[u] <= kth) {
                         if (slot < a.capg) dst[slot] = ((unsigned long long)ckey[u] << 32) | jo | (uint32_t)cpos[u];
                         ++slot;
@@ -1579,7 +1583,7 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
     }
     // ties at the cutoff beyond what is selected (or too many rows in the
     // running): the full selection in position order
-    block_radix_select<SPLIT_NT>(keys, scan, wc, ms->hist, ms->b, kth, n_less);
+    block_radix_select<NT>(keys, scan, wc, ms->hist, ms->b, kth, n_less);
     if (threadIdx.x == 0) {
         a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
         ms->base = atomicAdd(a.cnt_g + q, wc);
@@ -1588,15 +1592,15 @@ __global__ void __launch_bounds__(SPLIT_NT, 4) split_p1_kernel(const ScanArgs a,
     // need_eq equal to it (the stable order of gpu_global.cu:321-390)
     const int need_eq = wc - n_less;
     int eq_base = 0, out = 0;
-    for (int r0 = 0; r0 < scan; r0 += SPLIT_NT) {
+    for (int r0 = 0; r0 < scan; r0 += NT) {
         const int i = r0 + threadIdx.x;
         const bool in = i < scan;
         const uint32_t key = in ? keys[i] : 0xffffffffu;
         const int is_eq = (in && key == kth) ? 1 : 0;
         int eq_tot, s_tot;
-        const int eq_pre = block_exclusive_scan<SPLIT_NT>(is_eq, ms->warp, eq_tot);
+        const int eq_pre = block_exclusive_scan<NT>(is_eq, ms->warp, eq_tot);
         const bool sel = in && (key < kth || (is_eq && eq_base + eq_pre < need_eq));
-        const int s_pre = block_exclusive_scan<SPLIT_NT>(sel ? 1 : 0, ms->warp, s_tot);
+        const int s_pre = block_exclusive_scan<NT>(sel ? 1 : 0, ms->warp, s_tot);
         if (sel) {
             const int slot = ms->base + out + s_pre;
             if (slot < a.capg) dst[slot] = ((unsigned long long)key << 32) | jo | (uint32_t)i;
@@ -1855,7 +1859,7 @@ static SplitKernel pick_split_kernel(int M, int SD) {
 #define FG_SPLIT_CASE(m, sd)                                                                        \
     if (M == m && SD == sd)                                                                       \
         return P2 == 2 ? split_p2_kernel<m, sd, SPLIT_P2_NT>                                      \
-                       : (P2 == 1 ? split_p2_kernel<m, sd, SPLIT_NT> : split_p1_kernel<m, sd>);
+                       : (P2 == 1 ? split_p2_kernel<m, sd, SPLIT_NT> : split_p1_kernel<m, sd, SPLIT_P1_NT>);
     FG_SPLIT_CASE(4, 4)  // small test indexes
     FG_SPLIT_CASE(16, 4)
     FG_SPLIT_CASE(16, 8)
@@ -1991,7 +1995,7 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
         const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a.lmax) + (int)sizeof(SplitMisc);
         if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 1 needs %d bytes of shared memory", bytes);
         FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k1), bytes));
-        k1<<<(unsigned)((long long)nq * a.p1), SPLIT_NT, bytes, stream>>>(a, nq);
+        k1<<<(unsigned)((long long)nq * a.p1), SPLIT_P1_NT, bytes, stream>>>(a, nq);
         int rc = check_launch("split_p1_kernel");
         if (rc) return rc;
     }
