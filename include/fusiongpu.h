@@ -147,7 +147,10 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
  * With it, long lists (mean length above 400) run the split path: one CTA
  * per (query, probed list) for phase 1 and for phase 2, candidates in a
  * per-query region of the workspace, then one selection CTA per query --
- * the same results as fg_batch_logic, bit for bit.  fg_search uses it. */
+ * the same results as fg_batch_logic, bit for bit.  fg_search uses it.  The
+ * region holds max(4096, 2 * rerank_m) 8-byte keys per query (10,000 queries,
+ * rerank_m 4096: 655 MB), so split very large batches; a query whose
+ * candidates overflow its region is recomputed by the per-query kernel. */
 int fg_batch_logic_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params, int32_t nq,
                                   size_t* bytes);
 int fg_batch_logic_ws(const fg_ivfpq_view* index, const float* queries, int32_t nq,
