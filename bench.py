@@ -322,7 +322,10 @@ def main():
                        "ms_per_step": op_rc["ms_per_step"], "sweep": sweep_rc},
         "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
-        "gpu_launches": sum(launches_per_step(s["nprobe"]) for s in sweep + sweep_rc) * args.steps,
+        # this library's kernels inside timed regions: the two device sweeps, the
+        # host-buffer sweep (E2E_CHUNKS searches per step), the scan-only timing
+        "gpu_launches": (sum(launches_per_step(s["nprobe"]) for s in sweep + sweep_rc)
+                         + E2E_CHUNKS * sum(launches_per_step(s["nprobe"]) for s in sweep) + 1) * args.steps,
         "gpu_launches_per_step": launches_per_step(op["nprobe"]),
         "roofline": roof,
         "clocks": clocks.summary(),
@@ -442,6 +445,7 @@ def main_sharded(args, rank, world, local, device, barrier, max_over_ranks):
         "sweep": sweep,
         "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * CONFIG["k"] * 8)},
+        # per search: the coarse stage (4 or 6), scan, rerank, pack, merge; device and e2e sweeps
         "gpu_launches": sum((4 if s_["nprobe"] <= 4 else 6) + 4 for s_ in sweep) * args.steps * 2,
         "clocks": clocks.summary(),
     }
@@ -1025,7 +1029,9 @@ def main_c3(args):
         "latency_ms_by_batch_cuda_graph": lat_graph,
         "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
-        "gpu_launches": 4 * args.steps,
+        # per search: coarse stage 6, split scan 4, rerank 1; the timed step, batch
+        # latencies (3 batch sizes, eager and graph), scan-only, e2e (2 pieces)
+        "gpu_launches": 11 * args.steps * (1 + 6 + 2) + 4 * args.steps,
         "roofline": {"kernel": "scan (" + os.environ.get("FG_SCAN_KERNEL", "auto") + ")", "bound": "hbm",
                      "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak,
@@ -1204,7 +1210,8 @@ def main_c5(args):
                        l2="flushed (256 MB write) between timed steps", quick=bool(args.quick)),
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
-        "gpu_launches": 4 * args.steps,
+        # per search: coarse stage 6, split scan 4, rerank 1 (+ pack and merge on N GPUs); device and e2e
+        "gpu_launches": (11 + (2 if world > 1 else 0)) * args.steps * 2,
         "clocks": clocks.summary(),
         "build_s": t_build,
         "parity": parity,
