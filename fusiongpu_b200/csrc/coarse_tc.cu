@@ -560,10 +560,12 @@ __global__ void __launch_bounds__(256) coarse_bound_kernel(const uint32_t* __res
     if ((threadIdx.x & 31) == 0) tq[q] = key2f(kth);
 }
 
+constexpr int FIN_SEGS = 256;  // segment lists per query the finish kernel indexes (more: exact fallback)
+
 struct FinishSmem {
     int dim4, spow;
     __host__ __device__ int per_warp_bytes() const {
-        return dim4 * 4 + 256 * 4 + FIN_TOT * 8 + spow * 8 * 2;
+        return dim4 * 4 + 256 * 4 + FIN_TOT * 4 + (FIN_SEGS + 4) * 4 + spow * 8 * 2;  // 16-byte multiples
     }
 };
 
@@ -585,15 +587,15 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
     float* sq = reinterpret_cast<float*>(mine);
     uint32_t* hist = reinterpret_cast<uint32_t*>(mine + L.dim4 * 4);
     uint32_t* wk = hist + 256;
-    int32_t* wi = reinterpret_cast<int32_t*>(wk + FIN_TOT);
-    unsigned long long* sx = reinterpret_cast<unsigned long long*>(wi + FIN_TOT);
+    int32_t* pre = reinterpret_cast<int32_t*>(wk + FIN_TOT);  // first gathered position of each segment
+    unsigned long long* sx = reinterpret_cast<unsigned long long*>(pre + FIN_SEGS + 4);
     unsigned long long* ex = sx + L.spow;
     for (int t = lane; t < dim; t += 32) sq[t] = queries[(size_t)q * dim + t];
 
-    // gather the segments
+    // gather the segments' keys; a key's id stays in its global segment list
     int total = 0;
-    bool over = false;
-    for (int y = 0; y < gy; ++y) {
+    bool over = gy > FIN_SEGS;
+    for (int y = 0; y < gy && !over; ++y) {
         const int c = cnt[(size_t)q * gy + y];
         over |= c > cap;
         const int take = min(c, cap);
@@ -601,20 +603,23 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
             over = true;
             break;
         }
+        if (lane == 0) pre[y] = total;
         const size_t seg = ((size_t)q * gy + y) * cap;
-        for (int i = lane; i < take; i += 32) {
-            wk[total + i] = list_k[seg + i];
-            wi[total + i] = list_i[seg + i];
-        }
+        for (int i = lane; i < take; i += 32) wk[total + i] = list_k[seg + i];
         total += take;
     }
+    if (lane == 0 && !over) pre[gy] = total;
     __syncwarp();
     bool certified = false;
     if (*err == 0 && !over && total >= S) {
         uint32_t kth;
         int n_less;
         warp_radix_select(wk, total, S, hist, kth, n_less);
-        warp_collect_smallest(wk, total, S, kth, n_less, sx, [&](int i) { return wi[i]; });
+        warp_collect_smallest(wk, total, S, kth, n_less, sx, [&](int i) {
+            int y = 0;
+            while (pre[y + 1] <= i) ++y;  // the segment holding gathered position i
+            return list_i[((size_t)q * gy + y) * cap + (i - pre[y])];
+        });
         for (int i = S + lane; i < L.spow; i += 32) sx[i] = ~0ull;
         __syncwarp();
         warp_bitonic_sort(sx, L.spow);  // by approximate key
