@@ -530,8 +530,10 @@ def roofline(idx, qd, nprobe, args, device, SearchParams, flush):
             traffic = tr["dram_bytes_per_launch"]
     except Exception:
         pass
-    # the library's scan dispatch: the team kernel on short lists (mean length <= 400), else one CTA per query
-    kernel = "ivfpq_team_kernel" if idx.total / max(idx.nlist, 1) <= 400 else "ivfpq_batch_kernel"
+    # the library's scan dispatch: the team kernel on short lists (typical length <= 400: the larger of the
+    # mean and half the longest list), else the split path
+    typical = max(idx.total / max(idx.nlist, 1), 0.5 * idx.max_list_len)
+    kernel = "ivfpq_team_kernel" if typical <= 400 else "split_p1_kernel + split_p2_kernel"
     return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
             "traffic": traffic, "algorithmic_bytes": alg, "ms_per_launch": ms, "nprobe": nprobe}

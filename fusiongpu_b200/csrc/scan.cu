@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(SCAN_NT) ivfpq_batch_kernel(const ScanArgs a) 
 // over subspaces in order.
 
 constexpr int TEAM_THREADS = 1024;  // threads of a team CTA: TEAM_THREADS / NT teams of NT
-constexpr double TEAM_OTF_MAX_LEN = 400.0;  // mean list length up to which the team kernel (on-the-fly terms) runs
+constexpr double TEAM_OTF_MAX_LEN = 400.0;  // typical list length up to which the team kernel (on-the-fly terms) runs
 
 template <int NT>
 struct TeamMisc {
@@ -1913,6 +1913,14 @@ static ScanKernel pick_scan_kernel(int M, int SD) {
 
 // ---- the split path's choice and workspace ---------------------------------------
 
+// Typical length of a probed list: the mean over all lists, or half the
+// longest (rebalancing caps lists at twice the mean), whichever is larger.  A
+// shard of a list-sharded index keeps every list slot but owns only some
+// lists, so its mean over all slots understates the lists it scans.
+static double typical_list_len(const fg_ivfpq_view* ix) {
+    return std::max((double)ix->total / std::max(ix->nlist, 1), 0.5 * ix->max_list_len);
+}
+
 static int split_rsel(const fg_search_params* p) {
     return p->ref_compat ? (p->rerank_m < REF_BLOCK ? p->rerank_m : REF_BLOCK) : p->rerank_m;
 }
@@ -1923,7 +1931,7 @@ static int split_capg(const fg_search_params* p) {
 }
 
 // Whether the split path runs for this index, parameters and batch: long
-// lists (mean length above the team kernel's limit) and a supported shape,
+// lists (typical length above the team kernel's limit) and a supported shape,
 // unless FG_SCAN_KERNEL names another kernel (FG_SCAN_KERNEL=split forces it).
 static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
     if (!ix || !p || nq <= 0 || ix->pq_m <= 0 || ix->dim % ix->pq_m) return false;
@@ -1933,7 +1941,7 @@ static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int
     const std::string mode = force ? force : "";
     if (mode == "split") return true;
     if (!mode.empty()) return false;
-    return (double)ix->total / std::max(ix->nlist, 1) > TEAM_OTF_MAX_LEN;
+    return typical_list_len(ix) > TEAM_OTF_MAX_LEN;
 }
 
 struct SplitWs {
@@ -2111,7 +2119,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     // and FG_SCAN_TEAM_NT=64|128|256 override the choice (for tests and measurements).
     const char* force = getenv("FG_SCAN_KERNEL");
     const std::string mode = force ? force : "";
-    const double avg_len = (double)ix->total / ix->nlist;
+    const double avg_len = typical_list_len(ix);
     // measured: on long lists (C3: 680, C5: 1000 vectors per list at nprobe 64)
     // the per-query CTA kernel is faster than any team configuration
     if (mode != "block" && (!mode.empty() || avg_len <= TEAM_OTF_MAX_LEN)) {
