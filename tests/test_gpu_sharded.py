@@ -217,3 +217,35 @@ def test_graph_two_gpus_nccl_matches_oracle():
             f = np.load(os.path.join(d, f"rank{r}.npz"))
             np.testing.assert_array_equal(f["dists"], ed)
             np.testing.assert_array_equal(f["ids"], ei)
+
+
+def test_shard_of_long_lists_keeps_the_split_path():
+    """A shard owns a quarter of the lists but keeps every list slot, so the
+    mean over all slots understates its lists; the scan dispatch still sees
+    long lists (typical length = max(mean, longest / 2)) and runs the split
+    path, with the oracle's per-shard results."""
+    import ctypes as C
+    from fusiongpu_b200 import _lib
+    from fusiongpu_b200.index import SearchParams
+    from fusiongpu_b200.sharded import ShardedIndex
+    base, q = ds.generate(ds.scaled(ds.C1, 24000, 64, n_centres=16, seed=44))
+    index, _ = oracle.build_index(base, 16, 32, kmeans_iters=4, pq_sample=6000, pq_iters=4, rebalance_lists=False)
+    lens = np.diff(index["offsets"])
+    assert lens.mean() > 400
+    p = SearchParams(**dict(P, top_m=8, p1_lists=2))
+    shards = [ShardedIndex(index, base, r, 4) for r in range(4)]
+    for sh in shards:
+        local = sh.local
+        assert local.total / local.nlist <= 400 < local.max_list_len / 2
+        need = _lib.size_query("fg_batch_logic_workspace_size", C.byref(local.view), C.byref(p.c()), q.shape[0])
+        assert need > 0
+    qd = torch.from_numpy(q).cuda()
+    ds_, is_ = [], []
+    for sh in shards:
+        gi, d = sh.local_search(qd, p)
+        ds_.append(d.cpu().numpy())
+        is_.append(gi.cpu().numpy())
+    oi, od = _merge_gpu(np.stack(ds_), np.stack(is_), P["final_k"])
+    ei, ed = shard_ref.oracle_sharded_search(index, base, q, 4, **dict(P, top_m=8, p1_lists=2))
+    np.testing.assert_array_equal(od, ed)
+    np.testing.assert_array_equal(oi, ei)
