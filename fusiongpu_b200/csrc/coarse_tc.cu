@@ -625,18 +625,21 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
         warp_bitonic_sort(sx, L.spow);  // by approximate key
         const float E = approx_err(qn[q], __uint_as_float(*max_cn_bits));
         const float thr = rescore_limit(key2f((uint32_t)(sx[P - 1] >> 32)), E);
-        // rescore exactly the sorted prefix within thr
+        // rescore exactly the sorted prefix within thr.  Every lane runs every
+        // round (spow is below 32 when nlist is), so the ballot sees the whole warp.
         int r = 0;
-        for (int i = lane; i < L.spow; i += 32) {
-            const unsigned long long e = sx[i];
+        for (int i0 = 0; i0 < L.spow; i0 += 32) {
+            const int i = i0 + lane;
+            const bool in = i < L.spow;
+            const unsigned long long e = in ? sx[i] : ~0ull;
             unsigned long long key = ~0ull;
-            const bool take = i < S && key2f((uint32_t)(e >> 32)) <= thr;
+            const bool take = in && i < S && key2f((uint32_t)(e >> 32)) <= thr;
             if (take) {
                 const uint32_t cid = (uint32_t)(e & 0xffffffffu);
                 key = ((unsigned long long)f2key(l2_seq_dev(sq, centroids + (size_t)cid * dim, dim)) << 32) | cid;
             }
             r += __popc(__ballot_sync(0xffffffffu, take));
-            ex[i] = key;
+            if (in) ex[i] = key;
         }
         __syncwarp();
         warp_bitonic_sort(ex, next_pow2(r > P ? r : P));

@@ -146,6 +146,20 @@ def test_coarse_tc_odd_shapes(fg):
         np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
 
 
+@pytest.mark.parametrize("nlist", [5, 16, 31])
+def test_coarse_tc_fewer_lists_than_a_warp(fg, nlist):
+    """nlist below 32: the exactly rescored superset (every list) is shorter
+    than a warp, so the finish kernel's rescoring round has idle lanes."""
+    rng = np.random.default_rng(nlist)
+    cen = rng.normal(size=(nlist, 128)).astype(np.float32)
+    q = rng.normal(size=(70, 128)).astype(np.float32)
+    for top_m in sorted({1, 2, 4, min(8, nlist), nlist}):
+        ids, d, nfb = fg.coarse_search(q, cen, top_m, path="tc")
+        eids, ed = oracle.coarse(cen, q, top_m)
+        np.testing.assert_array_equal(_np(d), ed)
+        np.testing.assert_array_equal(_np(ids).astype(np.uint32), eids)
+
+
 def test_coarse_tc_ranges_cross_query_tiles(fg):
     """40 query tiles x 8 centroid tiles = 320 (query tile, centroid tile)
     pairs over at most 148 CTAs: ranges of 3 pairs start and end inside query
