@@ -62,6 +62,9 @@ struct ScanArgs {
     int32_t* flags;       // split select: 1 where the query falls back to the per-query kernel
     const int32_t* only;  // per-query kernel: run only the queries flagged here (null: all)
     int capg;
+    int* work;            // split: [0] phase-1 pairs, [1] phase-2 pairs, [2], [3] their work counters
+    int4* pairs1;         // split: the (query, probe) pairs with a non-empty list of each phase,
+    int4* pairs2;         //        as (q * top_m + j, list, start, length)
 };
 
 struct ScanMisc {
@@ -1353,12 +1356,16 @@ using TeamKernel = void (*)(const ScanArgs, int, int, int);
 // For long lists (hundreds of vectors per list, tens of probes per query) the
 // per-query kernel serialises a query's probes inside one CTA, with block
 // barriers around every LUT, selection and emission round.  The split path
-// gives every (query, probed list) pair its own CTA of SPLIT_NT threads:
+// gives every (query, probed list) pair a CTA of its own for its turn:
 //
-//   split_p1_kernel   phase 1 (the first p1 probes): LUT, ADC of the list,
+//   split_pairs_kernel  lists the pairs whose list is non-empty (a shard of a
+//                     list-sharded index owns only some of each query's
+//                     probes); persistent CTAs of the two phase kernels take
+//                     them from work counters;
+//   split_p1_pair     phase 1 (the first p1 probes): LUT, ADC of the list,
 //                     the limit_k smallest by (distance, position), the cutoff
 //                     (gpu_global.cu:79-166, 212-253, 321-390);
-//   split_p2_kernel   phase 2 (the other probes): threshold from the query's
+//   split_p2_pair     phase 2 (the other probes): threshold from the query's
 //                     phase-1 cutoffs (gpu_global.cu:394-426), LUT, ADC, the
 //                     passing vectors with the reference's 128-slot buffer and
 //                     overflow re-emission in ref_compat mode (:428-527);
@@ -1387,6 +1394,7 @@ constexpr int SPLIT_P2_NT = 256;  // phase-2 CTAs outside ref_compat (more warps
 constexpr int SPLIT_P1_NT = FG_SPLIT_P1_NT;  // phase-1 CTAs; also the rows that set its bound
 
 struct SplitMisc {
+    int4 rec;  // persistent phase kernels: the pair taken next
     uint32_t hist[256];
     int warp[SPLIT_P2_NT / 32];
     uint32_t b[2];
@@ -1498,18 +1506,11 @@ __device__ __forceinline__ void keys_bounded(const ScanArgs& a, int start, int f
 }
 
 template <int M, int SD, int NT>
-__global__ void __launch_bounds__(NT, 1024 / NT) split_p1_kernel(const ScanArgs a, int nq) {
-    extern __shared__ __align__(16) unsigned char smem[];
+__device__ void split_p1_pair(const ScanArgs& a, int q, int j, uint32_t c, int start, int len, unsigned char* smem) {
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
     uint32_t* keys = reinterpret_cast<uint32_t*>(res + (a.dim + 3) / 4 * 4);
     SplitMisc* ms = reinterpret_cast<SplitMisc*>(reinterpret_cast<unsigned char*>(keys) + split_keys_bytes(a.lmax));
-    const int pair = blockIdx.x;
-    const int q = pair / a.p1, j = pair - (pair / a.p1) * a.p1;
-    if (q >= nq) return;
-    uint32_t c;
-    int start, len;
-    split_probe(a, q, j, c, start, len);
     if (len <= 0) {
         if (threadIdx.x == 0) a.cut_g[(size_t)q * a.p1 + j] = 0.0f;
         return;
@@ -1620,19 +1621,11 @@ __device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int
 }
 
 template <int M, int SD, int NT>
-__global__ void __launch_bounds__(NT, 1024 / NT) split_p2_kernel(const ScanArgs a, int nq) {
-    extern __shared__ __align__(16) unsigned char smem[];
+__device__ void split_p2_pair(const ScanArgs& a, int q, int j, uint32_t c, int start, int len, unsigned char* smem) {
     float* lut = reinterpret_cast<float*>(smem);
     float* res = lut + M * 256;
     uint32_t* keys = reinterpret_cast<uint32_t*>(res + (a.dim + 3) / 4 * 4);
     SplitMisc* ms = reinterpret_cast<SplitMisc*>(reinterpret_cast<unsigned char*>(keys) + split_keys_bytes(a.lmax));
-    const int np2 = a.top_m - a.p1;
-    const int pair = blockIdx.x;
-    const int q = pair / np2, j = a.p1 + (pair - (pair / np2) * np2);
-    if (q >= nq) return;
-    uint32_t c;
-    int start, len;
-    split_probe(a, q, j, c, start, len);
     if (len <= 0) return;
     const int tid = threadIdx.x;
     if (tid == 0) {
@@ -1722,6 +1715,79 @@ __global__ void __launch_bounds__(NT, 1024 / NT) split_p2_kernel(const ScanArgs 
                 ++slot;
                 --left;
             }
+    }
+}
+
+// The (query, probe) pairs whose list is non-empty after the prune, listed
+// for the two phases (warp-aggregated appends, so a warp's pairs stay
+// together); an empty phase-1 probe gets its cutoff 0 here.  A shard of a
+// list-sharded index owns only some of each query's probes: the phase
+// kernels then run on its pairs alone.
+__global__ void __launch_bounds__(256) split_pairs_kernel(const ScanArgs a, int nq) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool in = t < (long long)nq * a.top_m;
+    const int q = in ? (int)(t / a.top_m) : 0, j = in ? (int)(t % a.top_m) : 0;
+    int len = 0, start = 0;
+    uint32_t c = 0;
+    if (in) {
+        split_probe(a, q, j, c, start, len);
+        if (len <= 0 && j < a.p1) a.cut_g[(size_t)q * a.p1 + j] = 0.0f;
+    }
+    const bool v1 = in && len > 0 && j < a.p1, v2 = in && len > 0 && j >= a.p1;
+    const unsigned m1 = __ballot_sync(0xffffffffu, v1), m2 = __ballot_sync(0xffffffffu, v2);
+    const int lane = threadIdx.x & 31;
+    int b1 = 0, b2 = 0;
+    if (lane == 0) {
+        if (m1) b1 = atomicAdd(a.work + 0, __popc(m1));
+        if (m2) b2 = atomicAdd(a.work + 1, __popc(m2));
+    }
+    b1 = __shfl_sync(0xffffffffu, b1, 0);
+    b2 = __shfl_sync(0xffffffffu, b2, 0);
+    const unsigned lt = lanemask_lt();
+    const int4 rec = make_int4(q * a.top_m + j, (int)c, start, len);
+    if (v1) a.pairs1[b1 + __popc(m1 & lt)] = rec;
+    if (v2) a.pairs2[b2 + __popc(m2 & lt)] = rec;
+}
+
+// Persistent CTAs taking the pairs of one phase from a work counter.  Thread
+// 0 keeps the next pair's index, claimed one pair ahead, and loads its record
+// while the current pair runs, so neither the atomic nor the load waits.
+template <int M, int SD, int NT, bool P2>
+__global__ void __launch_bounds__(NT, 1024 / NT) split_phase_kernel(const ScanArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    SplitMisc* ms = reinterpret_cast<SplitMisc*>(smem + (size_t)M * 256 * 4 + (size_t)(a.dim + 3) / 4 * 16 +
+                                                 split_keys_bytes(a.lmax));
+    int* ctr = a.work + (P2 ? 3 : 2);
+    const int4* recs = P2 ? a.pairs2 : a.pairs1;
+    const int count = a.work[P2 ? 1 : 0];
+    const int4 none = make_int4(-1, 0, 0, 0);
+    int nidx = 0;
+    if (threadIdx.x == 0) {
+        const int i0 = atomicAdd(ctr, 1);
+        nidx = atomicAdd(ctr, 1);
+        ms->rec = i0 < count ? recs[i0] : none;
+    }
+    __syncthreads();
+    for (;;) {
+        const int4 r = ms->rec;
+        if (r.x < 0) break;
+        int4 nrec = none;
+        int nnidx = 0;
+        if (threadIdx.x == 0) {
+            if (nidx < count) nrec = recs[nidx];
+            nnidx = atomicAdd(ctr, 1);
+        }
+        const int q = r.x / a.top_m, j = r.x - q * a.top_m;
+        if constexpr (P2)
+            split_p2_pair<M, SD, NT>(a, q, j, (uint32_t)r.y, r.z, r.w, smem);
+        else
+            split_p1_pair<M, SD, NT>(a, q, j, (uint32_t)r.y, r.z, r.w, smem);
+        __syncthreads();  // every thread has read this pair's record and shared state
+        if (threadIdx.x == 0) {
+            ms->rec = nrec;
+            nidx = nnidx;
+        }
+        __syncthreads();
     }
 }
 
@@ -1851,15 +1917,16 @@ __global__ void __launch_bounds__(SEL_NT) split_select_kernel(const ScanArgs a, 
     }
 }
 
-using SplitKernel = void (*)(const ScanArgs, int);
+using SplitKernel = void (*)(const ScanArgs);
 
 // P2: 0 phase 1, 1 phase 2 in ref_compat (128 threads), 2 phase 2 otherwise
 template <int P2>
 static SplitKernel pick_split_kernel(int M, int SD) {
 #define FG_SPLIT_CASE(m, sd)                                                                        \
     if (M == m && SD == sd)                                                                       \
-        return P2 == 2 ? split_p2_kernel<m, sd, SPLIT_P2_NT>                                      \
-                       : (P2 == 1 ? split_p2_kernel<m, sd, SPLIT_NT> : split_p1_kernel<m, sd, SPLIT_P1_NT>);
+        return P2 == 2 ? split_phase_kernel<m, sd, SPLIT_P2_NT, true>                             \
+                       : (P2 == 1 ? split_phase_kernel<m, sd, SPLIT_NT, true>                     \
+                                  : split_phase_kernel<m, sd, SPLIT_P1_NT, false>);
     FG_SPLIT_CASE(4, 4)  // small test indexes
     FG_SPLIT_CASE(16, 4)
     FG_SPLIT_CASE(16, 8)
@@ -1936,7 +2003,9 @@ static int split_capg(const fg_search_params* p) {
 static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
     if (!ix || !p || nq <= 0 || ix->pq_m <= 0 || ix->dim % ix->pq_m) return false;
     const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
-    if (!pick_split_kernel<0>(M, SD) || p->top_m > 4096 || ix->max_list_len >= (1 << 19)) return false;
+    if (!pick_split_kernel<0>(M, SD) || p->top_m > 4096 || ix->max_list_len >= (1 << 19) ||
+        (long long)nq * p->top_m >= (1LL << 31))
+        return false;
     const char* force = getenv("FG_SCAN_KERNEL");
     const std::string mode = force ? force : "";
     if (mode == "split") return true;
@@ -1946,8 +2015,10 @@ static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int
 
 struct SplitWs {
     float* cut;
+    int* work;  // pair counts and work counters, then the per-query candidate counts
     int32_t* cnt;
     int32_t* flags;
+    int4* pairs;
     unsigned long long* cand;
 };
 
@@ -1959,19 +2030,33 @@ static size_t split_carve(void* ws, int nq, const fg_search_params* p, SplitWs* 
         o += (bytes + 255) / 256 * 256;
         return r;
     };
-    const size_t oc = take((size_t)nq * p1 * 4), on = take((size_t)nq * 4), of = take((size_t)nq * 4),
+    const size_t oc = take((size_t)nq * p1 * 4), ow = take(16), on = take((size_t)nq * 4),
+                 of = take((size_t)nq * 4), op = take((size_t)nq * std::max(p->top_m, p1) * 16),
                  oa = take((size_t)nq * split_capg(p) * 8);
     if (out) {
         char* b = static_cast<char*>(ws);
         out->cut = reinterpret_cast<float*>(b + oc);
+        out->work = reinterpret_cast<int*>(b + ow);
         out->cnt = reinterpret_cast<int32_t*>(b + on);
         out->flags = reinterpret_cast<int32_t*>(b + of);
+        out->pairs = reinterpret_cast<int4*>(b + op);
         out->cand = reinterpret_cast<unsigned long long*>(b + oa);
     }
     return o;
 }
 
-// Launches the split path: zero the counts, phase 1, phase 2, per-query
+// Persistent grid of a split phase kernel: its resident CTAs on every SM, at
+// most one per pair.
+static int split_grid(SplitKernel k, int nt, int bytes, long long pairs, int* grid) {
+    int occ = 0;
+    FG_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void*>(k), nt, bytes));
+    const long long nsm = std::max(1, device_attr(cudaDevAttrMultiProcessorCount));
+    *grid = (int)std::max(1LL, std::min(pairs, nsm * std::max(occ, 1)));
+    return FG_OK;
+}
+
+// Launches the split path: zero the counters, list the non-empty (query,
+// probe) pairs, phase 1 and phase 2 over them (persistent CTAs), per-query
 // selection, then the per-query kernel for the queries the selection flagged
 // (its CTAs for the others return at once).
 static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* ws, cudaStream_t stream,
@@ -1989,6 +2074,9 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     a.flags = w.flags;
     a.cand_g = w.cand;
     a.capg = split_capg(&pp);
+    a.work = w.work;
+    a.pairs1 = w.pairs;
+    a.pairs2 = w.pairs + (size_t)nq * a.p1;
     // the fallback kernel's shared memory must fit, as on the per-query path
     ScanKernel k = pick_scan_kernel(M, SD);
     a.cap = a.rsel + SCAN_NT;
@@ -1996,15 +2084,26 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     if (!k || L.total > smem_max)
         return fail(FG_ERR_UNSUPPORTED, "scan needs %d bytes of shared memory (max %d): rerank_m=%d "
                     "max_list_len=%d", L.total, smem_max, a.rerank_m, a.lmax);
-    FG_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, (size_t)nq * 4, stream));
+    // the counters and the counts are adjacent: one memset
+    FG_CUDA_TRY(cudaMemsetAsync(w.work, 0, reinterpret_cast<char*>(w.cnt + nq) - reinterpret_cast<char*>(w.work),
+                                stream));
+    {
+        const long long n = (long long)nq * a.top_m;
+        split_pairs_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(a, nq);
+        int rc = check_launch("split_pairs_kernel");
+        if (rc) return rc;
+    }
     const int dpad = (a.dim + 3) / 4 * 4;
     if (a.p1 > 0) {
         SplitKernel k1 = pick_split_kernel<0>(M, SD);
         const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a.lmax) + (int)sizeof(SplitMisc);
         if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 1 needs %d bytes of shared memory", bytes);
         FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k1), bytes));
-        k1<<<(unsigned)((long long)nq * a.p1), SPLIT_P1_NT, bytes, stream>>>(a, nq);
-        int rc = check_launch("split_p1_kernel");
+        int grid = 1;
+        int rc = split_grid(k1, SPLIT_P1_NT, bytes, (long long)nq * a.p1, &grid);
+        if (rc) return rc;
+        k1<<<grid, SPLIT_P1_NT, bytes, stream>>>(a);
+        rc = check_launch("split_phase_kernel (phase 1)");
         if (rc) return rc;
     }
     if (a.top_m > a.p1) {
@@ -2015,8 +2114,11 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
         const int bytes = M * 256 * 4 + dpad * 4 + split_keys_bytes(a2.lmax) + (int)sizeof(SplitMisc);
         if (bytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split phase 2 needs %d bytes of shared memory", bytes);
         FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k2), bytes));
-        k2<<<(unsigned)((long long)nq * (a.top_m - a.p1)), nt2, bytes, stream>>>(a2, nq);
-        int rc = check_launch("split_p2_kernel");
+        int grid = 1;
+        int rc = split_grid(k2, nt2, bytes, (long long)nq * (a.top_m - a.p1), &grid);
+        if (rc) return rc;
+        k2<<<grid, nt2, bytes, stream>>>(a2);
+        rc = check_launch("split_phase_kernel (phase 2)");
         if (rc) return rc;
     }
     const int sort_cap = next_pow2(std::max(256, 2 * a.rsel));
