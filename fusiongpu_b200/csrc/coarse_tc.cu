@@ -560,12 +560,15 @@ __global__ void __launch_bounds__(256) coarse_bound_kernel(const uint32_t* __res
     if ((threadIdx.x & 31) == 0) tq[q] = key2f(kth);
 }
 
-constexpr int FIN_SEGS = 256;  // segment lists per query the finish kernel indexes (more: exact fallback)
-
+// Per-warp shared memory of the finish kernel: the query, a histogram, the
+// gathered keys, the first gathered position of each of the query's segment
+// lists (segs of them: 4 per CTA whose range touches the query's tile, so a
+// small batch spread over every SM has several hundred), the superset.
 struct FinishSmem {
-    int dim4, spow;
+    int dim4, spow, segs;
+    __host__ __device__ int seg_words() const { return (segs + 3) / 4 * 4 + 4; }
     __host__ __device__ int per_warp_bytes() const {
-        return dim4 * 4 + 256 * 4 + FIN_TOT * 4 + (FIN_SEGS + 4) * 4 + spow * 8 * 2;  // 16-byte multiples
+        return dim4 * 4 + 256 * 4 + FIN_TOT * 4 + seg_words() * 4 + spow * 8 * 2;  // 16-byte multiples
     }
 };
 
@@ -582,19 +585,19 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * FIN_WARPS + w;
     if (q >= nq) return;
-    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(S > P ? S : P)};
+    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(S > P ? S : P), gy};
     unsigned char* mine = smem + (size_t)w * L.per_warp_bytes();
     float* sq = reinterpret_cast<float*>(mine);
     uint32_t* hist = reinterpret_cast<uint32_t*>(mine + L.dim4 * 4);
     uint32_t* wk = hist + 256;
     int32_t* pre = reinterpret_cast<int32_t*>(wk + FIN_TOT);  // first gathered position of each segment
-    unsigned long long* sx = reinterpret_cast<unsigned long long*>(pre + FIN_SEGS + 4);
+    unsigned long long* sx = reinterpret_cast<unsigned long long*>(pre + L.seg_words());
     unsigned long long* ex = sx + L.spow;
     for (int t = lane; t < dim; t += 32) sq[t] = queries[(size_t)q * dim + t];
 
     // gather the segments' keys; a key's id stays in its global segment list
     int total = 0;
-    bool over = gy > FIN_SEGS;
+    bool over = false;
     for (int y = 0; y < gy && !over; ++y) {
         const int c = cnt[(size_t)q * gy + y];
         over |= c > cap;
@@ -616,8 +619,13 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_finish_kernel(
         int n_less;
         warp_radix_select(wk, total, S, hist, kth, n_less);
         warp_collect_smallest(wk, total, S, kth, n_less, sx, [&](int i) {
-            int y = 0;
-            while (pre[y + 1] <= i) ++y;  // the segment holding gathered position i
+            // the segment holding gathered position i: the last y with pre[y] <= i
+            // (empty segments share their successor's start)
+            int y = 0, hi = gy - 1;
+            while (y < hi) {
+                const int mid = (y + hi + 1) >> 1;
+                if (pre[mid] <= i) y = mid; else hi = mid - 1;
+            }
             return list_i[((size_t)q * gy + y) * cap + (i - pre[y])];
         });
         for (int i = S + lane; i < L.spow; i += 32) sx[i] = ~0ull;
@@ -686,7 +694,7 @@ __global__ void __launch_bounds__(FIN_WARPS * 32) coarse_topk_finish_kernel(
     if (q >= nq) return;
     const int ncand = nlists * topt;
     const int cpow = next_pow2(ncand);
-    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(P)};
+    const FinishSmem L{(dim + 3) / 4 * 4, next_pow2(P), 0};
     // per warp: query, histogram (fallback select), candidate keys [cpow]
     unsigned char* mine = smem + (size_t)w * ((size_t)L.dim4 * 4 + 256 * 4 + (size_t)cpow * 8);
     float* sq = reinterpret_cast<float*>(mine);
@@ -999,7 +1007,7 @@ int coarse_tc(const float* centroids, int nlist, int dim, const float* queries, 
     if ((rc = check_launch("coarse_gemm_kernel(filter)"))) return rc;
 
     // pass 2: select, rescore exactly, certify (or fall back)
-    const FinishSmem FL{(dim + 3) / 4 * 4, next_pow2(std::max(c.S, P))};
+    const FinishSmem FL{(dim + 3) / 4 * 4, next_pow2(std::max(c.S, P)), c.nlists};
     const int fin_smem = FIN_WARPS * FL.per_warp_bytes();
     FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&coarse_finish_kernel), fin_smem));
     coarse_finish_kernel<<<c.fin_cta, FIN_WARPS * 32, fin_smem, s>>>(centroids, nlist, dim, queries, (int)nq, cnt,
