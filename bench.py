@@ -533,7 +533,7 @@ def roofline(idx, qd, nprobe, args, device, SearchParams, flush):
     # the library's scan dispatch: the team kernel on short lists (typical length <= 400: the larger of the
     # mean and half the longest list), else the split path
     typical = max(idx.total / max(idx.nlist, 1), 0.5 * idx.max_list_len)
-    kernel = "ivfpq_team_kernel" if typical <= 400 else "split_p1_kernel + split_p2_kernel"
+    kernel = "ivfpq_team_kernel" if typical <= 400 else "split_phase_kernel (phase 1 + phase 2)"
     return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
             "traffic": traffic, "algorithmic_bytes": alg, "ms_per_launch": ms, "nprobe": nprobe}
@@ -1031,9 +1031,10 @@ def main_c3(args):
         "latency_ms_by_batch_cuda_graph": lat_graph,
         "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
-        # per search: coarse stage 6, split scan 4, rerank 1; the timed step, batch
-        # latencies (3 batch sizes, eager and graph), scan-only, e2e (2 pieces)
-        "gpu_launches": 11 * args.steps * (1 + 6 + 2) + 4 * args.steps,
+        # per search: coarse stage 6, split scan 5 (pairs, two phases, select, fallback),
+        # rerank 1; the timed step, batch latencies (3 batch sizes, eager and graph),
+        # scan-only, e2e (2 pieces)
+        "gpu_launches": 12 * args.steps * (1 + 6 + 2) + 5 * args.steps,
         "roofline": {"kernel": "scan (" + os.environ.get("FG_SCAN_KERNEL", "auto") + ")", "bound": "hbm",
                      "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak,
@@ -1212,8 +1213,9 @@ def main_c5(args):
                        l2="flushed (256 MB write) between timed steps", quick=bool(args.quick)),
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(queries.nbytes),
                 "d2h_bytes_per_step": int(nq * cfg["k"] * 8)},
-        # per search: coarse stage 6, split scan 4, rerank 1 (+ pack and merge on N GPUs); device and e2e
-        "gpu_launches": (11 + (2 if world > 1 else 0)) * args.steps * 2,
+        # per search: coarse stage 6, split scan 5 (pairs, two phases, select, fallback), rerank 1
+        # (+ pack and merge on N GPUs); device and e2e
+        "gpu_launches": (12 + (2 if world > 1 else 0)) * args.steps * 2,
         "clocks": clocks.summary(),
         "build_s": t_build,
         "parity": parity,
