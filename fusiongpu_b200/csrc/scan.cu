@@ -1451,57 +1451,56 @@ __device__ __forceinline__ void split_keys(const ScanArgs& a, int start, int n, 
     __syncthreads();
 }
 
-// ADC key of one row (its codes in registers), or 0xffffffff once the running
-// sum exceeds `bound`:
+// ADC key of one row, or 0xffffffff once the running sum exceeds `bound`:
 // every LUT entry is a sum of squares (>= 0), so under round-to-nearest the
 // running sum never decreases and such a row's full distance exceeds bound too.
 // Rows within the bound are summed to the end in subspace order, so their keys
-// are adc<M>'s bit for bit.
+// are adc<M>'s bit for bit.  `first` holds the row's first 16 codes; a later
+// 16-code word is loaded only while the row is alive, and issued halfway
+// through the word before it (a row dead after 8 terms is dead after 16), so
+// the rows rejected in their first word -- nearly all of them past a tight
+// bound -- cost one 16-byte load instead of M bytes.
 template <int M>
-__device__ __forceinline__ uint32_t adc_bounded_regs(const uint4 (&v)[M / 16], const float* lut, float bound) {
+__device__ __forceinline__ uint32_t adc_bounded_lazy(uint4 first, const uint8_t* row, const float* lut,
+                                                     float bound) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
     float d = 0.0f;
     bool alive = true;
+    uint4 v = first, next = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int w = 0; w < M / 16; ++w) {
         if (alive) {
-            const uint32_t wd[4] = {v[w].x, v[w].y, v[w].z, v[w].w};
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int b = 0; b < 16; ++b) {
                 const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
                 d = __fadd_rn(d, lut[(16 * w + b) * 256 + code]);
+                if (b == 7 && w + 1 < M / 16 && d <= bound) next = __ldg(r4 + w + 1);
             }
             alive = d <= bound;
+            v = next;
         }
     }
     return alive ? f2key(d) : 0xffffffffu;
 }
 
-template <int M>
-__device__ __forceinline__ void load_row(const uint8_t* row, uint4 (&v)[M / 16]) {
-    const uint4* r4 = reinterpret_cast<const uint4*>(row);
-#pragma unroll
-    for (int w = 0; w < M / 16; ++w) v[w] = __ldg(r4 + w);
-}
-
 // keys[i] for rows i = first, first + NT, ... < n of the list at `start`, each
-// bounded by `bound`; a row's codes are all loaded before its sum starts, and
-// the next row's while it runs.
+// bounded by `bound`; the next row's first 16 codes are loaded while a row's
+// sum runs.
 template <int M, int NT>
 __device__ __forceinline__ void keys_bounded(const ScanArgs& a, int start, int first, int n, const float* lut,
                                              float bound, uint32_t* keys) {
     static_assert(M % 16 == 0, "16-code chunks");
     int i = first + threadIdx.x;
     if (i >= n) return;
-    uint4 cur[M / 16], nxt[M / 16];
-    load_row<M>(a.codes + (size_t)(start + i) * M, cur);
+    const uint8_t* rows = a.codes + (size_t)start * M;
+    uint4 cur = __ldg(reinterpret_cast<const uint4*>(rows + (size_t)i * M));
     for (; i < n; i += NT) {
         const bool more = i + NT < n;
-        if (more) load_row<M>(a.codes + (size_t)(start + i + NT) * M, nxt);
-        keys[i] = adc_bounded_regs<M>(cur, lut, bound);
-        if (more) {
-#pragma unroll
-            for (int w = 0; w < M / 16; ++w) cur[w] = nxt[w];
-        }
+        uint4 nxt = cur;
+        if (more) nxt = __ldg(reinterpret_cast<const uint4*>(rows + (size_t)(i + NT) * M));
+        keys[i] = adc_bounded_lazy<M>(cur, rows + (size_t)i * M, lut, bound);
+        cur = nxt;
     }
 }
 
