@@ -1418,8 +1418,9 @@ __device__ __forceinline__ void split_probe(const ScanArgs& a, int q, int j, uin
     len = a.offsets[c + 1] - start;
 }
 
-// LUT of (query, list c) in shared memory: the entries of build_lut.
-template <int M, int SD, int NT = SPLIT_NT>
+// LUT of (query, list c) in shared memory: the entries of build_lut, for the
+// first MB subspaces (all M by default); the residual covers every dimension.
+template <int M, int SD, int NT = SPLIT_NT, int MB = M>
 __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, uint32_t c, float* res, float* lut) {
     const float* cv = a.centroids + (size_t)c * a.dim;
     for (int t = threadIdx.x; t < a.dim; t += NT) res[t] = qv[t] - cv[t];
@@ -1427,7 +1428,7 @@ __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, ui
     if constexpr (SD == 2) {
         // two codewords per thread: one 16-byte codebook load, one 8-byte store
 #pragma unroll 4
-        for (int e2 = threadIdx.x; e2 < M * 128; e2 += NT) {
+        for (int e2 = threadIdx.x; e2 < MB * 128; e2 += NT) {
             const int m = e2 >> 7;
             const float4 cb = __ldg(reinterpret_cast<const float4*>(a.codebook) + e2);
             const float2 r = *reinterpret_cast<const float2*>(res + m * 2);
@@ -1436,7 +1437,7 @@ __device__ __forceinline__ void split_lut(const ScanArgs& a, const float* qv, ui
         }
     } else {
 #pragma unroll 4
-        for (int e = threadIdx.x; e < M * 256; e += NT) {
+        for (int e = threadIdx.x; e < MB * 256; e += NT) {
             const int m = e >> 8;
             lut[e] = sub_dist<SD>(res + m * SD, a.codebook + (size_t)e * SD);
         }
@@ -1502,6 +1503,85 @@ __device__ __forceinline__ void keys_bounded(const ScanArgs& a, int start, int f
         keys[i] = adc_bounded_lazy<M>(cur, rows + (size_t)i * M, lut, bound);
         cur = nxt;
     }
+}
+
+// Terms 16w .. 16w + 15 of a row computed from the codebook instead of a LUT:
+// the LUT entry's expression (sd_arith on the same residual and codeword), so
+// the same floats, added in subspace order.  The codewords of TB terms are
+// loaded before they are summed.
+template <int SD>
+__device__ __forceinline__ float otf_word(uint4 v, int w, const float* res, const float* cb, float d) {
+    constexpr int TB = SD <= 2 ? 16 : (SD <= 4 ? 4 : 2);
+    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int b0 = 0; b0 < 16; b0 += TB) {
+        float cv[TB][SD];
+#pragma unroll
+        for (int k = 0; k < TB; ++k) {
+            const int b = b0 + k;
+            const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
+            load_sub<SD, true>(cb + ((size_t)(16 * w + b) * 256 + code) * SD, cv[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < TB; ++k) {
+            float rv[SD];
+            load_sub<SD, false>(res + (16 * w + b0 + k) * SD, rv);
+            d = __fadd_rn(d, sd_arith<SD>(rv, cv[k]));
+        }
+    }
+    return d;
+}
+
+// adc_bounded_lazy with a LUT of the first 16 subspaces only: past a tight
+// bound nearly every row is rejected within its first 16 terms, so the other
+// subspaces' LUT entries would mostly go unread; a row still alive after them
+// finishes from the codebook (otf_word).  Bit for bit adc<M>'s key for rows
+// within the bound.
+template <int M, int SD>
+__device__ __forceinline__ uint32_t adc_bounded_prefix(uint4 first, const uint8_t* row, const float* lut,
+                                                       const float* res, const float* cb, float bound) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    float d = 0.0f;
+    uint4 next = make_uint4(0u, 0u, 0u, 0u);
+    {
+        const uint32_t wd[4] = {first.x, first.y, first.z, first.w};
+#pragma unroll
+        for (int b = 0; b < 16; ++b) {
+            const uint32_t code = (wd[b >> 2] >> (8 * (b & 3))) & 0xffu;
+            d = __fadd_rn(d, lut[b * 256 + code]);
+            if (b == 7 && M / 16 > 1 && d <= bound) next = __ldg(r4 + 1);
+        }
+    }
+    bool alive = d <= bound;
+#pragma unroll 1
+    for (int w = 1; w < M / 16; ++w) {
+        if (!alive) break;
+        const uint4 v = next;
+        if (w + 1 < M / 16) next = __ldg(r4 + w + 1);
+        d = otf_word<SD>(v, w, res, cb, d);
+        alive = d <= bound;
+    }
+    return alive ? f2key(d) : 0xffffffffu;
+}
+
+// keys_bounded over a LUT of the first 16 subspaces (adc_bounded_prefix).
+template <int M, int SD, int NT>
+__device__ __forceinline__ void keys_bounded_prefix(const ScanArgs& a, int start, int n, const float* lut,
+                                                    const float* res, float bound, uint32_t* keys) {
+    static_assert(M % 16 == 0, "16-code chunks");
+    int i = threadIdx.x;
+    if (i < n) {
+        const uint8_t* rows = a.codes + (size_t)start * M;
+        uint4 cur = __ldg(reinterpret_cast<const uint4*>(rows + (size_t)i * M));
+        for (; i < n; i += NT) {
+            const bool more = i + NT < n;
+            uint4 nxt = cur;
+            if (more) nxt = __ldg(reinterpret_cast<const uint4*>(rows + (size_t)(i + NT) * M));
+            keys[i] = adc_bounded_prefix<M, SD>(cur, rows + (size_t)i * M, lut, res, a.codebook, bound);
+            cur = nxt;
+        }
+    }
+    __syncthreads();
 }
 
 template <int M, int SD, int NT>
@@ -1610,15 +1690,6 @@ __device__ void split_p1_pair(const ScanArgs& a, int q, int j, uint32_t c, int s
     }
 }
 
-// Phase-2 keys: a row whose running sum passes thr cannot pass the threshold
-// and gets the key 0xffffffff (never emitted).
-template <int M, int NT>
-__device__ __forceinline__ void split_keys_thr(const ScanArgs& a, int start, int n, const float* lut, float thr,
-                                               uint32_t* keys) {
-    keys_bounded<M, NT>(a, start, 0, n, lut, thr, keys);
-    __syncthreads();
-}
-
 template <int M, int SD, int NT>
 __device__ void split_p2_pair(const ScanArgs& a, int q, int j, uint32_t c, int start, int len, unsigned char* smem) {
     float* lut = reinterpret_cast<float*>(smem);
@@ -1636,10 +1707,14 @@ __device__ void split_p2_pair(const ScanArgs& a, int q, int j, uint32_t c, int s
         }
         ms->thr = (mn < FLT_MAX) ? mn * a.coeff : FLT_MAX;
     }
-    split_lut<M, SD, NT>(a, a.queries + (size_t)q * a.dim, c, res, lut);
+    const float* qv = a.queries + (size_t)q * a.dim;
+    if constexpr (M % 16 == 0)
+        split_lut<M, SD, NT, 16>(a, qv, c, res, lut);  // the first 16 subspaces
+    else
+        split_lut<M, SD, NT>(a, qv, c, res, lut);
     const float thr = ms->thr;
     if constexpr (M % 16 == 0)
-        split_keys_thr<M, NT>(a, start, len, lut, thr, keys);
+        keys_bounded_prefix<M, SD, NT>(a, start, len, lut, res, thr, keys);
     else
         split_keys<M, NT>(a, start, len, lut, keys);
     unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
