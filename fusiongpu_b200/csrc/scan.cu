@@ -64,7 +64,8 @@ struct ScanArgs {
     int capg;
     int* work;            // split: [0] phase-1 pairs, [1] phase-2 pairs, [2], [3] their work counters
     int4* pairs1;         // split: the (query, probe) pairs with a non-empty list of each phase,
-    int4* pairs2;         //        as (q * top_m + j, list, start, length)
+    int4* pairs2;         //        as (q * top_m + j, list, start, length), grouped by list
+    int* hist;            // split: per-list pair counts, then offsets: phase 1 [nlist + 1], phase 2 [nlist + 1]
 };
 
 struct ScanMisc {
@@ -1358,10 +1359,10 @@ using TeamKernel = void (*)(const ScanArgs, int, int, int);
 // barriers around every LUT, selection and emission round.  The split path
 // gives every (query, probed list) pair a CTA of its own for its turn:
 //
-//   split_pairs_kernel  lists the pairs whose list is non-empty (a shard of a
+//   split_pairs_*     list the pairs whose list is non-empty (a shard of a
 //                     list-sharded index owns only some of each query's
-//                     probes); persistent CTAs of the two phase kernels take
-//                     them from work counters;
+//                     probes), grouped by list; persistent CTAs of the two
+//                     phase kernels take them from work counters;
 //   split_p1_pair     phase 1 (the first p1 probes): LUT, ADC of the list,
 //                     the limit_k smallest by (distance, position), the cutoff
 //                     (gpu_global.cu:79-166, 212-253, 321-390);
@@ -1792,35 +1793,58 @@ __device__ void split_p2_pair(const ScanArgs& a, int q, int j, uint32_t c, int s
     }
 }
 
-// The (query, probe) pairs whose list is non-empty after the prune, listed
-// for the two phases (warp-aggregated appends, so a warp's pairs stay
-// together); an empty phase-1 probe gets its cutoff 0 here.  A shard of a
-// list-sharded index owns only some of each query's probes: the phase
-// kernels then run on its pairs alone.
-__global__ void __launch_bounds__(256) split_pairs_kernel(const ScanArgs a, int nq) {
+// The (query, probe) pairs whose list is non-empty after the prune, as
+// records grouped by list (a counting sort: count, scan, scatter), so that the
+// ~nq * top_m / nlist queries probing one list run back to back and its codes
+// are read from DRAM about once per batch instead of once per query.  An empty
+// phase-1 probe gets its cutoff 0 here.  A shard of a list-sharded index owns
+// only some of each query's probes: the phase kernels run on its pairs alone.
+// The order inside a list does not matter: candidates are ranked by (distance,
+// probe, position) whatever the order they arrive in.
+__global__ void __launch_bounds__(256) split_pairs_count_kernel(const ScanArgs a, int nq) {
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const bool in = t < (long long)nq * a.top_m;
-    const int q = in ? (int)(t / a.top_m) : 0, j = in ? (int)(t % a.top_m) : 0;
-    int len = 0, start = 0;
-    uint32_t c = 0;
-    if (in) {
-        split_probe(a, q, j, c, start, len);
-        if (len <= 0 && j < a.p1) a.cut_g[(size_t)q * a.p1 + j] = 0.0f;
+    if (t >= (long long)nq * a.top_m) return;
+    const int q = (int)(t / a.top_m), j = (int)(t % a.top_m);
+    uint32_t c;
+    int start, len;
+    split_probe(a, q, j, c, start, len);
+    if (len <= 0) {
+        if (j < a.p1) a.cut_g[(size_t)q * a.p1 + j] = 0.0f;
+        return;
     }
-    const bool v1 = in && len > 0 && j < a.p1, v2 = in && len > 0 && j >= a.p1;
-    const unsigned m1 = __ballot_sync(0xffffffffu, v1), m2 = __ballot_sync(0xffffffffu, v2);
-    const int lane = threadIdx.x & 31;
-    int b1 = 0, b2 = 0;
-    if (lane == 0) {
-        if (m1) b1 = atomicAdd(a.work + 0, __popc(m1));
-        if (m2) b2 = atomicAdd(a.work + 1, __popc(m2));
+    atomicAdd(a.hist + (j < a.p1 ? 0 : a.nlist + 1) + c, 1);
+}
+
+// Exclusive scan of one phase's per-list counts (CTA 0: phase 1, CTA 1:
+// phase 2) in place; the phase's pair count goes to work[phase].
+__global__ void __launch_bounds__(1024) split_pairs_scan_kernel(const ScanArgs a) {
+    __shared__ int warp[32];
+    int* h = a.hist + (size_t)blockIdx.x * (a.nlist + 1);
+    const int n = a.nlist, per = (n + 1023) / 1024;
+    const int b = min(n, (int)threadIdx.x * per), e = min(n, b + per);
+    int sum = 0;
+    for (int i = b; i < e; ++i) sum += h[i];
+    int tot;
+    int pre = block_exclusive_scan<1024>(sum, warp, tot);
+    for (int i = b; i < e; ++i) {
+        const int v = h[i];
+        h[i] = pre;
+        pre += v;
     }
-    b1 = __shfl_sync(0xffffffffu, b1, 0);
-    b2 = __shfl_sync(0xffffffffu, b2, 0);
-    const unsigned lt = lanemask_lt();
-    const int4 rec = make_int4(q * a.top_m + j, (int)c, start, len);
-    if (v1) a.pairs1[b1 + __popc(m1 & lt)] = rec;
-    if (v2) a.pairs2[b2 + __popc(m2 & lt)] = rec;
+    if (threadIdx.x == 0) a.work[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(256) split_pairs_scatter_kernel(const ScanArgs a, int nq) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)nq * a.top_m) return;
+    const int q = (int)(t / a.top_m), j = (int)(t % a.top_m);
+    uint32_t c;
+    int start, len;
+    split_probe(a, q, j, c, start, len);
+    if (len <= 0) return;
+    const bool p2 = j >= a.p1;
+    const int pos = atomicAdd(a.hist + (p2 ? a.nlist + 1 : 0) + c, 1);
+    (p2 ? a.pairs2 : a.pairs1)[pos] = make_int4(q * a.top_m + j, (int)c, start, len);
 }
 
 // Persistent CTAs taking the pairs of one phase from a work counter.  Thread
@@ -2089,14 +2113,15 @@ static bool split_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int
 
 struct SplitWs {
     float* cut;
-    int* work;  // pair counts and work counters, then the per-query candidate counts
+    int* work;  // pair counts and work counters, then the per-list pair counts, then the per-query candidate counts
+    int* hist;
     int32_t* cnt;
     int32_t* flags;
     int4* pairs;
     unsigned long long* cand;
 };
 
-static size_t split_carve(void* ws, int nq, const fg_search_params* p, SplitWs* out) {
+static size_t split_carve(void* ws, int nq, int nlist, const fg_search_params* p, SplitWs* out) {
     const int p1 = std::max(1, std::min(p->top_m, p->p1_lists));
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -2104,13 +2129,15 @@ static size_t split_carve(void* ws, int nq, const fg_search_params* p, SplitWs* 
         o += (bytes + 255) / 256 * 256;
         return r;
     };
-    const size_t oc = take((size_t)nq * p1 * 4), ow = take(16), on = take((size_t)nq * 4),
+    const size_t oc = take((size_t)nq * p1 * 4), ow = take(16), oh = take((size_t)2 * (nlist + 1) * 4),
+                 on = take((size_t)nq * 4),
                  of = take((size_t)nq * 4), op = take((size_t)nq * std::max(p->top_m, p1) * 16),
                  oa = take((size_t)nq * split_capg(p) * 8);
     if (out) {
         char* b = static_cast<char*>(ws);
         out->cut = reinterpret_cast<float*>(b + oc);
         out->work = reinterpret_cast<int*>(b + ow);
+        out->hist = reinterpret_cast<int*>(b + oh);
         out->cnt = reinterpret_cast<int32_t*>(b + on);
         out->flags = reinterpret_cast<int32_t*>(b + of);
         out->pairs = reinterpret_cast<int4*>(b + op);
@@ -2142,13 +2169,14 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     pp.rerank_m = a.rerank_m;
     pp.ref_compat = a.ref_compat;
     SplitWs w;
-    split_carve(ws, nq, &pp, &w);
+    split_carve(ws, nq, ix->nlist, &pp, &w);
     a.cut_g = w.cut;
     a.cnt_g = w.cnt;
     a.flags = w.flags;
     a.cand_g = w.cand;
     a.capg = split_capg(&pp);
     a.work = w.work;
+    a.hist = w.hist;
     a.pairs1 = w.pairs;
     a.pairs2 = w.pairs + (size_t)nq * a.p1;
     // the fallback kernel's shared memory must fit, as on the per-query path
@@ -2158,14 +2186,19 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     if (!k || L.total > smem_max)
         return fail(FG_ERR_UNSUPPORTED, "scan needs %d bytes of shared memory (max %d): rerank_m=%d "
                     "max_list_len=%d", L.total, smem_max, a.rerank_m, a.lmax);
-    // the counters and the counts are adjacent: one memset
+    // the counters, the per-list counts and the per-query counts are adjacent: one memset
     FG_CUDA_TRY(cudaMemsetAsync(w.work, 0, reinterpret_cast<char*>(w.cnt + nq) - reinterpret_cast<char*>(w.work),
                                 stream));
     {
         const long long n = (long long)nq * a.top_m;
-        split_pairs_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(a, nq);
-        int rc = check_launch("split_pairs_kernel");
+        const unsigned blocks = (unsigned)((n + 255) / 256);
+        split_pairs_count_kernel<<<blocks, 256, 0, stream>>>(a, nq);
+        int rc = check_launch("split_pairs_count_kernel");
         if (rc) return rc;
+        split_pairs_scan_kernel<<<2, 1024, 0, stream>>>(a);
+        if ((rc = check_launch("split_pairs_scan_kernel"))) return rc;
+        split_pairs_scatter_kernel<<<blocks, 256, 0, stream>>>(a, nq);
+        if ((rc = check_launch("split_pairs_scatter_kernel"))) return rc;
     }
     const int dpad = (a.dim + 3) / 4 * 4;
     if (a.p1 > 0) {
@@ -2210,7 +2243,7 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
 
 size_t batch_logic_workspace(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
     if (!split_chosen(ix, p, nq)) return 0;
-    return split_carve(nullptr, nq, p, nullptr) + 256;
+    return split_carve(nullptr, nq, ix->nlist, p, nullptr) + 256;
 }
 
 int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uint32_t* probe_ids,
@@ -2285,7 +2318,7 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     if (smem_max <= 0 || smem_sm <= 0) return fail(FG_ERR_CUDA, "cannot read the device's shared-memory limits");
 
     if (split_chosen(ix, p, nq)) {
-        const size_t need = split_carve(nullptr, nq, p, nullptr);
+        const size_t need = split_carve(nullptr, nq, ix->nlist, p, nullptr);
         if (ws && ws_bytes >= need) return batch_logic_split(a, ix, nq, ws, stream, smem_max);
         if (getenv("FG_SCAN_KERNEL") && std::string(getenv("FG_SCAN_KERNEL")) == "split")
             return fail(FG_ERR_WORKSPACE, "FG_SCAN_KERNEL=split needs %zu workspace bytes", need);

@@ -145,10 +145,11 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
 /* The same with a caller workspace of at least fg_batch_logic_workspace_size
  * bytes (256-byte aligned; 0 bytes, and any pointer, when the size is 0).
  * With it, long lists (typical length above 400: the larger of the mean
- * over all lists and half the longest) run the split path: one CTA
- * per (query, probed list) for phase 1 and for phase 2, candidates in a
- * per-query region of the workspace, then one selection CTA per query --
- * the same results as fg_batch_logic, bit for bit.  fg_search uses it.  The
+ * over all lists and half the longest) run the split path: the (query,
+ * probed list) pairs grouped by list, each pair taken by one resident CTA for
+ * phase 1 and for phase 2, candidates in a per-query region of the
+ * workspace, then one selection CTA per query -- the same results as
+ * fg_batch_logic, bit for bit.  fg_search uses it.  The
  * region holds max(4096, 2 * rerank_m) 8-byte keys per query (10,000 queries,
  * rerank_m 4096: 655 MB), so split very large batches; a query whose
  * candidates overflow its region is recomputed by the per-query kernel. */
