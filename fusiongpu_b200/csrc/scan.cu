@@ -66,6 +66,7 @@ struct ScanArgs {
     int4* pairs1;         // split: the (query, probe) pairs with a non-empty list of each phase,
     int4* pairs2;         //        as (q * top_m + j, list, start, length), grouped by list
     int* hist;            // split: per-list pair counts, then offsets: phase 1 [nlist + 1], phase 2 [nlist + 1]
+    int2* groups;         // group kernel: (first record, records) of up to GRP_G queries probing one list
 };
 
 struct ScanMisc {
@@ -1036,6 +1037,112 @@ __device__ __forceinline__ void adc_skew_stream(const uint8_t* __restrict__ rows
     if (nw > 0 && nw - 1 < nr) lkey[tt + (nw - 1) * NT] = f2key(dprev);
 }
 
+// adc_skew_stream for G queries probing the same list: each step reads the
+// codebook entry once and adds its term for every query (residuals res + g *
+// rstride), so the codebook traffic per term falls G-fold.  Every query's
+// terms are still added in subspace order from 0.0f: lkey[g * lstride + i] is
+// the key adc_skew_stream writes for query g.  The caller syncs the team.
+template <int M, int SD, int NT, int G>
+__device__ __forceinline__ void adc_skew_stream_multi(const uint8_t* __restrict__ rows, int n, int tt,
+                                                      const float* cbT, const float* res, int rstride,
+                                                      uint32_t* lkey, int lstride) {
+    constexpr int Z = AdcSkew<M, SD>::Z;
+    constexpr int W = M / 4;
+    constexpr int HW = (Z - 1 + 3) / 4;
+    const int j = (threadIdx.x & 31) % Z;
+    const int nr = n > tt ? (n - tt + NT - 1) / NT : 0;
+    const int tw = tt & ~31;
+    const int nw = n > tw ? (n - tw + NT - 1) / NT : 0;
+    uint32_t pm[HW];
+#pragma unroll
+    for (int u = 0; u < HW; ++u) {
+        const int e = j - 4 * u;
+        pm[u] = e >= 4 ? 0xffffffffu : (e <= 0 ? 0u : (1u << (8 * e)) - 1u);
+    }
+    uint32_t rl[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+        rl[g] = static_cast<uint32_t>(__cvta_generic_to_shared(res + (size_t)g * rstride)) - 4u * SD * j;
+    const uint32_t cl = static_cast<uint32_t>(__cvta_generic_to_shared(cbT)) - 4u * SD * j;
+    uint32_t prev[HW];
+#pragma unroll
+    for (int u = 0; u < HW; ++u) prev[u] = 0u;
+    float dprev[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) dprev[g] = 0.0f;
+    for (int r = 0; r < nw; ++r) {
+        uint32_t w[W];
+        if (r < nr) {
+            load_rotated<M, Z>(rows + (size_t)(tt + r * NT) * M, j, w);
+        } else {
+#pragma unroll
+            for (int u = 0; u < W; ++u) w[u] = 0u;
+        }
+        uint32_t h[HW];
+#pragma unroll
+        for (int u = 0; u < HW; ++u) h[u] = (prev[u] & pm[u]) | (w[u] & ~pm[u]);
+        float dcur[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) dcur[g] = 0.0f;
+#pragma unroll
+        for (int st = 0; st < M; ++st) {
+            if (st < Z - 1) {
+                const bool tail = st < j;  // previous row, subspace st - j + M
+                const int sp = tail ? st + M : st;
+                const uint32_t k = code_byte<HW>(h, st);
+                float cv[SD];
+                lds_sub<SD>(cl + 4u * SD * (k * M + sp), cv);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float rv[SD];
+                    lds_sub<SD>(rl[g] + 4u * SD * sp, rv);
+                    const float t = sd_arith<SD>(rv, cv);
+                    if (tail)
+                        dprev[g] = __fadd_rn(dprev[g], t);
+                    else
+                        dcur[g] = __fadd_rn(dcur[g], t);
+                }
+            } else {
+                const uint32_t k = code_byte<W>(w, st);
+                float cv[SD];
+                lds_sub<SD>(cl + 4u * SD * (k * M + st), cv);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float rv[SD];
+                    lds_sub<SD>(rl[g] + 4u * SD * st, rv);
+                    dcur[g] = __fadd_rn(dcur[g], sd_arith<SD>(rv, cv));
+                }
+            }
+        }
+        if (r > 0 && r - 1 < nr) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) lkey[g * lstride + tt + (r - 1) * NT] = f2key(dprev[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) dprev[g] = dcur[g];
+#pragma unroll
+        for (int u = 0; u < HW; ++u) prev[u] = w[u];
+    }
+#pragma unroll
+    for (int st = 0; st < Z - 1; ++st) {
+        if (st < j) {
+            const uint32_t k = code_byte<HW>(prev, st);
+            float cv[SD];
+            lds_sub<SD>(cl + 4u * SD * (k * M + st + M), cv);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float rv[SD];
+                lds_sub<SD>(rl[g] + 4u * SD * (st + M), rv);
+                dprev[g] = __fadd_rn(dprev[g], sd_arith<SD>(rv, cv));
+            }
+        }
+    }
+    if (nw > 0 && nw - 1 < nr) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) lkey[g * lstride + tt + (nw - 1) * NT] = f2key(dprev[g]);
+    }
+}
+
 // Residual of list c for this query; with LUT also the list's table from the
 // resident codebook.  Ends on the team barrier.
 template <int M, int SD, bool LUT, int NT>
@@ -1889,6 +1996,150 @@ __global__ void __launch_bounds__(NT, 1024 / NT) split_phase_kernel(const ScanAr
     }
 }
 
+// ---- group kernel: short lists, the queries probing one list together ------------
+//
+// Short lists without phase 2 (every probe within p1_lists) and many probes
+// per query (C2 at nprobe 8-12; group_chosen has the measured crossover).
+// The phase-1 pair records, grouped by list, are cut into groups of up to
+// GRP_G consecutive records of one list; a team of GRP_NT threads takes a
+// group, computes the group's residuals, runs the skewed on-the-fly ADC over
+// the list once for all of its queries (each codebook read serves every
+// query of the group) and then has one warp per query select and emit that
+// query's limit_k smallest by (distance, position) into the query's
+// candidate region -- split_select_kernel ranks them.  The codebook is
+// resident in shared memory for the launch, as in ivfpq_team_kernel.
+
+constexpr int GRP_G = 3;      // queries per group, one selecting warp each (4 spilled registers on C2)
+constexpr int GRP_MIN_TOP_M = 8;  // the group kernel runs by default from this many probes per query
+constexpr int GRP_NT = 128;   // threads per team
+constexpr int GRP_TEAMS = 7;  // teams per CTA at most (896 threads: 72 registers each)
+
+struct GroupLayout {
+    int res, lkey, hist, misc, total, dpad, lpad;
+};
+
+__host__ __device__ inline GroupLayout group_layout(int dim, int lmax) {
+    GroupLayout L;
+    L.dpad = (dim + 3) / 4 * 4;
+    L.lpad = ((lmax > 0 ? lmax : 1) + 3) / 4 * 4;
+    int o = 0;
+    L.res = take16(o, GRP_G * L.dpad * 4);
+    L.lkey = take16(o, GRP_G * L.lpad * 4);
+    L.hist = take16(o, (GRP_NT / 32) * 256 * 4);
+    L.misc = take16(o, 16);
+    L.total = o;
+    return L;
+}
+
+// Groups of the phase-1 records (grouped by list; after the scatter hist[c]
+// is the end of list c's records): a record starts a group when its index
+// within its list is a multiple of GRP_G.  work[4] counts the groups.
+__global__ void __launch_bounds__(256) group_cut_kernel(const ScanArgs a) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.work[0]) return;
+    const int c = a.pairs1[i].y;
+    const int s = c > 0 ? a.hist[c - 1] : 0, e = a.hist[c];
+    if ((i - s) % GRP_G) return;
+    const int gi = atomicAdd(a.work + 4, 1);
+    a.groups[gi] = make_int2(i, min(GRP_G, e - i));
+}
+
+template <int M, int SD, int G>
+__device__ __forceinline__ void group_adc(const ScanArgs& a, int start, int scan, int tt, const float* cb,
+                                          const float* res, int dpad, uint32_t* lkey, int lpad) {
+    adc_skew_stream_multi<M, SD, GRP_NT, G>(a.codes + (size_t)start * M, scan, tt, cb, res, dpad, lkey, lpad);
+}
+
+template <int M, int SD>
+__global__ void __launch_bounds__(GRP_TEAMS * GRP_NT, 1) ivfpq_group_kernel(const ScanArgs a, int team_bytes) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    static_assert(AdcSkew<M, SD>::value, "skewed on-the-fly ADC shape");
+    constexpr int CBF = M * 256 * SD;
+    float* cb = reinterpret_cast<float*>(smem);
+    // [subspace][code][SD] -> [code][subspace][SD], as ivfpq_team_kernel
+    for (int e = threadIdx.x; e < M * 256; e += blockDim.x) {
+        const int k = e / M, m = e - k * M;
+        float v[SD];
+        load_sub<SD, true>(a.codebook + ((size_t)m * 256 + k) * SD, v);
+#pragma unroll
+        for (int t = 0; t < SD; ++t) cb[(size_t)e * SD + t] = v[t];
+    }
+    __syncthreads();
+    const int team = threadIdx.x / GRP_NT, tt = threadIdx.x % GRP_NT;
+    const int bar = 1 + team;
+    unsigned char* ts = smem + (size_t)(CBF * 4 + 15) / 16 * 16 + (size_t)team * team_bytes;
+    const GroupLayout L = group_layout(a.dim, a.lmax);
+    float* res = reinterpret_cast<float*>(ts + L.res);
+    uint32_t* lkey = reinterpret_cast<uint32_t*>(ts + L.lkey);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(ts + L.hist);
+    int* next = reinterpret_cast<int*>(ts + L.misc);
+    const int ngroups = a.work[4];
+    const int w = tt >> 5, lane = tt & 31;
+    for (;;) {
+        if (tt == 0) *next = atomicAdd(a.work + 5, 1);
+        team_sync<GRP_NT>(bar);
+        const int gi = *next;
+        if (gi >= ngroups) break;
+        const int2 g2 = a.groups[gi];
+        const int first = g2.x, gcnt = g2.y;
+        const int4 r0 = a.pairs1[first];
+        const uint32_t c = (uint32_t)r0.y;
+        const int start = r0.z, len = r0.w;
+        const int wc = len < a.limit_k ? len : a.limit_k;
+        const int scan = (a.ref_compat && len > REF_P1_CLAMP) ? REF_P1_CLAMP : len;
+        const float* cv = a.centroids + (size_t)c * a.dim;
+        for (int e = tt; e < gcnt * a.dim; e += GRP_NT) {
+            const int g = e / a.dim, t = e - g * a.dim;
+            const int q = a.pairs1[first + g].x / a.top_m;
+            res[g * L.dpad + t] = a.queries[(size_t)q * a.dim + t] - cv[t];
+        }
+        team_sync<GRP_NT>(bar);
+        switch (gcnt) {
+            case 1: group_adc<M, SD, 1>(a, start, scan, tt, cb, res, L.dpad, lkey, L.lpad); break;
+            case 2: group_adc<M, SD, 2>(a, start, scan, tt, cb, res, L.dpad, lkey, L.lpad); break;
+            default: group_adc<M, SD, 3>(a, start, scan, tt, cb, res, L.dpad, lkey, L.lpad); break;
+        }
+        team_sync<GRP_NT>(bar);
+        if (w < gcnt) {
+            // warp w: query w of the group selects its wc smallest by (key,
+            // position) and appends them to its region (gpu_global.cu:321-390)
+            const int qj = a.pairs1[first + w].x;
+            const int q = qj / a.top_m, j = qj - q * a.top_m;
+            const uint32_t* keys = lkey + w * L.lpad;
+            uint32_t kth;
+            int n_less;
+            warp_select_keys(keys, scan, wc, hist + w * 256, kth, n_less);
+            int base = 0;
+            if (lane == 0) {
+                base = atomicAdd(a.cnt_g + q, wc);
+                a.cut_g[(size_t)q * a.p1 + j] = key2f(kth);
+            }
+            base = __shfl_sync(0xffffffffu, base, 0);
+            unsigned long long* dst = a.cand_g + (size_t)q * a.capg;
+            const unsigned long long jo = (unsigned long long)((uint32_t)j << 20);
+            const unsigned lt = lanemask_lt();
+            const int need_eq = wc - n_less;
+            int eq_base = 0, out = 0;
+            for (int i0 = 0; i0 < scan; i0 += 32) {
+                const int i = i0 + lane;
+                const bool in = i < scan;
+                const uint32_t key = in ? keys[i] : 0xffffffffu;
+                const bool is_eq = in && key == kth;
+                const unsigned eqb = __ballot_sync(0xffffffffu, is_eq);
+                const bool sel = in && (key < kth || (is_eq && eq_base + __popc(eqb & lt) < need_eq));
+                const unsigned sb = __ballot_sync(0xffffffffu, sel);
+                if (sel) {
+                    const int slot = base + out + __popc(sb & lt);
+                    if (slot < a.capg) dst[slot] = ((unsigned long long)key << 32) | jo | (uint32_t)i;
+                }
+                eq_base += __popc(eqb);
+                out += __popc(sb);
+            }
+        }
+        team_sync<GRP_NT>(bar);  // the next group reuses every buffer
+    }
+}
+
 // k-th smallest high word (1-based) of n 64-bit keys in global memory; the
 // block_radix_select scheme (four 8-bit MSD passes).
 __device__ void sel_radix_select_hi(const unsigned long long* keys, int n, int k, uint32_t* s_hist, uint32_t* s_b,
@@ -2118,10 +2369,11 @@ struct SplitWs {
     int32_t* cnt;
     int32_t* flags;
     int4* pairs;
+    int2* groups;
     unsigned long long* cand;
 };
 
-static size_t split_carve(void* ws, int nq, int nlist, const fg_search_params* p, SplitWs* out) {
+static size_t split_carve(void* ws, int nq, int nlist, const fg_search_params* p, int capg, SplitWs* out) {
     const int p1 = std::max(1, std::min(p->top_m, p->p1_lists));
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -2129,10 +2381,10 @@ static size_t split_carve(void* ws, int nq, int nlist, const fg_search_params* p
         o += (bytes + 255) / 256 * 256;
         return r;
     };
-    const size_t oc = take((size_t)nq * p1 * 4), ow = take(16), oh = take((size_t)2 * (nlist + 1) * 4),
+    const size_t oc = take((size_t)nq * p1 * 4), ow = take(32), oh = take((size_t)2 * (nlist + 1) * 4),
                  on = take((size_t)nq * 4),
                  of = take((size_t)nq * 4), op = take((size_t)nq * std::max(p->top_m, p1) * 16),
-                 oa = take((size_t)nq * split_capg(p) * 8);
+                 og = take((size_t)nq * p1 * 8), oa = take((size_t)nq * capg * 8);
     if (out) {
         char* b = static_cast<char*>(ws);
         out->cut = reinterpret_cast<float*>(b + oc);
@@ -2141,6 +2393,7 @@ static size_t split_carve(void* ws, int nq, int nlist, const fg_search_params* p
         out->cnt = reinterpret_cast<int32_t*>(b + on);
         out->flags = reinterpret_cast<int32_t*>(b + of);
         out->pairs = reinterpret_cast<int4*>(b + op);
+        out->groups = reinterpret_cast<int2*>(b + og);
         out->cand = reinterpret_cast<unsigned long long*>(b + oa);
     }
     return o;
@@ -2169,7 +2422,7 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     pp.rerank_m = a.rerank_m;
     pp.ref_compat = a.ref_compat;
     SplitWs w;
-    split_carve(ws, nq, ix->nlist, &pp, &w);
+    split_carve(ws, nq, ix->nlist, &pp, split_capg(&pp), &w);
     a.cut_g = w.cut;
     a.cnt_g = w.cnt;
     a.flags = w.flags;
@@ -2241,9 +2494,123 @@ static int batch_logic_split(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* 
     return check_launch("ivfpq_batch_kernel");
 }
 
+using GroupKernel = void (*)(const ScanArgs, int);
+
+static GroupKernel pick_group_kernel(int M, int SD) {
+#define FG_GROUP_CASE(m, sd) \
+    if (M == m && SD == sd) return ivfpq_group_kernel<m, sd>;
+    FG_GROUP_CASE(16, 4)
+    FG_GROUP_CASE(16, 8)
+    FG_GROUP_CASE(32, 2)
+    FG_GROUP_CASE(32, 4)
+    FG_GROUP_CASE(48, 2)
+    FG_GROUP_CASE(64, 2)
+#undef FG_GROUP_CASE
+    return nullptr;
+}
+
+// Whether the group kernel runs: short lists (typical length up to the team
+// kernel's limit), no phase 2 (top_m <= p1_lists), a skewed-ADC shape and at
+// least GRP_MIN_TOP_M probes per query, unless FG_SCAN_KERNEL names another
+// kernel (FG_SCAN_KERNEL=group forces it at any top_m).  Measured on C2 (4,104
+// lists of ~244, 10,000 queries): 2.82 -> 2.44 ms per step at nprobe 8, a tie
+// at 4, and slower at 1 and 2 (0.39 -> 0.53, 0.63 -> 0.76 ms), where a list
+// has only 2.4 or 4.9 probing queries and the separate selection kernel
+// (0.12 ms) outweighs the shared codebook reads.
+static bool group_chosen(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
+    if (!ix || !p || nq <= 0 || ix->pq_m <= 0 || ix->dim % ix->pq_m) return false;
+    const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
+    if (!pick_group_kernel(M, SD) || p->top_m > p->p1_lists || ix->max_list_len >= (1 << 19) ||
+        (long long)nq * p->top_m >= (1LL << 31))
+        return false;
+    const char* force = getenv("FG_SCAN_KERNEL");
+    const std::string mode = force ? force : "";
+    if (mode == "group") return true;
+    if (!mode.empty()) return false;
+    return p->top_m >= GRP_MIN_TOP_M && typical_list_len(ix) <= TEAM_OTF_MAX_LEN;
+}
+
+// Candidate region of a query on the group path: every probe is a phase-1
+// probe, so a query emits at most top_m * min(limit_k, longest list).
+static int group_capg(const fg_ivfpq_view* ix, const fg_search_params* p) {
+    const long long m = (long long)p->top_m * std::min(p->limit_k, std::max(ix->max_list_len, 1));
+    return (int)((std::max(m, 32LL) + 31) / 32 * 32);
+}
+
+constexpr int GROUP_NOT_LAUNCHED = -1;
+
+// Launches the group path: zero the counters, list the phase-1 pairs grouped
+// by list, cut them into groups, the group kernel, per-query selection, then
+// the per-query kernel for any query the selection flagged.  Returns
+// GROUP_NOT_LAUNCHED (nothing queued) when the codebook and one team do not
+// fit in shared memory.
+static int batch_logic_group(ScanArgs a, const fg_ivfpq_view* ix, int nq, void* ws, cudaStream_t stream,
+                             int smem_max) {
+    const int M = ix->pq_m, SD = ix->dim / ix->pq_m;
+    GroupKernel gk = pick_group_kernel(M, SD);
+    ScanKernel k = pick_scan_kernel(M, SD);
+    const int cb_bytes = (M * 256 * SD * 4 + 15) / 16 * 16;
+    const GroupLayout GL = group_layout(a.dim, a.lmax);
+    const int nteams = std::min(GRP_TEAMS, (smem_max - cb_bytes) / GL.total);
+    a.cap = a.rsel + SCAN_NT;
+    const ScanLayout L = scan_layout(M, a.dim, a.top_m, a.p1, a.lmax, a.cap, a.sort_n);
+    if (!gk || !k || nteams < 1 || L.total > smem_max) return GROUP_NOT_LAUNCHED;
+    fg_search_params pp{};
+    pp.top_m = a.top_m;
+    pp.p1_lists = a.p1;
+    pp.rerank_m = a.rerank_m;
+    pp.ref_compat = a.ref_compat;
+    pp.limit_k = a.limit_k;
+    const int capg = group_capg(ix, &pp);
+    SplitWs w;
+    split_carve(ws, nq, ix->nlist, &pp, capg, &w);
+    a.cut_g = w.cut;
+    a.cnt_g = w.cnt;
+    a.flags = w.flags;
+    a.cand_g = w.cand;
+    a.capg = capg;
+    a.work = w.work;
+    a.hist = w.hist;
+    a.pairs1 = w.pairs;
+    a.pairs2 = w.pairs + (size_t)nq * a.p1;
+    a.groups = w.groups;
+    FG_CUDA_TRY(cudaMemsetAsync(w.work, 0, reinterpret_cast<char*>(w.cnt + nq) - reinterpret_cast<char*>(w.work),
+                                stream));
+    const long long n = (long long)nq * a.top_m;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    split_pairs_count_kernel<<<blocks, 256, 0, stream>>>(a, nq);
+    int rc = check_launch("split_pairs_count_kernel");
+    if (rc) return rc;
+    split_pairs_scan_kernel<<<2, 1024, 0, stream>>>(a);
+    if ((rc = check_launch("split_pairs_scan_kernel"))) return rc;
+    split_pairs_scatter_kernel<<<blocks, 256, 0, stream>>>(a, nq);
+    if ((rc = check_launch("split_pairs_scatter_kernel"))) return rc;
+    group_cut_kernel<<<(unsigned)(((long long)nq * a.p1 + 255) / 256), 256, 0, stream>>>(a);
+    if ((rc = check_launch("group_cut_kernel"))) return rc;
+    const int bytes = cb_bytes + nteams * GL.total;
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(gk), bytes));
+    const int nsm = std::max(1, device_attr(cudaDevAttrMultiProcessorCount));
+    gk<<<nsm, nteams * GRP_NT, bytes, stream>>>(a, GL.total);
+    if ((rc = check_launch("ivfpq_group_kernel"))) return rc;
+    const int sort_cap = next_pow2(std::max(256, std::min(2 * a.rsel, capg)));
+    const int sbytes = sort_cap * 8 + (int)sizeof(SelMisc);
+    if (sbytes > smem_max) return fail(FG_ERR_UNSUPPORTED, "split select needs %d bytes of shared memory", sbytes);
+    FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(&split_select_kernel), sbytes));
+    split_select_kernel<<<nq, SEL_NT, sbytes, stream>>>(a, nq, sort_cap);
+    if ((rc = check_launch("split_select_kernel"))) return rc;
+    if (capg >= 2 * a.rsel) {  // only then can a query overflow the selection buffer
+        a.only = w.flags;
+        FG_CUDA_TRY(ensure_smem(reinterpret_cast<const void*>(k), L.total));
+        k<<<nq, SCAN_NT, L.total, stream>>>(a);
+        return check_launch("ivfpq_batch_kernel");
+    }
+    return FG_OK;
+}
+
 size_t batch_logic_workspace(const fg_ivfpq_view* ix, const fg_search_params* p, int nq) {
-    if (!split_chosen(ix, p, nq)) return 0;
-    return split_carve(nullptr, nq, ix->nlist, p, nullptr) + 256;
+    if (split_chosen(ix, p, nq)) return split_carve(nullptr, nq, ix->nlist, p, split_capg(p), nullptr) + 256;
+    if (group_chosen(ix, p, nq)) return split_carve(nullptr, nq, ix->nlist, p, group_capg(ix, p), nullptr) + 256;
+    return 0;
 }
 
 int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uint32_t* probe_ids,
@@ -2311,6 +2678,11 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     a.flags = nullptr;
     a.only = nullptr;
     a.capg = 0;
+    a.work = nullptr;
+    a.hist = nullptr;
+    a.pairs1 = nullptr;
+    a.pairs2 = nullptr;
+    a.groups = nullptr;
 
     int smem_max = 0, smem_sm = 0;
     smem_max = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin);
@@ -2318,10 +2690,21 @@ int batch_logic(const fg_ivfpq_view* ix, const float* queries, int nq, const uin
     if (smem_max <= 0 || smem_sm <= 0) return fail(FG_ERR_CUDA, "cannot read the device's shared-memory limits");
 
     if (split_chosen(ix, p, nq)) {
-        const size_t need = split_carve(nullptr, nq, ix->nlist, p, nullptr);
+        const size_t need = split_carve(nullptr, nq, ix->nlist, p, split_capg(p), nullptr);
         if (ws && ws_bytes >= need) return batch_logic_split(a, ix, nq, ws, stream, smem_max);
         if (getenv("FG_SCAN_KERNEL") && std::string(getenv("FG_SCAN_KERNEL")) == "split")
             return fail(FG_ERR_WORKSPACE, "FG_SCAN_KERNEL=split needs %zu workspace bytes", need);
+    }
+    if (group_chosen(ix, p, nq)) {
+        const size_t need = split_carve(nullptr, nq, ix->nlist, p, group_capg(ix, p), nullptr);
+        const bool forced = getenv("FG_SCAN_KERNEL") && std::string(getenv("FG_SCAN_KERNEL")) == "group";
+        if (ws && ws_bytes >= need) {
+            const int rc = batch_logic_group(a, ix, nq, ws, stream, smem_max);
+            if (rc != GROUP_NOT_LAUNCHED) return rc;
+            if (forced) return fail(FG_ERR_UNSUPPORTED, "FG_SCAN_KERNEL=group: the group kernel does not fit");
+        } else if (forced) {
+            return fail(FG_ERR_WORKSPACE, "FG_SCAN_KERNEL=group needs %zu workspace bytes", need);
+        }
     }
     // The team kernel when the codebook and at least one team fit in shared
     // memory (two teams for on-the-fly ADC).  FG_SCAN_KERNEL=block|team|team_lut|team_otf

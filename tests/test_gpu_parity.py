@@ -28,7 +28,7 @@ def fg():
 
 
 SCAN_KERNELS = ["auto", "block", "team_otf/64", "team_otf/128", "team_otf/256", "team_lut/64", "team_lut/128",
-                "team_lut/256", "team_otf/64/teamselect", "split"]
+                "team_lut/256", "team_otf/64/teamselect", "split", "group"]
 
 
 @pytest.fixture(params=SCAN_KERNELS)
@@ -36,8 +36,10 @@ def scan_kernel(request, monkeypatch):
     """Runs the test once per scan kernel: the per-query CTA kernel, the
     team kernel with table or on-the-fly ADC, teams of 64, 128 or 256 threads
     (FG_SCAN_KERNEL, FG_SCAN_TEAM_NT; 64 yields to 128 under ref_compat), the
-    team-wide list selection (FG_SCAN_WARP_SELECT=0), and the split path (one
-    CTA per probed list, candidates in the workspace)."""
+    team-wide list selection (FG_SCAN_WARP_SELECT=0), the split path (one
+    CTA per probed list, candidates in the workspace) and the group kernel
+    (the queries probing one list together; parameters with a phase 2 run
+    the team kernel under it)."""
     if request.param != "auto":
         kern, _, rest = request.param.partition("/")
         nt, _, sel = rest.partition("/")
@@ -86,6 +88,9 @@ PARAMS = {
                      final_k=20, mini_batch=64, epsilon=0.05, beta=3),
     "prune": dict(top_m=32, p1_lists=40, limit_k=10, threshold_coeff=1.0, prune_ratio=1.05, rerank_m=64,
                   final_k=8, mini_batch=16, epsilon=0.2, beta=1),
+    # the C2 operating point's shape: two probes, both in phase 1, deep rerank
+    "nprobe2": dict(top_m=2, p1_lists=12, limit_k=50, threshold_coeff=1.0, prune_ratio=100.0, rerank_m=1000,
+                    final_k=100, mini_batch=128, epsilon=0.1, beta=2),
 }
 
 
