@@ -149,10 +149,14 @@ int fg_batch_logic(const fg_ivfpq_view* index, const float* queries, int32_t nq,
  * probed list) pairs grouped by list, each pair taken by one resident CTA for
  * phase 1 and for phase 2, candidates in a per-query region of the
  * workspace, then one selection CTA per query -- the same results as
- * fg_batch_logic, bit for bit.  fg_search uses it.  The
- * region holds max(4096, 2 * rerank_m) 8-byte keys per query (10,000 queries,
- * rerank_m 4096: 655 MB), so split very large batches; a query whose
- * candidates overflow its region is recomputed by the per-query kernel. */
+ * fg_batch_logic, bit for bit.  Short lists with top_m between 8 and
+ * p1_lists (every probe in phase 1) run the group kernel instead: up to 3
+ * queries probing one list share its codebook reads, candidates in the same
+ * per-query regions (top_m * limit_k keys each).  fg_search uses it.  The
+ * split path's region holds max(4096, 2 * rerank_m) 8-byte keys per query
+ * (10,000 queries, rerank_m 4096: 655 MB), so split very large batches; a
+ * query whose candidates overflow its region is recomputed by the per-query
+ * kernel.  The size is 0 when neither path applies. */
 int fg_batch_logic_workspace_size(const fg_ivfpq_view* index, const fg_search_params* params, int32_t nq,
                                   size_t* bytes);
 int fg_batch_logic_ws(const fg_ivfpq_view* index, const float* queries, int32_t nq,
