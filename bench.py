@@ -218,8 +218,11 @@ def main():
     sweep = []
     def launches_per_step(nprobe):
         # two bf16 splits + coarse GEMM + finish (top_m <= 4), or splits + prefix GEMM
-        # + bound + filter GEMM + finish; then the scan and the rerank
-        return (4 if nprobe <= 4 else 6) + 2
+        # + bound + filter GEMM + finish; then the scan (the team kernel, or from 8 probes
+        # with every probe in phase 1 the group path: pair count, scan, scatter, group cut,
+        # group kernel, selection) and the rerank
+        scan = 6 if 8 <= nprobe <= CONFIG["p1_lists"] else 1
+        return (4 if nprobe <= 4 else 6) + scan + 1
     clocks = ClockSampler(local)
 
     def run_sweep(ref_compat):
