@@ -84,3 +84,35 @@ def test_library_defaults_match_reference():
     assert (p.top_m, p.p1_lists, p.limit_k, p.rerank_m, p.final_k, p.mini_batch, p.beta) == (
         20, 12, 50, 10000, 10, 128, 2)
     assert abs(p.epsilon - 0.1) < 1e-7 and p.prune_ratio == 100.0 and p.threshold_coeff == 1.0
+
+
+def test_scan_dispatch_by_list_length_and_probe_count(monkeypatch):
+    """fg_batch_logic_workspace_size states which candidate-generation path a
+    search takes (host logic only, no GPU): short lists with fewer than 8
+    probes run the team kernel (no workspace); short lists with 8 or more
+    probes, all in phase 1, the group kernel (top_m * limit_k candidate keys
+    per query); long lists, or a shard whose longest list is long, the split
+    path (max(4096, 2 * rerank_m) keys per query)."""
+    from fusiongpu_b200 import _lib
+    monkeypatch.delenv("FG_SCAN_KERNEL", raising=False)
+
+    def ws(total, max_len, top_m, p1_lists, nq=1000, rerank_m=1000, limit_k=50):
+        v = _lib.IvfpqView(0, 0, 0, 0, 0, 4104, 128, 64, total, max_len)
+        p = _lib.SearchParams()
+        _lib.lib().fg_search_params_default(ctypes.byref(p))
+        p.top_m, p.p1_lists, p.rerank_m, p.limit_k = top_m, p1_lists, rerank_m, limit_k
+        return _lib.size_query("fg_batch_logic_workspace_size", ctypes.byref(v), ctypes.byref(p), nq)
+
+    c2 = dict(total=1_000_000, max_len=488)  # C2: 4,104 lists of ~244
+    assert ws(**c2, top_m=2, p1_lists=12) == 0
+    assert ws(**c2, top_m=4, p1_lists=12) == 0
+    assert ws(**c2, top_m=16, p1_lists=12) == 0  # phase 2: the team kernel
+    g8 = ws(**c2, top_m=8, p1_lists=12)
+    assert 1000 * 8 * 50 * 8 <= g8 < 1000 * 4096 * 8  # the group path's keys, not the split path's
+    assert ws(**c2, top_m=12, p1_lists=12) > g8
+    s = ws(total=4_000_000, max_len=1400, top_m=64, p1_lists=12)  # lists of ~975
+    assert s >= 1000 * 4096 * 8
+    shard = ws(total=250_000, max_len=1400, top_m=64, p1_lists=12)  # a quarter of the lists owned
+    assert shard >= 1000 * 4096 * 8
+    monkeypatch.setenv("FG_SCAN_KERNEL", "team")
+    assert ws(**c2, top_m=8, p1_lists=12) == 0
